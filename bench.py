@@ -1,0 +1,373 @@
+"""Attention forward throughput on B200 — the headline metric of BASELINE.json.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
+
+One step = one forward pass of the configured workload through the public API
+(mlx_primitives.*) on each rank's GPU.  Default workload (config "c2", the one BASELINE's
+metric is quoted on): flash_attention bf16, BHSD, causal, batch 4 x 32 heads x 4096 tokens x
+head_dim 128 per GPU.  Multi-GPU runs (torchrun, one process per GPU) give every rank its own
+(batch, head) units — no collective on the data path — so per-GPU work is fixed ("weak").
+
+Printed by rank 0, one JSON line: value = whole-job TFLOPS (algorithmic FLOPs: 4*D per
+admissible (query, key) pair, masked pairs not counted) over the max-over-ranks device time;
+e2e = the same through the public API with pinned host tensors, H2D/D2H inside the timed
+region; roofline = the attention kernel against MEASURED_PEAKS.json; cpu_baseline = the CPU
+oracle (test infrastructure, the reference's algorithm restated) on a bounded sample.
+`--impl reference` times that CPU path alone on rank 0 (the reference's own MLX code cannot
+run on Linux without Apple hardware).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+for _p in (REPO, REPO / "mlx-primitives_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+METRIC = "attention fwd TFLOPS/GPU and % of BF16 tensor peak at 1/2/4/8 B200"
+
+CONFIGS = {
+    "c1": dict(workload="flash_attention fp32 BSHD causal (config 1)", api="flash", dtype="fp32",
+               layout="BSHD", B=2, H=12, S=1024, Skv=1024, D=64, causal=True, window=-1, std=1.0),
+    "c2": dict(workload="flash_attention bf16 BHSD causal (config 2)", api="flash", dtype="bf16",
+               layout="BHSD", B=4, H=32, S=4096, Skv=4096, D=128, causal=True, window=-1, std=1.0),
+    "c3": dict(workload="SlidingWindowAttention bf16 BSHD causal W4096 (config 3)", api="swa",
+               dtype="bf16", layout="BSHD", B=2, H=32, S=16384, Skv=16384, D=128, causal=True,
+               window=4096, std=1.0),
+    "c4": dict(workload="ChunkedCrossAttention bf16 BSHD chunk4096 (config 4)", api="chunked",
+               dtype="bf16", layout="BSHD", B=8, H=16, S=512, Skv=65536, D=64, causal=False,
+               window=-1, std=0.5),
+}
+
+L2_BYTES = 126 * 1024 * 1024
+
+
+def admissible_pairs(Sq, Skv, causal, wl=-1, wr=-1, qoff=0, kvoff=0) -> int:
+    """Number of (query, key) pairs the mask admits for one (batch, head)."""
+    qpos = np.arange(Sq, dtype=np.int64) + qoff
+    lo = np.zeros(Sq, np.int64)
+    hi = np.full(Sq, Skv, np.int64)
+    if wl >= 0:
+        lo = np.maximum(lo, qpos - wl - kvoff)
+    if causal:
+        hi = np.minimum(hi, qpos - kvoff + 1)
+    if wr >= 0:
+        hi = np.minimum(hi, qpos + wr - kvoff + 1)
+    return int(np.clip(hi - lo, 0, None).sum())
+
+
+def config_flops(c) -> float:
+    """Algorithmic FLOPs of one forward of config c on one GPU."""
+    wr = -1 if c["causal"] else c["window"]
+    pairs = admissible_pairs(c["S"], c["Skv"], c["causal"], c["window"], wr,
+                             (c["Skv"] - c["S"]) if (c["api"] == "flash" and c["causal"]) else 0)
+    return 4.0 * c["D"] * pairs * c["B"] * c["H"]
+
+
+def config_bytes(c) -> float:
+    es = 4 if c["dtype"] == "fp32" else 2
+    return es * c["B"] * c["H"] * c["D"] * (2 * c["S"] + 2 * c["Skv"])
+
+
+def load_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["bf16_tflops"], d.get("bf16_tflops_sustained"), d["hbm_gbs"], "MEASURED_PEAKS.json (measured)"
+    return 1590.0, 1400.0, 6650.0, "profiling-recipe fallback"
+
+
+# ------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples SM clock and throttle reasons with NVML while the timed region runs."""
+
+    REASONS = {
+        "sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, index: int, period_s: float = 0.002):
+        self.index, self.period = index, period_s
+        self.samples, self.reasons = [], set()
+        self._stop = threading.Event()
+        self._t = None
+        self.max_mhz = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # noqa: BLE001 - clocks are reported as unavailable
+            self.nv = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            self.sample()
+            time.sleep(self.period)
+
+    def sample(self):
+        if self.nv is None:
+            return
+        try:
+            self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+            r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            for name, bit in self.REASONS.items():
+                if r & bit:
+                    self.reasons.add(name)
+        except Exception:  # noqa: BLE001
+            pass
+
+    def __enter__(self):
+        if self.nv is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._t is not None:
+            self._t.join()
+        self.sample()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        return {"sm_mhz": float(statistics.median(self.samples)), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------------------ CPU side
+def cpu_oracle_tflops(c, budget_s: float, max_units: int | None = None):
+    """Time the CPU oracle (dense fp32 restatement of the reference's CPU path, numpy + BLAS)
+    on whole (batch, head) units of config c until budget_s is used.  Returns (TFLOPS, units,
+    seconds, threads)."""
+    from oracle import attention_oracle as O
+
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max((i.get("num_threads", 1) for i in threadpool_info()), default=os.cpu_count())
+    except Exception:  # noqa: BLE001
+        threads = os.cpu_count()
+    D, S, Skv = c["D"], c["S"], c["Skv"]
+    wr = -1 if c["causal"] else c["window"]
+    qoff = (Skv - S) if (c["api"] == "flash" and c["causal"]) else 0
+    pairs = admissible_pairs(S, Skv, c["causal"], c["window"], wr, qoff)
+    rng = np.random.RandomState(1234)
+    q = (rng.standard_normal((1, 1, S, D)) * c["std"]).astype(np.float32)
+    k = (rng.standard_normal((1, 1, Skv, D)) * c["std"]).astype(np.float32)
+    v = (rng.standard_normal((1, 1, Skv, D)) * c["std"]).astype(np.float32)
+    if c["dtype"] != "fp32":
+        q, k, v = (O.round_bf16(a) for a in (q, k, v))
+    units, t_total = 0, 0.0
+    cap = max_units or c["B"] * c["H"]
+    while units < cap and (units == 0 or t_total < budget_s):
+        t0 = time.perf_counter()
+        O.attention_bhsd(q, k, v, 1.0 / math.sqrt(D), causal=c["causal"], window_left=c["window"],
+                         window_right=wr, q_offset=qoff, dtype=np.float32)
+        t_total += time.perf_counter() - t0
+        units += 1
+    return 4.0 * D * pairs * units / t_total / 1e12, units, t_total, threads
+
+
+def run_reference_arm(args, c, rank):
+    """--impl reference: the CPU path (oracle port) on rank 0's host cores."""
+    if rank != 0:
+        return
+    per_step = []
+    total_units = 0
+    threads = None
+    for i in range(args.warmup + args.steps):
+        tf, units, secs, threads = cpu_oracle_tflops(c, budget_s=0.0, max_units=1)
+        if i >= args.warmup:
+            per_step.append(secs)
+            total_units += units
+    D = c["D"]
+    wr = -1 if c["causal"] else c["window"]
+    qoff = (c["Skv"] - c["S"]) if (c["api"] == "flash" and c["causal"]) else 0
+    unit_flops = 4.0 * D * admissible_pairs(c["S"], c["Skv"], c["causal"], c["window"], wr, qoff)
+    secs = sum(per_step)
+    value = unit_flops * total_units / secs / 1e12
+    sample = f"{total_units} (batch, head) units of {c['workload']}, one per step, fp32 numpy"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOPS",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * secs / max(len(per_step), 1), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_json(c, args.gpus),
+        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "MLX (the reference's runtime) cannot run on this Linux/NVIDIA box; this arm times "
+                "the oracle's restatement of the reference's CPU algorithm (dense fp32 SDPA path)",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_json(c, n):
+    return {"workload": c["workload"], "global_batch": c["B"] * n, "batch_per_gpu": c["B"],
+            "heads": c["H"], "seq_len": c["S"], "kv_len": c["Skv"], "head_dim": c["D"],
+            "layout": c["layout"], "causal": c["causal"], "window": c["window"],
+            "parallelism": f"dp{n} over (batch, head) units, no collective",
+            "l2": ("inputs larger than L2" if config_bytes(c) > L2_BYTES
+                   else "L2 flushed between timed iterations")}
+
+
+# ------------------------------------------------------------------------------ GPU side
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+
+    c = CONFIGS[args.config]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference_arm(args, c, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import mlx_primitives as mp
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    dtype = torch.float32 if c["dtype"] == "fp32" else torch.bfloat16
+    B, H, S, Skv, D = c["B"], c["H"], c["S"], c["Skv"], c["D"]
+    shape_q = (B, H, S, D) if c["layout"] == "BHSD" else (B, S, H, D)
+    shape_kv = (B, H, Skv, D) if c["layout"] == "BHSD" else (B, Skv, H, D)
+    g = torch.Generator(device=dev)
+    g.manual_seed(42 + rank)
+    q = (torch.randn(shape_q, generator=g, device=dev) * c["std"]).to(dtype)
+    k = (torch.randn(shape_kv, generator=g, device=dev) * c["std"]).to(dtype)
+    v = (torch.randn(shape_kv, generator=g, device=dev) * c["std"]).to(dtype)
+
+    def step(qq, kk, vv):
+        if c["api"] == "flash":
+            return mp.flash_attention(qq, kk, vv, causal=c["causal"], layout=c["layout"])
+        if c["api"] == "swa":
+            return mp.sliding_window_attention(qq, kk, vv, window_size=c["window"], causal=c["causal"])
+        return mp.chunked_cross_attention(qq, kk, vv, chunk_size=4096, causal=c["causal"])
+
+    launches_per_step = 2 if c["api"] == "chunked" else 1
+    flush = config_bytes(c) <= L2_BYTES
+    scratch = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev) if flush else None
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step(q, k, v)
+    stream = torch.cuda.current_stream(dev)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clocks:
+        for i in range(args.steps):
+            if flush:
+                scratch.fill_(i & 0xFF)
+            starts[i].record(stream)
+            step(q, k, v)
+            ends[i].record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    ms_local = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
+    ms = max_over_ranks(ms_local)
+
+    flops = config_flops(c)  # per GPU per step
+    value = world * flops / (ms * 1e-3) / 1e12
+    peak, peak_sus, hbm, peak_src = load_peaks()
+    achieved = flops / (ms_local * 1e-3) / 1e12  # this rank's work per step / its step time
+
+    # ---- e2e: public API with pinned host tensors (H2D and D2H inside the timed region)
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    step(hq, hk, hv)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        out_host = step(hq, hk, hv)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.e2e_steps)
+    e2e_value = world * flops / (e2e_ms * 1e-3) / 1e12
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
+    d2h = out_host.numel() * out_host.element_size()
+
+    line = None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32" if c["dtype"] == "fp32" else "bf16",
+            "data": "synthetic: seeded N(0, std^2) tensors generated on device (seed 42 + rank)",
+            "config": config_json(c, world),
+            "tflops_per_gpu": value / world,
+            "pct_of_bf16_peak": 100.0 * (value / world) / peak,
+            "roofline": {
+                "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "traffic": None,
+                "kernel": "attn_fwd_fp32_kernel" if c["dtype"] == "fp32" else "attn_fwd_sm100_kernel",
+                "peak_source": f"{peak_src}: bf16_tflops (burst); sustained {peak_sus}",
+                "algorithmic_flops_per_launch": flops,
+                "hbm_gbs_at_min_bytes": config_bytes(c) / (ms_local * 1e-3) / 1e9,
+            },
+            "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+            "gpu_launches": args.steps * launches_per_step,
+            "clocks": clocks.summary(),
+        }
+        if world == 1:
+            tf, units, secs, threads = cpu_oracle_tflops(c, budget_s=args.cpu_budget)
+            line["cpu_baseline"] = {
+                "value": tf, "unit": "TFLOPS", "cores": threads, "kind": "port",
+                "sample": f"{units} of {c['B'] * c['H']} (batch, head) units, dense fp32 numpy, "
+                          f"{secs:.1f} s"}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,161 @@
+/*
+ * mlxp_attn.h — C ABI of libmlxp_attn.so, the B200 (sm_100a) attention forward library.
+ *
+ * This is the drop-in boundary that replaces the reference's kernel dispatch for the
+ * mlx_primitives.attention forward path.  Every pointer is a device pointer unless stated
+ * otherwise, every stride is in ELEMENTS and given in (batch, head, seq, dim) order, so the
+ * BSHD and BHSD layouts are both just stride vectors (no transpose kernel anywhere).  The
+ * dim stride must be 1.  Calls are asynchronous on the given CUDA stream (NULL = legacy
+ * default stream) and never allocate device memory: scratch space is passed in by the caller
+ * (see mlxp_attn_workspace_size).  Every function returns an mlxp_status; the message of the
+ * last failure on the calling thread is available from mlxp_last_error().
+ *
+ * Reference interfaces replaced (paths inside zakkeown/mlx-primitives):
+ *   mlx_primitives/attention/flash.py:178-183, 220-235   mx.fast.scaled_dot_product_attention calls
+ *   mlx_primitives/attention/flash.py:319-476            flash_attention Metal kernel + launch
+ *   mlx_primitives/attention/sliding_window.py:46-133,316-360   sliding-window Metal kernel + launch
+ *   mlx_primitives/attention/chunked.py:258-407          chunked cross-attention Metal kernel + launch
+ *   mlx_primitives/attention/_online_softmax.py:42-106   online_softmax_merge (LSE merge)
+ *   mlx_primitives/kernels/_registry.py:122-156          get_kernel (kernel cache)
+ */
+#ifndef MLXP_ATTN_H
+#define MLXP_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  The reference raises ValueError for bad shapes/dtypes/layouts
+ * (flash.py:123-169) and RuntimeError for kernel failures (flash.py:236-251); the Python shim
+ * maps MLXP_ERR_INVALID to ValueError and everything else to RuntimeError. */
+typedef enum mlxp_status {
+  MLXP_OK = 0,
+  MLXP_ERR_INVALID = 1,     /* bad argument: shape, stride, alignment, null pointer */
+  MLXP_ERR_UNSUPPORTED = 2, /* valid but not built: head_dim / dtype combination      */
+  MLXP_ERR_CUDA = 3,        /* a CUDA runtime or driver call failed                    */
+  MLXP_ERR_NCCL = 4,        /* an NCCL call failed or NCCL could not be loaded         */
+  MLXP_ERR_TIMEOUT = 5,     /* a bounded device-side wait ran out (see mlxp_device_status) */
+  MLXP_ERR_WORKSPACE = 6    /* workspace missing or smaller than mlxp_attn_workspace_size */
+} mlxp_status;
+
+/* Element types. */
+typedef enum mlxp_dtype {
+  MLXP_DTYPE_FP32 = 0,
+  MLXP_DTYPE_BF16 = 1,
+  MLXP_DTYPE_FP16 = 2
+} mlxp_dtype;
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+int mlxp_version(void);
+
+/* Message of the last failure on the calling thread ("" if none).  Thread-local. */
+const char* mlxp_last_error(void);
+
+/*
+ * Attention forward:  O = softmax(scale * Q K^T + mask) V, per (batch, head).
+ *
+ * Replaces the SDPA call / Metal kernel launch of flash_attention (flash.py:178-183, 220-235,
+ * 463-474), sliding_window_attention (sliding_window.py:217, 351-358) and
+ * chunked_cross_attention (chunked.py:394-405).
+ *
+ * Shapes: q [B,H,Sq,D], k/v [B,H,Skv,D], o [B,H,Sq,D] (logical, in the given strides).
+ * Masking uses absolute positions qpos = i + q_pos_offset, kpos = j + kv_pos_offset:
+ *   causal != 0          requires kpos <= qpos
+ *   window_left  >= 0    requires qpos - kpos <= window_left   (-1 = unbounded)
+ *   window_right >= 0    requires kpos - qpos <= window_right  (-1 = unbounded)
+ * The reference's conventions map onto these as:
+ *   flash_attention causal (bottom-right aligned, utils/masking.py:14-66):  q_pos_offset = Skv - Sq
+ *   sliding window |i-j| <= W (+ causal)  (sliding_window.py:136-161):     window_left = W [, window_right = W]
+ *   chunked causal, top-left absolute positions (_online_softmax.py:149-161): offsets 0
+ * A query row with no admissible key yields O = 0 and LSE = -inf.
+ *
+ * lse (nullable): fp32 [B,H,Sq] contiguous, natural-log sum-exp of the scaled, masked scores.
+ * dtype: element type of q, k, v and o.  BF16/FP16 run the tcgen05 tensor-core kernel
+ * (head_dim 64 or 128); FP32 runs the CUDA-core kernel (head_dim 32, 64 or 128).
+ * kv_splits: 1 = no split, 0 = automatic, >1 = split the key range into that many parts that
+ * run as separate CTAs and are combined by an LSE merge (needs workspace).
+ */
+int mlxp_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
+                  int dtype, int64_t B, int64_t H, int64_t Sq, int64_t Skv, int64_t D,
+                  const int64_t q_strides[4], const int64_t k_strides[4],
+                  const int64_t v_strides[4], const int64_t o_strides[4],
+                  float scale, int causal, int64_t window_left, int64_t window_right,
+                  int64_t q_pos_offset, int64_t kv_pos_offset,
+                  int64_t kv_splits, void* workspace, size_t ws_bytes, void* cuda_stream);
+
+/*
+ * Bytes of workspace mlxp_attn_fwd needs for these arguments (0 when no split is used).
+ * kv_splits as for mlxp_attn_fwd (0 = the automatic choice mlxp_attn_fwd would make).
+ * Replaces the reference's implicit MLX allocation of intermediate arrays (chunked.py:142-166).
+ */
+size_t mlxp_attn_workspace_size(int dtype, int64_t B, int64_t H, int64_t Sq, int64_t Skv,
+                                int64_t D, int causal, int64_t window_left,
+                                int64_t window_right, int64_t q_pos_offset,
+                                int64_t kv_pos_offset, int64_t kv_splits);
+
+/*
+ * Partial attention forward: as mlxp_attn_fwd, but writes the NORMALISED output in fp32
+ * (o_part, [B,H,Sq,D] with o_strides) and the natural-log LSE (lse_part, [B,H,Sq]
+ * contiguous, required).  This is the (O, m, l) triple of compute_chunk_attention
+ * (_online_softmax.py:109-176) in LSE form, used by the ring pass and by callers that merge
+ * several key ranges themselves.  bf16/fp16 inputs only; no split.
+ */
+int mlxp_attn_fwd_partial(const void* q, const void* k, const void* v, float* o_part,
+                          float* lse_part, int dtype, int64_t B, int64_t H, int64_t Sq,
+                          int64_t Skv, int64_t D, const int64_t q_strides[4],
+                          const int64_t k_strides[4], const int64_t v_strides[4],
+                          const int64_t o_strides[4], float scale, int causal,
+                          int64_t window_left, int64_t window_right, int64_t q_pos_offset,
+                          int64_t kv_pos_offset, void* cuda_stream);
+
+/*
+ * LSE merge of n_parts partial results (online_softmax_merge, _online_softmax.py:42-106, in
+ * LSE form):  w_i = exp(lse_i - max_j lse_j);  O = sum_i w_i O_i / sum_i w_i;
+ * lse = max_j lse_j + log(sum_i w_i).
+ * o_parts: fp32 [n_parts,B,H,S,D] contiguous; lse_parts: fp32 [n_parts,B,H,S] contiguous.
+ * o: output in dtype with o_strides; lse_out (nullable): fp32 [B,H,S] contiguous.
+ */
+int mlxp_lse_merge(const float* o_parts, const float* lse_parts, int64_t n_parts, void* o,
+                   float* lse_out, int dtype, int64_t B, int64_t H, int64_t S, int64_t D,
+                   const int64_t o_strides[4], void* cuda_stream);
+
+/*
+ * In-place running merge for the ring pass: (o_acc, lse_acc) <- merge((o_acc, lse_acc),
+ * (o_new, lse_new)).  All fp32; o_acc/o_new [B,H,S,D] contiguous, lse [B,H,S] contiguous.
+ * An accumulator row with lse_acc = -inf is simply replaced.
+ */
+int mlxp_lse_merge_accumulate(float* o_acc, float* lse_acc, const float* o_new,
+                              const float* lse_new, int64_t B, int64_t H, int64_t S,
+                              int64_t D, void* cuda_stream);
+
+/*
+ * Final conversion of a ring accumulator: o = o_acc cast to dtype (o_strides).
+ */
+int mlxp_cast_output(const float* o_acc, void* o, int dtype, int64_t B, int64_t H, int64_t S,
+                     int64_t D, const int64_t o_strides[4], void* cuda_stream);
+
+/*
+ * Device-side status word of the current device: 0 when every bounded wait completed,
+ * otherwise MLXP_ERR_TIMEOUT | (site << 8).  Synchronises the device.  reset != 0 clears it.
+ */
+int mlxp_device_status(int* status_out, int reset);
+
+/* Limit for every bounded device-side wait, in nanoseconds (default 2 s). */
+int mlxp_set_wait_timeout_ns(uint64_t ns);
+
+/*
+ * Self-test of the bounded-wait machinery: launches one CTA whose threads wait on an
+ * mbarrier that nothing ever arrives on, with the given limit.  Returns MLXP_ERR_TIMEOUT
+ * (and leaves the device status set) when the wait correctly gave up; MLXP_OK would mean the
+ * wait completed, which cannot happen.  Synchronises the stream.
+ */
+int mlxp_selftest_wait_timeout(uint64_t timeout_ns, void* cuda_stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MLXP_ATTN_H */

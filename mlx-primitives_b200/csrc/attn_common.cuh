@@ -1,0 +1,139 @@
+// attn_common.cuh — parameters and mask arithmetic shared by the attention kernels.
+//
+// Masking semantics (positions are absolute: qpos = i + q_off, kpos = j + kv_off):
+//   causal        kpos <= qpos                       (flash.py:286 kv_limit = q_end;
+//                                                     _online_softmax.py:149-161)
+//   window_left   qpos - kpos <= wl  (wl >= 0)       (sliding_window.py:154-160, |i-j| <= W)
+//   window_right  kpos - qpos <= wr  (wr >= 0)
+//   key index j < Skv (rows past the end of K/V are zero-filled by TMA and must be masked).
+// For one query row the admissible keys of a tile form one contiguous interval, so masking a
+// boundary tile costs two compares per score and no tile is ever masked element-wise unless it
+// straddles a boundary.
+#pragma once
+
+#include <cstdint>
+
+namespace mlxp {
+
+struct MaskSpec {
+  int causal;
+  long long wl, wr;     // -1 = unbounded
+  long long q_off, kv_off;
+  long long Skv;
+};
+
+// Admissible key-index range [lo, hi) for the query rows [r0, r1) (local indices, r1 > r0).
+__host__ __device__ inline void kv_index_range(const MaskSpec& m, long long r0, long long r1,
+                                               long long& lo, long long& hi) {
+  const long long qmin = r0 + m.q_off, qmax = r1 - 1 + m.q_off;
+  lo = 0;
+  hi = m.Skv;
+  if (m.wl >= 0) {
+    const long long l = qmin - m.wl - m.kv_off;
+    if (l > lo) lo = l;
+  }
+  bool bounded = false;
+  long long up = 0;
+  if (m.causal) {
+    up = qmax;
+    bounded = true;
+  }
+  if (m.wr >= 0) {
+    const long long u = qmax + m.wr;
+    up = bounded ? (u < up ? u : up) : u;
+    bounded = true;
+  }
+  if (bounded) {
+    const long long h = up - m.kv_off + 1;
+    if (h < hi) hi = h;
+  }
+  if (hi < lo) hi = lo;
+}
+
+// Key-tile range [tlo, thi) of width BN for the query rows [r0, r1); empty when r1 <= r0.
+__host__ __device__ inline void kv_tile_range(const MaskSpec& m, long long r0, long long r1,
+                                              int BN, int& tlo, int& thi) {
+  if (r1 <= r0) {
+    tlo = thi = 0;
+    return;
+  }
+  long long lo, hi;
+  kv_index_range(m, r0, r1, lo, hi);
+  if (hi <= lo) {
+    tlo = thi = 0;
+    return;
+  }
+  tlo = (int)(lo / BN);
+  thi = (int)((hi + BN - 1) / BN);
+}
+
+// True when every (query row in [r0, r1), key in [c0, c1)) is admissible and c1 <= Skv.
+__host__ __device__ inline bool tile_is_full(const MaskSpec& m, long long r0, long long r1,
+                                             long long c0, long long c1) {
+  if (c1 > m.Skv) return false;
+  const long long qmin = r0 + m.q_off, qmax = r1 - 1 + m.q_off;
+  const long long kmin = c0 + m.kv_off, kmax = c1 - 1 + m.kv_off;
+  if (m.causal && kmax > qmin) return false;
+  if (m.wl >= 0 && qmax - kmin > m.wl) return false;
+  if (m.wr >= 0 && kmax - qmin > m.wr) return false;
+  return true;
+}
+
+// Admissible columns [c_lo, c_hi] (inclusive, tile-local, clamped to [-1, BN]) of the tile
+// starting at key index c0 for the query at local row `row`.
+__host__ __device__ inline void row_col_interval(const MaskSpec& m, long long row, long long c0,
+                                                 int BN, int& c_lo, int& c_hi) {
+  const long long base = row + m.q_off - (c0 + m.kv_off);  // qpos - kpos of column 0
+  long long lo = 0, hi = BN - 1;
+  if (m.Skv - 1 - c0 < hi) hi = m.Skv - 1 - c0;
+  if (m.causal && base < hi) hi = base;
+  if (m.wr >= 0 && base + m.wr < hi) hi = base + m.wr;
+  if (m.wl >= 0 && base - m.wl > lo) lo = base - m.wl;
+  if (lo > BN) lo = BN;
+  if (hi < -1) hi = -1;
+  c_lo = (int)lo;
+  c_hi = (int)hi;
+}
+
+// Parameters of the tensor-core (bf16/fp16) kernel.  Q/K/V are described by TMA tensor maps;
+// the slot fields give, for each of q, k and v, the tensor-map dimension (1..3) that holds
+// seq, head and batch, and whether head/batch are broadcast (stride 0 -> coordinate 0).
+struct TmaCoordMap {
+  int8_t slot_s, slot_h, slot_b;  // tensor-map dims 1..3
+  int8_t bcast_h, bcast_b;        // 1 = that dim was size-1/broadcast: always coordinate 0
+};
+
+struct FwdParams {
+  int B, H, Sq, Skv;
+  int n_qblk;           // query blocks of 256 rows
+  int splits;           // >= 1 key-range splits
+  int tiles_per_split;  // key tiles per split (splits > 1)
+  int heavy_first;      // order query blocks by descending work (causal)
+  // output: normal (dtype, normalised) or fp32 (normalised, for merges)
+  int out_f32;
+  void* o;
+  long long o_sb, o_sh, o_ss, o_split;  // element strides; o_split = stride between splits
+  float* lse;                           // [split][B][H][Sq] contiguous, nullable unless out_f32
+  long long lse_split;
+  float scale_log2;     // softmax scale * log2(e)
+  MaskSpec mask;
+  TmaCoordMap cq, ck, cv;
+  int* status;
+  unsigned long long timeout_ns;
+};
+
+// Parameters of the CUDA-core fp32 kernel (plain pointers and strides).
+struct FwdParamsF32 {
+  int B, H, Sq, Skv;
+  const float* q;
+  const float* k;
+  const float* v;
+  long long q_sb, q_sh, q_ss, k_sb, k_sh, k_ss, v_sb, v_sh, v_ss;
+  float* o;
+  long long o_sb, o_sh, o_ss;
+  float* lse;  // [B][H][Sq] contiguous, nullable
+  float scale_log2;
+  MaskSpec mask;
+};
+
+}  // namespace mlxp

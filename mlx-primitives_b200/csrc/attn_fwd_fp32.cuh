@@ -1,0 +1,298 @@
+// attn_fwd_fp32.cuh — fp32 attention forward on CUDA cores (FFMA), the tight-parity variant.
+//
+// The reference's fp32 paths (flash.py:257-316 tiled online softmax, flash.py:329-408 Metal
+// per-query kernel) accumulate in fp32 and rescale exactly on every new maximum; this kernel
+// does the same (no lazy rescale), with scores scaled into the log2 domain once.
+//
+// CTA = 64 query rows x one (batch, head); 256 threads as a 16 x 16 grid: thread (ty, tx) owns
+// query rows 4*ty .. 4*ty+3 (scores, running max/sum and output accumulators) and the key
+// columns tx + 16*c of each key tile / output columns tx + 16*c of the head dimension.  Row
+// reductions are 16-lane shuffles (the 16 threads of a row group share a warp).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "attn_common.cuh"
+#include "sm100_ptx.cuh"
+
+namespace mlxp {
+
+template <int D>
+struct F32Cfg {
+  static constexpr int BM = 64;
+  static constexpr int BN = (D >= 128) ? 32 : 64;
+  static constexpr int NC = BN / 16;  // key columns per thread
+  static constexpr int ND = D / 16;   // output columns per thread
+  static constexpr int SQ = D;        // row pitch (floats) of Q in smem
+  static constexpr int SK = D + 1;    // padded pitch of K (column reads by tx)
+  static constexpr int SV = D;
+  static constexpr int SP = BN + 1;
+  static constexpr int SMEM_FLOATS = BM * SQ + BN * SK + BN * SV + BM * SP;
+  static constexpr int SMEM_BYTES = SMEM_FLOATS * 4;
+  static_assert(D % 16 == 0 && D <= 128, "head_dim multiple of 16, <= 128");
+};
+
+template <int D>
+__global__ void __launch_bounds__(256) attn_fwd_fp32_kernel(const FwdParamsF32 p) {
+  using C = F32Cfg<D>;
+  extern __shared__ float fsm[];
+  float* Qs = fsm;
+  float* Ks = Qs + C::BM * C::SQ;
+  float* Vs = Ks + C::BN * C::SK;
+  float* Ps = Vs + C::BN * C::SV;
+
+  const int tid = threadIdx.x;
+  const int ty = tid >> 4, tx = tid & 15;
+  const int n_qblk = (p.Sq + C::BM - 1) / C::BM;
+  const int bh = blockIdx.x / n_qblk;
+  int qb = blockIdx.x - bh * n_qblk;
+  if (p.mask.causal) qb = n_qblk - 1 - qb;  // heaviest first
+  const int h = bh % p.H, b = bh / p.H;
+  const int q0 = qb * C::BM;
+
+  const float* qg = p.q + (long long)b * p.q_sb + (long long)h * p.q_sh;
+  const float* kg = p.k + (long long)b * p.k_sb + (long long)h * p.k_sh;
+  const float* vg = p.v + (long long)b * p.v_sb + (long long)h * p.v_sh;
+
+  // Q tile -> smem (rows past Sq are zero)
+  for (int i = tid; i < C::BM * (D / 4); i += 256) {
+    const int r = i / (D / 4), c4 = i % (D / 4);
+    float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (q0 + r < p.Sq) val = *reinterpret_cast<const float4*>(qg + (long long)(q0 + r) * p.q_ss + c4 * 4);
+    *reinterpret_cast<float4*>(Qs + r * C::SQ + c4 * 4) = val;
+  }
+
+  const long long r0 = q0;
+  const long long r1 = (q0 + C::BM < p.Sq) ? q0 + C::BM : p.Sq;
+  int tlo, thi;
+  kv_tile_range(p.mask, r0, r1, C::BN, tlo, thi);
+
+  float m[4], l[4], acc[4][C::ND];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m[i] = -INFINITY;
+    l[i] = 0.f;
+#pragma unroll
+    for (int d = 0; d < C::ND; ++d) acc[i][d] = 0.f;
+  }
+  const float sl2 = p.scale_log2;
+
+  for (int jt = tlo; jt < thi; ++jt) {
+    const int c0 = jt * C::BN;
+    __syncthreads();  // previous tile fully consumed (and Q stored, first time)
+    for (int i = tid; i < C::BN * (D / 4); i += 256) {
+      const int r = i / (D / 4), c4 = i % (D / 4);
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+      if (c0 + r < p.Skv) {
+        kv = *reinterpret_cast<const float4*>(kg + (long long)(c0 + r) * p.k_ss + c4 * 4);
+        vv = *reinterpret_cast<const float4*>(vg + (long long)(c0 + r) * p.v_ss + c4 * 4);
+      }
+      float* kd = Ks + r * C::SK + c4 * 4;
+      kd[0] = kv.x;
+      kd[1] = kv.y;
+      kd[2] = kv.z;
+      kd[3] = kv.w;
+      *reinterpret_cast<float4*>(Vs + r * C::SV + c4 * 4) = vv;
+    }
+    __syncthreads();
+
+    float s[4][C::NC];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int c = 0; c < C::NC; ++c) s[i][c] = 0.f;
+#pragma unroll 4
+    for (int d = 0; d < D; ++d) {
+      float qv[4], kv[C::NC];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) qv[i] = Qs[(ty * 4 + i) * C::SQ + d];
+#pragma unroll
+      for (int c = 0; c < C::NC; ++c) kv[c] = Ks[(tx + 16 * c) * C::SK + d];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int c = 0; c < C::NC; ++c) s[i][c] = fmaf(qv[i], kv[c], s[i][c]);
+    }
+
+    const bool full = tile_is_full(p.mask, r0, r1, c0, c0 + C::BN);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int row = q0 + ty * 4 + i;
+      int c_lo = 0, c_hi = C::BN - 1;
+      if (!full) row_col_interval(p.mask, row, c0, C::BN, c_lo, c_hi);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < C::NC; ++c) {
+        const int col = tx + 16 * c;
+        s[i][c] = (col < c_lo || col > c_hi) ? -INFINITY : s[i][c] * sl2;
+        mx = fmaxf(mx, s[i][c]);
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off, 16));
+      const float m_new = fmaxf(m[i], mx);
+      const float alpha = (m[i] == -INFINITY) ? 0.f : exp2f(m[i] - m_new);
+      const float mu = (m_new == -INFINITY) ? 0.f : m_new;
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < C::NC; ++c) {
+        const float e = exp2f(s[i][c] - mu);
+        rs += e;
+        Ps[(ty * 4 + i) * C::SP + tx + 16 * c] = e;
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) rs += __shfl_xor_sync(0xffffffffu, rs, off, 16);
+      l[i] = l[i] * alpha + rs;
+      m[i] = m_new;
+#pragma unroll
+      for (int d = 0; d < C::ND; ++d) acc[i][d] *= alpha;
+    }
+    __syncthreads();
+
+#pragma unroll 4
+    for (int kk = 0; kk < C::BN; ++kk) {
+      float pv[4], vv[C::ND];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) pv[i] = Ps[(ty * 4 + i) * C::SP + kk];
+#pragma unroll
+      for (int d = 0; d < C::ND; ++d) vv[d] = Vs[kk * C::SV + tx + 16 * d];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int d = 0; d < C::ND; ++d) acc[i][d] = fmaf(pv[i], vv[d], acc[i][d]);
+    }
+  }
+
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int row = q0 + ty * 4 + i;
+    if (row >= p.Sq) continue;
+    const float inv_l = (l[i] > 0.f) ? 1.0f / l[i] : 0.f;
+    float* og = p.o + (long long)b * p.o_sb + (long long)h * p.o_sh + (long long)row * p.o_ss;
+#pragma unroll
+    for (int d = 0; d < C::ND; ++d) og[tx + 16 * d] = acc[i][d] * inv_l;
+    if (p.lse != nullptr && tx == 0)
+      p.lse[((long long)b * p.H + h) * p.Sq + row] =
+          (l[i] > 0.f) ? (m[i] + log2f(l[i])) * 0.69314718055994531f : -INFINITY;
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// LSE merge: one warp per (b, h, s) row.
+// ------------------------------------------------------------------------------------------
+template <typename OutT>
+__device__ __forceinline__ void store_elem(OutT* p, float v);
+template <>
+__device__ __forceinline__ void store_elem<float>(float* p, float v) { *p = v; }
+template <>
+__device__ __forceinline__ void store_elem<__nv_bfloat16>(__nv_bfloat16* p, float v) {
+  *p = __float2bfloat16_rn(v);
+}
+template <>
+__device__ __forceinline__ void store_elem<__half>(__half* p, float v) {
+  *p = __float2half_rn(v);
+}
+
+template <typename OutT>
+__global__ void __launch_bounds__(256) lse_merge_kernel(const float* __restrict__ o_parts,
+                                                        const float* __restrict__ lse_parts,
+                                                        int n_parts, OutT* o, float* lse_out,
+                                                        int B, int H, int S, int D,
+                                                        long long o_sb, long long o_sh,
+                                                        long long o_ss) {
+  const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const long long n_rows = (long long)B * H * S;
+  if (row >= n_rows) return;
+  const long long part_rows = n_rows;
+  float mx = -INFINITY;
+  for (int i = 0; i < n_parts; ++i) mx = fmaxf(mx, lse_parts[i * part_rows + row]);
+  const long long s = row % S;
+  const long long bh = row / S;
+  const long long hh = bh % H, bb = bh / H;
+  OutT* orow = o + bb * o_sb + hh * o_sh + s * o_ss;
+  if (mx == -INFINITY) {
+    for (int d = lane; d < D; d += 32) store_elem<OutT>(orow + d, 0.f);
+    if (lse_out != nullptr && lane == 0) lse_out[row] = -INFINITY;
+    return;
+  }
+  float wsum = 0.f;
+  for (int i = 0; i < n_parts; ++i) wsum += expf(lse_parts[i * part_rows + row] - mx);
+  const float inv = 1.0f / wsum;
+  for (int d = lane; d < D; d += 32) {
+    float a = 0.f;
+    for (int i = 0; i < n_parts; ++i) {
+      const float w = expf(lse_parts[i * part_rows + row] - mx);
+      a = fmaf(w, o_parts[(i * part_rows + row) * D + d], a);
+    }
+    store_elem<OutT>(orow + d, a * inv);
+  }
+  if (lse_out != nullptr && lane == 0) lse_out[row] = mx + logf(wsum);
+}
+
+// (o_acc, lse_acc) <- merge((o_acc, lse_acc), (o_new, lse_new)), all fp32 contiguous.
+__global__ void __launch_bounds__(256) lse_merge_acc_kernel(float* __restrict__ o_acc,
+                                                            float* __restrict__ lse_acc,
+                                                            const float* __restrict__ o_new,
+                                                            const float* __restrict__ lse_new,
+                                                            long long n_rows, int D) {
+  const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= n_rows) return;
+  const float la = lse_acc[row], ln = lse_new[row];
+  const float mx = fmaxf(la, ln);
+  if (ln == -INFINITY) return;  // nothing to add
+  const float ea = (la == -INFINITY) ? 0.f : expf(la - mx);
+  const float en = expf(ln - mx);
+  const float sum = ea + en;
+  const float wa = ea / sum, wn = en / sum;
+  float* oa = o_acc + row * D;
+  const float* on = o_new + row * D;
+  for (int d = lane; d < D; d += 32) oa[d] = fmaf(wa, oa[d], wn * on[d]);
+  __syncwarp();
+  if (lane == 0) lse_acc[row] = mx + logf(sum);
+}
+
+template <typename OutT>
+__global__ void __launch_bounds__(256) cast_rows_kernel(const float* __restrict__ src, OutT* dst,
+                                                        long long n_rows, int H, int S, int D,
+                                                        long long o_sb, long long o_sh,
+                                                        long long o_ss) {
+  const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= n_rows) return;
+  const long long s = row % S, bh = row / S, hh = bh % H, bb = bh / H;
+  OutT* orow = dst + bb * o_sb + hh * o_sh + s * o_ss;
+  for (int d = lane; d < D; d += 32) store_elem<OutT>(orow + d, src[row * D + d]);
+}
+
+// Fills O with zeros and LSE with -inf (no admissible keys at all, e.g. Skv == 0).
+template <typename OutT>
+__global__ void __launch_bounds__(256) fill_empty_kernel(OutT* o, float* lse, long long n_rows,
+                                                         int H, int S, int D, long long o_sb,
+                                                         long long o_sh, long long o_ss) {
+  const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= n_rows) return;
+  const long long s = row % S, bh = row / S, hh = bh % H, bb = bh / H;
+  OutT* orow = o + bb * o_sb + hh * o_sh + s * o_ss;
+  for (int d = lane; d < D; d += 32) store_elem<OutT>(orow + d, 0.f);
+  if (lse != nullptr && lane == 0) lse[row] = -INFINITY;
+}
+
+// Self-test of the bounded wait: thread 0 initialises an mbarrier that nothing arrives on and
+// every thread waits on it with the given limit.
+__global__ void wait_selftest_kernel(int* status, unsigned long long timeout_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const WaitCtx w{&abort_flag, status, timeout_ns};
+  (void)mbar_wait(smem_u32(&bar), 0, w, 7);
+}
+
+}  // namespace mlxp

@@ -1,0 +1,602 @@
+// mlxp_attn.cu — host side of libmlxp_attn.so: argument validation, TMA tensor maps, the
+// key-split heuristic, kernel launches and the extern "C" entry points of include/mlxp_attn.h.
+//
+// The library never allocates device memory: splits write to a caller-provided workspace.
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/mlxp_attn.h"
+#include "attn_common.cuh"
+#include "attn_fwd_fp32.cuh"
+#include "attn_fwd_sm100.cuh"
+
+namespace mlxp {
+
+__device__ int g_dev_status = 0;
+
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(MLXP_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
+
+constexpr int kMaxDevices = 64;
+std::mutex g_dev_mu;
+int* g_status_ptr[kMaxDevices] = {};
+int g_num_sms[kMaxDevices] = {};
+unsigned g_attr_done[kMaxDevices] = {};
+
+int current_device(int& dev) {
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(MLXP_ERR_CUDA, "device ordinal %d out of range", dev);
+  return MLXP_OK;
+}
+
+// Device status word and SM count of the current device (looked up once per device).
+int device_info(int** status, int* sms) {
+  int dev;
+  if (int rc = current_device(dev)) return rc;
+  std::lock_guard<std::mutex> g(g_dev_mu);
+  if (g_status_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_dev_status);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(status)");
+    int n = 0;
+    e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+    g_status_ptr[dev] = static_cast<int*>(ptr);
+    g_num_sms[dev] = n;
+  }
+  if (status) *status = g_status_ptr[dev];
+  if (sms) *sms = g_num_sms[dev];
+  return MLXP_OK;
+}
+
+// Sets the dynamic shared memory limit of a kernel once per device.
+template <typename K>
+int ensure_smem_attr(K kernel, int bytes, unsigned bit) {
+  int dev;
+  if (int rc = current_device(dev)) return rc;
+  {
+    std::lock_guard<std::mutex> g(g_dev_mu);
+    if (g_attr_done[dev] & bit) return MLXP_OK;
+  }
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
+  std::lock_guard<std::mutex> g(g_dev_mu);
+  g_attr_done[dev] |= bit;
+  return MLXP_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+int g_encode_rc = MLXP_OK;
+std::string g_encode_err;
+
+int get_encode_fn() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr) {
+      g_encode_rc = MLXP_ERR_CUDA;
+      g_encode_err = "cudaGetDriverEntryPoint(cuTensorMapEncodeTiled) failed";
+      return;
+    }
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (g_encode_rc != MLXP_OK) return fail(g_encode_rc, "%s", g_encode_err.c_str());
+  return MLXP_OK;
+}
+
+// Builds a 4-D tensor map over a (b, h, s, d)-strided tensor with a box of 64 d-elements by
+// `box_rows` s-rows.  The three outer dims are ordered by stride so that the map is monotonic
+// whatever the layout (BHSD: s,h,b; BSHD: h,s,b); size-1 and stride-0 (broadcast) dims are
+// given coordinate 0.  The box lands in shared memory as box_rows rows of 128 bytes, 128-byte
+// swizzled, for every layout.
+int make_tmap(const void* ptr, bool bf16, int64_t B, int64_t H, int64_t S, int64_t D,
+              const int64_t st[4], int box_rows, const char* name, CUtensorMap* map,
+              TmaCoordMap* cm) {
+  if (int rc = get_encode_fn()) return rc;
+  const int es = 2;
+  if (reinterpret_cast<uintptr_t>(ptr) % 16)
+    return fail(MLXP_ERR_INVALID, "%s: base address must be 16-byte aligned", name);
+  if (st[3] != 1) return fail(MLXP_ERR_INVALID, "%s: head_dim stride must be 1", name);
+  struct Dim {
+    int64_t size, stride;
+    int which;  // 0 = s, 1 = h, 2 = b
+    bool unit;
+  } dims[3] = {{S, st[2], 0, false}, {H, st[1], 1, false}, {B, st[0], 2, false}};
+  bool bcast[3] = {false, false, false};
+  for (auto& d : dims) {
+    if (d.which != 0 && (d.size == 1 || d.stride == 0)) {
+      bcast[d.which] = true;
+      d.size = 1;
+      d.unit = true;
+    } else if (d.which == 0 && d.size == 1) {
+      d.unit = true;
+    } else {
+      if (d.stride <= 0)
+        return fail(MLXP_ERR_INVALID, "%s: stride of dim %d must be positive", name, d.which);
+      if ((d.stride * es) % 16)
+        return fail(MLXP_ERR_INVALID, "%s: strides must be multiples of 16 bytes", name);
+    }
+  }
+  std::stable_sort(dims, dims + 3, [](const Dim& a, const Dim& b) {
+    if (a.unit != b.unit) return !a.unit;  // size-1 dims last
+    return a.stride < b.stride;
+  });
+  // benign stride for unit dims: past the span of everything before them
+  int64_t span = D * es;
+  for (auto& d : dims) {
+    if (d.unit) {
+      d.stride = ((span + 15) / 16) * 16 / es;
+    }
+    span = std::max<int64_t>(span, d.stride * es * d.size);
+  }
+  cuuint64_t gdim[4] = {(cuuint64_t)D, (cuuint64_t)dims[0].size, (cuuint64_t)dims[1].size,
+                        (cuuint64_t)dims[2].size};
+  cuuint64_t gstride[3] = {(cuuint64_t)(dims[0].stride * es), (cuuint64_t)(dims[1].stride * es),
+                           (cuuint64_t)(dims[2].stride * es)};
+  cuuint32_t box[4] = {64, 1, 1, 1};
+  for (int i = 0; i < 3; ++i)
+    if (dims[i].which == 0) box[1 + i] = box_rows;
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = g_encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        4, const_cast<void*>(ptr), gdim, gstride, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(MLXP_ERR_INVALID, "%s: cuTensorMapEncodeTiled failed (code %d)", name, (int)r);
+  for (int i = 0; i < 3; ++i) {
+    if (dims[i].which == 0) cm->slot_s = (int8_t)(1 + i);
+    if (dims[i].which == 1) cm->slot_h = (int8_t)(1 + i);
+    if (dims[i].which == 2) cm->slot_b = (int8_t)(1 + i);
+  }
+  cm->bcast_h = bcast[1];
+  cm->bcast_b = bcast[2];
+  return MLXP_OK;
+}
+
+struct Problem {
+  int dtype;
+  int64_t B, H, Sq, Skv, D;
+  int causal;
+  int64_t wl, wr, qoff, kvoff;
+};
+
+MaskSpec mask_of(const Problem& pr) {
+  return MaskSpec{pr.causal, (long long)pr.wl, (long long)pr.wr, (long long)pr.qoff,
+                  (long long)pr.kvoff, (long long)pr.Skv};
+}
+
+int validate(const Problem& pr) {
+  if (pr.B <= 0 || pr.H <= 0 || pr.Sq < 0 || pr.Skv < 0 || pr.D <= 0)
+    return fail(MLXP_ERR_INVALID, "invalid shape B=%lld H=%lld Sq=%lld Skv=%lld D=%lld",
+                (long long)pr.B, (long long)pr.H, (long long)pr.Sq, (long long)pr.Skv,
+                (long long)pr.D);
+  if (pr.Sq > (1ll << 30) || pr.Skv > (1ll << 30) || pr.B * pr.H > (1ll << 24))
+    return fail(MLXP_ERR_INVALID, "shape too large");
+  if (pr.wl < -1 || pr.wr < -1) return fail(MLXP_ERR_INVALID, "window must be >= 0 or -1");
+  if (pr.dtype == MLXP_DTYPE_BF16 || pr.dtype == MLXP_DTYPE_FP16) {
+    if (pr.D != 64 && pr.D != 128)
+      return fail(MLXP_ERR_UNSUPPORTED, "bf16/fp16 attention supports head_dim 64 and 128, got %lld",
+                  (long long)pr.D);
+  } else if (pr.dtype == MLXP_DTYPE_FP32) {
+    if (pr.D != 32 && pr.D != 64 && pr.D != 128)
+      return fail(MLXP_ERR_UNSUPPORTED, "fp32 attention supports head_dim 32, 64 and 128, got %lld",
+                  (long long)pr.D);
+  } else {
+    return fail(MLXP_ERR_INVALID, "unknown dtype %d", pr.dtype);
+  }
+  return MLXP_OK;
+}
+
+constexpr int kBM2 = 256;  // query rows per tensor-core CTA
+constexpr int kBN = 128;   // keys per tensor-core tile
+
+// Key-range split count: splits exist only to fill the machine when there are few CTAs.
+int choose_splits(const Problem& pr, int sms) {
+  const long long n_qblk = (pr.Sq + kBM2 - 1) / kBM2;
+  const long long base = n_qblk * pr.B * pr.H;
+  const long long kv_tiles = (pr.Skv + kBN - 1) / kBN;
+  if (base <= 0 || kv_tiles < 16 || pr.causal || pr.wl >= 0 || pr.wr >= 0) return 1;
+  auto eff = [&](long long s) {
+    const long long ctas = base * s;
+    const long long waves = (ctas + sms - 1) / sms;
+    return double(ctas) / double(waves * sms);
+  };
+  int best = 1;
+  double best_eff = eff(1);
+  for (int s = 2; s <= 16; ++s) {
+    if (kv_tiles / s < 8) break;
+    const double e = eff(s);
+    if (e > best_eff + 0.05) {
+      best = s;
+      best_eff = e;
+    }
+  }
+  return best;
+}
+
+size_t split_workspace(const Problem& pr, int splits) {
+  if (splits <= 1) return 0;
+  const size_t rows = (size_t)splits * pr.B * pr.H * pr.Sq;
+  const size_t o_bytes = ((rows * pr.D * 4) + 255) / 256 * 256;
+  return o_bytes + rows * 4;
+}
+
+template <int D, bool BF16>
+struct TcKernel {
+  static constexpr int NSK = (D == 128) ? 2 : 3;
+  static constexpr int NSV = (D == 128) ? 2 : 3;
+  using Cfg = Sm100Cfg<D, NSK, NSV>;
+  static constexpr unsigned kBit = 1u << ((D == 128 ? 0 : 1) + (BF16 ? 0 : 2));
+  static int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                    const FwdParams& p, cudaStream_t stream) {
+    auto kern = attn_fwd_sm100_kernel<D, BF16, NSK, NSV>;
+    if (int rc = ensure_smem_attr(kern, Cfg::SMEM_ALLOC, kBit)) return rc;
+    const long long grid = (long long)p.n_qblk * p.B * p.H * p.splits;
+    if (grid <= 0) return MLXP_OK;
+    kern<<<(unsigned)grid, Cfg::THREADS, Cfg::SMEM_ALLOC, stream>>>(mq, mk, mv, p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "attn_fwd_sm100 launch");
+    return MLXP_OK;
+  }
+};
+
+int launch_tc(int D, bool bf16, const CUtensorMap& mq, const CUtensorMap& mk,
+              const CUtensorMap& mv, const FwdParams& p, cudaStream_t s) {
+  if (D == 128) return bf16 ? TcKernel<128, true>::launch(mq, mk, mv, p, s)
+                            : TcKernel<128, false>::launch(mq, mk, mv, p, s);
+  return bf16 ? TcKernel<64, true>::launch(mq, mk, mv, p, s)
+              : TcKernel<64, false>::launch(mq, mk, mv, p, s);
+}
+
+template <int D>
+int launch_f32_t(const FwdParamsF32& p, cudaStream_t s) {
+  using C = F32Cfg<D>;
+  auto kern = attn_fwd_fp32_kernel<D>;
+  if (int rc = ensure_smem_attr(kern, C::SMEM_BYTES, 1u << (8 + (D / 32)))) return rc;
+  const long long grid = (long long)((p.Sq + C::BM - 1) / C::BM) * p.B * p.H;
+  if (grid <= 0) return MLXP_OK;
+  kern<<<(unsigned)grid, 256, C::SMEM_BYTES, s>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "attn_fwd_fp32 launch");
+  return MLXP_OK;
+}
+
+int check_out_strides(const void* o, const int64_t st[4], int align_elems, const char* name) {
+  if (o == nullptr) return fail(MLXP_ERR_INVALID, "%s is null", name);
+  if (st[3] != 1) return fail(MLXP_ERR_INVALID, "%s: head_dim stride must be 1", name);
+  if (reinterpret_cast<uintptr_t>(o) % 16)
+    return fail(MLXP_ERR_INVALID, "%s: base address must be 16-byte aligned", name);
+  for (int i = 0; i < 3; ++i)
+    if (st[i] % align_elems)
+      return fail(MLXP_ERR_INVALID, "%s: strides must be multiples of 16 bytes", name);
+  return MLXP_OK;
+}
+
+int fill_empty(const Problem& pr, void* o, float* lse, const int64_t ost[4], cudaStream_t s) {
+  const long long rows = pr.B * pr.H * pr.Sq;
+  if (rows == 0) return MLXP_OK;
+  const unsigned grid = (unsigned)((rows + 7) / 8);
+  if (pr.dtype == MLXP_DTYPE_FP32)
+    fill_empty_kernel<float><<<grid, 256, 0, s>>>((float*)o, lse, rows, pr.H, pr.Sq, pr.D, ost[0], ost[1], ost[2]);
+  else if (pr.dtype == MLXP_DTYPE_BF16)
+    fill_empty_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((__nv_bfloat16*)o, lse, rows, pr.H, pr.Sq, pr.D, ost[0], ost[1], ost[2]);
+  else
+    fill_empty_kernel<__half><<<grid, 256, 0, s>>>((__half*)o, lse, rows, pr.H, pr.Sq, pr.D, ost[0], ost[1], ost[2]);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MLXP_OK : cuda_fail(e, "fill_empty launch");
+}
+
+template <typename OutT>
+int launch_merge(const float* o_parts, const float* lse_parts, int n, void* o, float* lse_out,
+                 const Problem& pr, const int64_t ost[4], cudaStream_t s) {
+  const long long rows = pr.B * pr.H * pr.Sq;
+  if (rows == 0) return MLXP_OK;
+  lse_merge_kernel<OutT><<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(
+      o_parts, lse_parts, n, (OutT*)o, lse_out, (int)pr.B, (int)pr.H, (int)pr.Sq, (int)pr.D,
+      ost[0], ost[1], ost[2]);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MLXP_OK : cuda_fail(e, "lse_merge launch");
+}
+
+int merge_dispatch(const float* o_parts, const float* lse_parts, int n, void* o, float* lse_out,
+                   const Problem& pr, const int64_t ost[4], cudaStream_t s) {
+  if (pr.dtype == MLXP_DTYPE_FP32) return launch_merge<float>(o_parts, lse_parts, n, o, lse_out, pr, ost, s);
+  if (pr.dtype == MLXP_DTYPE_BF16)
+    return launch_merge<__nv_bfloat16>(o_parts, lse_parts, n, o, lse_out, pr, ost, s);
+  return launch_merge<__half>(o_parts, lse_parts, n, o, lse_out, pr, ost, s);
+}
+
+// Shared implementation of mlxp_attn_fwd (out_f32 = 0) and mlxp_attn_fwd_partial (out_f32 = 1).
+int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* lse,
+                  const Problem& pr, const int64_t* qs, const int64_t* ks, const int64_t* vs,
+                  const int64_t* os, float scale, int64_t kv_splits, void* ws, size_t ws_bytes,
+                  bool out_f32, cudaStream_t stream) {
+  if (int rc = validate(pr)) return rc;
+  if (!(scale > 0.f) || !std::isfinite(scale))
+    return fail(MLXP_ERR_INVALID, "scale must be positive and finite");
+  if (!q || !k || !v) return fail(MLXP_ERR_INVALID, "q, k and v must be non-null");
+  if (!qs || !ks || !vs || !os) return fail(MLXP_ERR_INVALID, "stride arrays must be non-null");
+  if (out_f32 && lse == nullptr) return fail(MLXP_ERR_INVALID, "partial output needs lse");
+  const bool fp32 = pr.dtype == MLXP_DTYPE_FP32;
+  if (int rc = check_out_strides(o, os, (fp32 || out_f32) ? 4 : 8, "o")) return rc;
+  if (reinterpret_cast<uintptr_t>(lse) % 4) return fail(MLXP_ERR_INVALID, "lse misaligned");
+  if (pr.Sq == 0) return MLXP_OK;
+  int* status = nullptr;
+  int sms = 0;
+  if (int rc = device_info(&status, &sms)) return rc;
+
+  Problem pe = pr;
+  if (out_f32) pe.dtype = MLXP_DTYPE_FP32;  // output element type for the empty fill
+  if (pr.Skv == 0) return fill_empty(pe, o, lse, os, stream);
+
+  const float scale_log2 = scale * 1.4426950408889634f;
+  if (fp32) {
+    for (const int64_t* st : {qs, ks, vs})
+      if (st[3] != 1 || (st[0] % 4) || (st[1] % 4) || (st[2] % 4))
+        return fail(MLXP_ERR_INVALID, "fp32 q/k/v need unit head_dim stride and 16-byte aligned rows");
+    for (const void* ptr : {q, k, v})
+      if (reinterpret_cast<uintptr_t>(ptr) % 16)
+        return fail(MLXP_ERR_INVALID, "fp32 q/k/v base addresses must be 16-byte aligned");
+    FwdParamsF32 p{};
+    p.B = (int)pr.B;
+    p.H = (int)pr.H;
+    p.Sq = (int)pr.Sq;
+    p.Skv = (int)pr.Skv;
+    p.q = (const float*)q;
+    p.k = (const float*)k;
+    p.v = (const float*)v;
+    p.q_sb = qs[0]; p.q_sh = qs[1]; p.q_ss = qs[2];
+    p.k_sb = ks[0]; p.k_sh = ks[1]; p.k_ss = ks[2];
+    p.v_sb = vs[0]; p.v_sh = vs[1]; p.v_ss = vs[2];
+    p.o = (float*)o;
+    p.o_sb = os[0]; p.o_sh = os[1]; p.o_ss = os[2];
+    p.lse = lse;
+    p.scale_log2 = scale_log2;
+    p.mask = mask_of(pr);
+    switch (pr.D) {
+      case 32: return launch_f32_t<32>(p, stream);
+      case 64: return launch_f32_t<64>(p, stream);
+      default: return launch_f32_t<128>(p, stream);
+    }
+  }
+
+  const bool bf16 = pr.dtype == MLXP_DTYPE_BF16;
+  CUtensorMap mq, mk, mv;
+  FwdParams p{};
+  if (int rc = make_tmap(q, bf16, pr.B, pr.H, pr.Sq, pr.D, qs, 128, "q", &mq, &p.cq)) return rc;
+  if (int rc = make_tmap(k, bf16, pr.B, pr.H, pr.Skv, pr.D, ks, kBN, "k", &mk, &p.ck)) return rc;
+  if (int rc = make_tmap(v, bf16, pr.B, pr.H, pr.Skv, pr.D, vs, kBN, "v", &mv, &p.cv)) return rc;
+
+  int splits = 1;
+  if (!out_f32) {
+    if (kv_splits == 0) splits = choose_splits(pr, sms);
+    else if (kv_splits > 1) splits = (int)std::min<int64_t>(kv_splits, (pr.Skv + kBN - 1) / kBN);
+  }
+  p.B = (int)pr.B;
+  p.H = (int)pr.H;
+  p.Sq = (int)pr.Sq;
+  p.Skv = (int)pr.Skv;
+  p.n_qblk = (int)((pr.Sq + kBM2 - 1) / kBM2);
+  p.splits = splits;
+  const int kv_tiles = (int)((pr.Skv + kBN - 1) / kBN);
+  p.tiles_per_split = (kv_tiles + splits - 1) / splits;
+  p.heavy_first = pr.causal ? 1 : 0;
+  p.scale_log2 = scale_log2;
+  p.mask = mask_of(pr);
+  p.status = status;
+  p.timeout_ns = g_timeout_ns.load();
+
+  if (splits == 1) {
+    p.out_f32 = out_f32 ? 1 : 0;
+    p.o = o;
+    p.o_sb = os[0];
+    p.o_sh = os[1];
+    p.o_ss = os[2];
+    p.o_split = 0;
+    p.lse = lse;
+    p.lse_split = 0;
+    return launch_tc((int)pr.D, bf16, mq, mk, mv, p, stream);
+  }
+  const size_t need = split_workspace(pr, splits);
+  if (ws == nullptr || ws_bytes < need)
+    return fail(MLXP_ERR_WORKSPACE, "workspace of %zu bytes needed for %d key splits, got %zu",
+                need, splits, ws_bytes);
+  if (reinterpret_cast<uintptr_t>(ws) % 256)
+    return fail(MLXP_ERR_INVALID, "workspace must be 256-byte aligned");
+  const long long rows = pr.B * pr.H * pr.Sq;
+  float* o_parts = static_cast<float*>(ws);
+  float* lse_parts = reinterpret_cast<float*>(static_cast<char*>(ws) +
+                                              ((size_t)splits * rows * pr.D * 4 + 255) / 256 * 256);
+  p.out_f32 = 1;
+  p.o = o_parts;
+  p.o_sb = pr.H * pr.Sq * pr.D;
+  p.o_sh = pr.Sq * pr.D;
+  p.o_ss = pr.D;
+  p.o_split = rows * pr.D;
+  p.lse = lse_parts;
+  p.lse_split = rows;
+  if (int rc = launch_tc((int)pr.D, bf16, mq, mk, mv, p, stream)) return rc;
+  return merge_dispatch(o_parts, lse_parts, splits, o, lse, pr, os, stream);
+}
+
+}  // namespace
+}  // namespace mlxp
+
+using namespace mlxp;
+
+extern "C" {
+
+int mlxp_version(void) { return 100; }
+
+const char* mlxp_last_error(void) { return t_last_error.c_str(); }
+
+int mlxp_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int dtype,
+                  int64_t B, int64_t H, int64_t Sq, int64_t Skv, int64_t D,
+                  const int64_t q_strides[4], const int64_t k_strides[4],
+                  const int64_t v_strides[4], const int64_t o_strides[4], float scale,
+                  int causal, int64_t window_left, int64_t window_right, int64_t q_pos_offset,
+                  int64_t kv_pos_offset, int64_t kv_splits, void* workspace, size_t ws_bytes,
+                  void* cuda_stream) {
+  Problem pr{dtype, B, H, Sq, Skv, D, causal ? 1 : 0, window_left, window_right, q_pos_offset,
+             kv_pos_offset};
+  return attn_fwd_impl(q, k, v, o, lse, pr, q_strides, k_strides, v_strides, o_strides, scale,
+                       kv_splits, workspace, ws_bytes, false,
+                       static_cast<cudaStream_t>(cuda_stream));
+}
+
+size_t mlxp_attn_workspace_size(int dtype, int64_t B, int64_t H, int64_t Sq, int64_t Skv,
+                                int64_t D, int causal, int64_t window_left,
+                                int64_t window_right, int64_t q_pos_offset,
+                                int64_t kv_pos_offset, int64_t kv_splits) {
+  Problem pr{dtype, B, H, Sq, Skv, D, causal ? 1 : 0, window_left, window_right, q_pos_offset,
+             kv_pos_offset};
+  if (validate(pr) != MLXP_OK || dtype == MLXP_DTYPE_FP32 || Sq == 0 || Skv == 0) return 0;
+  int splits = 1;
+  if (kv_splits == 0) {
+    int sms = 148;
+    if (device_info(nullptr, &sms) != MLXP_OK) sms = 148;
+    splits = choose_splits(pr, sms);
+  } else if (kv_splits > 1) {
+    splits = (int)std::min<int64_t>(kv_splits, (Skv + kBN - 1) / kBN);
+  }
+  return split_workspace(pr, splits);
+}
+
+int mlxp_attn_fwd_partial(const void* q, const void* k, const void* v, float* o_part,
+                          float* lse_part, int dtype, int64_t B, int64_t H, int64_t Sq,
+                          int64_t Skv, int64_t D, const int64_t q_strides[4],
+                          const int64_t k_strides[4], const int64_t v_strides[4],
+                          const int64_t o_strides[4], float scale, int causal,
+                          int64_t window_left, int64_t window_right, int64_t q_pos_offset,
+                          int64_t kv_pos_offset, void* cuda_stream) {
+  if (dtype == MLXP_DTYPE_FP32)
+    return fail(MLXP_ERR_UNSUPPORTED, "mlxp_attn_fwd_partial takes bf16/fp16 inputs");
+  Problem pr{dtype, B, H, Sq, Skv, D, causal ? 1 : 0, window_left, window_right, q_pos_offset,
+             kv_pos_offset};
+  return attn_fwd_impl(q, k, v, o_part, lse_part, pr, q_strides, k_strides, v_strides,
+                       o_strides, scale, 1, nullptr, 0, true,
+                       static_cast<cudaStream_t>(cuda_stream));
+}
+
+int mlxp_lse_merge(const float* o_parts, const float* lse_parts, int64_t n_parts, void* o,
+                   float* lse_out, int dtype, int64_t B, int64_t H, int64_t S, int64_t D,
+                   const int64_t o_strides[4], void* cuda_stream) {
+  if (!o_parts || !lse_parts || n_parts < 1 || B < 1 || H < 1 || S < 0 || D < 1)
+    return fail(MLXP_ERR_INVALID, "invalid lse_merge arguments");
+  if (dtype < 0 || dtype > 2) return fail(MLXP_ERR_INVALID, "unknown dtype %d", dtype);
+  if (!o_strides || o == nullptr || o_strides[3] != 1)
+    return fail(MLXP_ERR_INVALID, "o must be non-null with unit head_dim stride");
+  Problem pr{dtype, B, H, S, 0, D, 0, -1, -1, 0, 0};
+  return merge_dispatch(o_parts, lse_parts, (int)n_parts, o, lse_out, pr, o_strides,
+                        static_cast<cudaStream_t>(cuda_stream));
+}
+
+int mlxp_lse_merge_accumulate(float* o_acc, float* lse_acc, const float* o_new,
+                              const float* lse_new, int64_t B, int64_t H, int64_t S, int64_t D,
+                              void* cuda_stream) {
+  if (!o_acc || !lse_acc || !o_new || !lse_new || B < 1 || H < 1 || S < 0 || D < 1)
+    return fail(MLXP_ERR_INVALID, "invalid lse_merge_accumulate arguments");
+  const long long rows = B * H * S;
+  if (rows == 0) return MLXP_OK;
+  lse_merge_acc_kernel<<<(unsigned)((rows + 7) / 8), 256, 0,
+                         static_cast<cudaStream_t>(cuda_stream)>>>(o_acc, lse_acc, o_new,
+                                                                   lse_new, rows, (int)D);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MLXP_OK : cuda_fail(e, "lse_merge_accumulate launch");
+}
+
+int mlxp_cast_output(const float* o_acc, void* o, int dtype, int64_t B, int64_t H, int64_t S,
+                     int64_t D, const int64_t o_strides[4], void* cuda_stream) {
+  if (!o_acc || !o || !o_strides || o_strides[3] != 1 || B < 1 || H < 1 || S < 0 || D < 1)
+    return fail(MLXP_ERR_INVALID, "invalid cast_output arguments");
+  const long long rows = B * H * S;
+  if (rows == 0) return MLXP_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(cuda_stream);
+  const unsigned grid = (unsigned)((rows + 7) / 8);
+  if (dtype == MLXP_DTYPE_FP32)
+    cast_rows_kernel<float><<<grid, 256, 0, s>>>(o_acc, (float*)o, rows, (int)H, (int)S, (int)D, o_strides[0], o_strides[1], o_strides[2]);
+  else if (dtype == MLXP_DTYPE_BF16)
+    cast_rows_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(o_acc, (__nv_bfloat16*)o, rows, (int)H, (int)S, (int)D, o_strides[0], o_strides[1], o_strides[2]);
+  else if (dtype == MLXP_DTYPE_FP16)
+    cast_rows_kernel<__half><<<grid, 256, 0, s>>>(o_acc, (__half*)o, rows, (int)H, (int)S, (int)D, o_strides[0], o_strides[1], o_strides[2]);
+  else
+    return fail(MLXP_ERR_INVALID, "unknown dtype %d", dtype);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MLXP_OK : cuda_fail(e, "cast_output launch");
+}
+
+int mlxp_device_status(int* status_out, int reset) {
+  int* status = nullptr;
+  if (int rc = device_info(&status, nullptr)) return rc;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  int v = 0;
+  e = cudaMemcpy(&v, status, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "read device status");
+  if (status_out) *status_out = v;
+  if (reset) {
+    const int zero = 0;
+    e = cudaMemcpy(status, &zero, sizeof(int), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e, "reset device status");
+  }
+  return MLXP_OK;
+}
+
+int mlxp_set_wait_timeout_ns(uint64_t ns) {
+  if (ns == 0) return fail(MLXP_ERR_INVALID, "timeout must be positive");
+  g_timeout_ns.store(ns);
+  return MLXP_OK;
+}
+
+int mlxp_selftest_wait_timeout(uint64_t timeout_ns, void* cuda_stream) {
+  int* status = nullptr;
+  if (int rc = device_info(&status, nullptr)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(cuda_stream);
+  const int zero = 0;
+  cudaError_t e0 = cudaMemcpy(status, &zero, sizeof(int), cudaMemcpyHostToDevice);
+  if (e0 != cudaSuccess) return cuda_fail(e0, "selftest reset status");
+  // The self-test reports through the status word, the wait's own error channel.
+  wait_selftest_kernel<<<1, 64, 0, s>>>(status, (unsigned long long)timeout_ns);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "selftest launch");
+  e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "selftest sync");
+  int v = 0;
+  e = cudaMemcpy(&v, status, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "selftest read status");
+  if ((v & 0xff) == kDevTimeout) return fail(MLXP_ERR_TIMEOUT, "bounded wait gave up at site %d", v >> 8);
+  return MLXP_OK;
+}
+
+}  // extern "C"

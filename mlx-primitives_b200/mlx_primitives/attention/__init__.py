@@ -1,0 +1,23 @@
+"""Attention forward path of mlx_primitives, rebuilt for B200 (sm_100a).
+
+The public names match mlx_primitives/attention/__init__.py of the reference for the attention
+kernels: flash, sliding-window and chunked cross-attention, plus the sequence-parallel ring
+pass that runs the causal long-context case over several GPUs.
+"""
+
+from .chunked import ChunkedCrossAttention, chunked_cross_attention, estimate_memory_savings
+from .flash import FlashAttention, flash_attention, get_optimal_flash_config
+from .sliding_window import (SlidingWindowAttention, create_sliding_window_mask,
+                             sliding_window_attention)
+
+__all__ = [
+    "sliding_window_attention",
+    "create_sliding_window_mask",
+    "SlidingWindowAttention",
+    "flash_attention",
+    "FlashAttention",
+    "get_optimal_flash_config",
+    "chunked_cross_attention",
+    "ChunkedCrossAttention",
+    "estimate_memory_savings",
+]

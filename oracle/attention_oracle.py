@@ -1,0 +1,349 @@
+"""CPU oracle for the attention forward path — TEST INFRASTRUCTURE ONLY.
+
+This module restates, in numpy, the algorithms of the reference's attention path
+(zakkeown/mlx-primitives, mlx_primitives/attention/*.py).  Only tests/, __graft_entry__.smoke()
+and bench.py's CPU-baseline / reference arm may import it, and only as the checker or the timed
+CPU baseline.  The product (mlx_primitives + libmlxp_attn.so) never calls it.
+
+Parity is pinned: tests/golden/*.npz hold outputs of the reference's own Python code paths
+(flash.py:257-316 tiled loop, flash.py:479-525 dense path, sliding_window.py:363-511 tiled
+loop, chunked.py:129-203 chunk loop and dense path, _online_softmax.py:42-176 merge/chunk
+helpers) executed over a numpy stand-in for the mlx.core array functions they call
+(tests/golden/make_golden.py); tests/test_oracle_golden.py checks this restatement against them.
+
+Conventions (file:line in the reference):
+  mask value -1e38                                   constants.py:100
+  softmax-denominator epsilon 1e-6 (tiled paths)     constants.py:110, flash.py:312
+  causal, equal lengths: j <= i                      flash.py:286, _online_softmax.py:149-161
+  causal mask Sq != Skv: bottom-right aligned        utils/masking.py:14-66 (triu k=Skv-Sq+1)
+  sliding window: |i - j| <= W (and j <= i)          sliding_window.py:136-161
+  chunked causal: top-left absolute positions        chunked.py:192-197
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+MASK_VALUE = -1e38     # constants.py:100 ATTENTION_MASK_VALUE
+SOFTMAX_EPS = 1e-6     # constants.py:110 METAL_SOFTMAX_EPSILON
+
+
+# ----------------------------------------------------------------------------------------
+# Masks
+# ----------------------------------------------------------------------------------------
+def admissible(sq: int, skv: int, causal: bool, window_left: int = -1, window_right: int = -1,
+               q_offset: int = 0, kv_offset: int = 0) -> np.ndarray:
+    """Boolean (sq, skv): key j admissible for query i, positions qpos = i + q_offset,
+    kpos = j + kv_offset (the C-ABI's convention)."""
+    qpos = np.arange(sq, dtype=np.int64)[:, None] + q_offset
+    kpos = np.arange(skv, dtype=np.int64)[None, :] + kv_offset
+    ok = np.ones((sq, skv), dtype=bool)
+    if causal:
+        ok &= kpos <= qpos
+    if window_left >= 0:
+        ok &= (qpos - kpos) <= window_left
+    if window_right >= 0:
+        ok &= (kpos - qpos) <= window_right
+    return ok
+
+
+def create_causal_mask(seq_q: int, seq_kv: int, dtype=np.float32) -> np.ndarray:
+    """utils/masking.py:14-66: additive -1e38 above diagonal offset seq_kv - seq_q + 1."""
+    return np.triu(np.full((seq_q, seq_kv), MASK_VALUE, dtype=dtype), k=seq_kv - seq_q + 1)
+
+
+def create_sliding_window_mask(seq_len: int, window_size: int, causal: bool = True) -> np.ndarray:
+    """sliding_window.py:628-656: True where |i - j| <= W (and j <= i if causal)."""
+    pos = np.arange(seq_len)
+    mask = np.abs(pos[:, None] - pos[None, :]) <= window_size
+    if causal:
+        mask &= pos[None, :] <= pos[:, None]
+    return mask
+
+
+# ----------------------------------------------------------------------------------------
+# Dense attention: the semantic definition every kernel is checked against
+# ----------------------------------------------------------------------------------------
+def attention_bhsd(q, k, v, scale: float, causal: bool = False, window_left: int = -1,
+                   window_right: int = -1, q_offset: int = 0, kv_offset: int = 0,
+                   dtype=np.float64, empty_rows: str = "zero", return_lse: bool = False):
+    """softmax(scale * Q K^T + mask) V per (b, h) for BHSD arrays, computed in `dtype`.
+
+    This is the reference's dense path (flash.py:186-192 / 479-525, sliding_window.py:514-560,
+    chunked.py:172-203) with the mask given in absolute positions.  Rows with no admissible key:
+    empty_rows="zero" gives O = 0 / LSE = -inf (the B200 library's definition); "mean" gives the
+    reference's finite-mask result mean(V) (every score replaced by -1e38).
+    """
+    q = np.asarray(q, dtype=dtype)
+    k = np.asarray(k, dtype=dtype)
+    v = np.asarray(v, dtype=dtype)
+    B, H, Sq, D = q.shape
+    Skv = k.shape[2]
+    ok = admissible(Sq, Skv, causal, window_left, window_right, q_offset, kv_offset)
+    empty = ~ok.any(axis=1)
+    out = np.zeros((B, H, Sq, v.shape[3]), dtype=dtype)
+    lse = np.full((B, H, Sq), -np.inf, dtype=np.float64)
+    for b in range(B):
+        for h in range(H):
+            s = (q[b, h] @ k[b, h].T) * scale
+            s = np.where(ok, s, -np.inf)
+            m = s.max(axis=1, keepdims=True)
+            m = np.where(np.isfinite(m), m, 0.0)
+            e = np.exp(s - m)
+            den = e.sum(axis=1, keepdims=True)
+            o = (e @ v[b, h]) / np.where(den > 0, den, 1.0)
+            with np.errstate(divide="ignore"):
+                lse[b, h] = np.where(den[:, 0] > 0, np.log(np.where(den[:, 0] > 0, den[:, 0], 1.0)) + m[:, 0], -np.inf)
+            if empty.any():
+                o[empty] = v[b, h].mean(axis=0) if empty_rows == "mean" else 0.0
+            out[b, h] = o
+    return (out, lse) if return_lse else out
+
+
+def attention_rows_bhsd(q, k, v, rows, scale: float, causal: bool = True, window_left: int = -1,
+                        window_right: int = -1, q_offset: int = 0, kv_offset: int = 0,
+                        bh=None):
+    """Exact fp64 outputs for selected query rows only: [len(bh), len(rows), D].
+
+    Row-sampled oracle for shapes whose full score matrix is too large (e.g. 128K tokens):
+    each sampled row against its full admissible key range.  `bh` lists (b, h) pairs
+    (default: all)."""
+    q = np.asarray(q)
+    B, H = q.shape[:2]
+    pairs = bh if bh is not None else [(b, h) for b in range(B) for h in range(H)]
+    rows = np.asarray(rows, dtype=np.int64)
+    out = np.zeros((len(pairs), len(rows), v.shape[3]), dtype=np.float64)
+    Skv = k.shape[2]
+    for n, (b, h) in enumerate(pairs):
+        qs = np.asarray(q[b, h, rows], dtype=np.float64)
+        kk = np.asarray(k[b, h], dtype=np.float64)
+        vv = np.asarray(v[b, h], dtype=np.float64)
+        s = (qs @ kk.T) * scale
+        qpos = rows[:, None] + q_offset
+        kpos = np.arange(Skv)[None, :] + kv_offset
+        ok = np.ones_like(s, dtype=bool)
+        if causal:
+            ok &= kpos <= qpos
+        if window_left >= 0:
+            ok &= (qpos - kpos) <= window_left
+        if window_right >= 0:
+            ok &= (kpos - qpos) <= window_right
+        s = np.where(ok, s, -np.inf)
+        m = s.max(axis=1, keepdims=True)
+        e = np.exp(s - m)
+        out[n] = (e @ vv) / e.sum(axis=1, keepdims=True)
+    return out
+
+
+def to_bhsd(x, layout: str):
+    return x if layout == "BHSD" else np.swapaxes(x, 1, 2)
+
+
+def from_bhsd(x, layout: str):
+    return x if layout == "BHSD" else np.swapaxes(x, 1, 2)
+
+
+# ----------------------------------------------------------------------------------------
+# Public-API semantics of the reference (what each entry point computes)
+# ----------------------------------------------------------------------------------------
+def flash_attention(q, k, v, scale=None, causal=True, layout="BSHD", dtype=np.float64):
+    """flash.py:52-254 semantics: causal aligned bottom-right (SDPA mask="causal",
+    utils/masking.py:14-66), default scale 1/sqrt(head_dim), output in `layout`."""
+    qb, kb, vb = (to_bhsd(np.asarray(t), layout) for t in (q, k, v))
+    if scale is None:
+        scale = 1.0 / math.sqrt(qb.shape[-1])
+    sq, skv = qb.shape[2], kb.shape[2]
+    o = attention_bhsd(qb, kb, vb, scale, causal=causal, q_offset=(skv - sq) if causal else 0,
+                       dtype=dtype)
+    return from_bhsd(o, layout)
+
+
+def sliding_window_attention(q, k, v, window_size, scale=None, causal=True, dtype=np.float64):
+    """sliding_window.py:227-312 semantics (BSHD): |i - j| <= W, and j <= i if causal."""
+    qb, kb, vb = (to_bhsd(np.asarray(t), "BSHD") for t in (q, k, v))
+    if scale is None:
+        scale = 1.0 / math.sqrt(qb.shape[-1])
+    o = attention_bhsd(qb, kb, vb, scale, causal=causal, window_left=window_size,
+                       window_right=-1 if causal else window_size, dtype=dtype)
+    return from_bhsd(o, "BSHD")
+
+
+def chunked_cross_attention(q, k, v, chunk_size=1024, scale=None, causal=False, dtype=np.float64):
+    """chunked.py:43-126 semantics (BSHD): full attention over Skv, causal top-left."""
+    qb, kb, vb = (to_bhsd(np.asarray(t), "BSHD") for t in (q, k, v))
+    if scale is None:
+        scale = 1.0 / math.sqrt(qb.shape[-1])
+    o = attention_bhsd(qb, kb, vb, scale, causal=causal, dtype=dtype)
+    return from_bhsd(o, "BSHD")
+
+
+# ----------------------------------------------------------------------------------------
+# The reference's own blockwise algorithms (fp32, as MLX computes them)
+# ----------------------------------------------------------------------------------------
+def compute_chunk_attention(q, k_chunk, v_chunk, scale, causal=False, q_offset=0, kv_offset=0):
+    """_online_softmax.py:109-176 — BSHD block scores, -1e38 causal mask in absolute
+    positions, row max m, row sum l of exp(s - m), unnormalised O = sum exp(s - m) V."""
+    s = np.einsum("bqhd,bkhd->bqhk", q, k_chunk).astype(np.float32) * np.float32(scale)
+    if causal:
+        qpos = np.arange(q.shape[1]) + q_offset
+        kpos = np.arange(k_chunk.shape[1]) + kv_offset
+        ok = kpos[None, :] <= qpos[:, None]
+        s = np.where(ok[None, :, None, :], s, np.float32(MASK_VALUE))
+    m = s.max(axis=-1)
+    e = np.exp(s - m[..., None])
+    l = e.sum(axis=-1)
+    o = np.einsum("bqhk,bkhd->bqhd", e, v_chunk)
+    return o.astype(np.float32), m.astype(np.float32), l.astype(np.float32)
+
+
+def online_softmax_merge(acc_o, acc_m, acc_l, new_o, new_m, new_l):
+    """_online_softmax.py:42-106 — m' = max(m1, m2); l' = l1 e^(m1-m') + l2 e^(m2-m');
+    O' = O1 e^(m1-m') + O2 e^(m2-m')."""
+    gm = np.maximum(acc_m, new_m)
+    ca = np.exp(acc_m - gm)
+    cn = np.exp(new_m - gm)
+    return acc_o * ca[..., None] + new_o * cn[..., None], gm, acc_l * ca + new_l * cn
+
+
+def tiled_flash_attention(q, k, v, scale, causal, block_q=32, block_kv=32):
+    """flash.py:257-316 — query blocks x key blocks (causal: keys < q_end), merged with
+    online_softmax_merge, normalised by (l + 1e-6)."""
+    q, k, v = (np.asarray(t, dtype=np.float32) for t in (q, k, v))
+    B, S, H, D = q.shape
+    outs = []
+    for q0 in range(0, S, block_q):
+        q1 = min(q0 + block_q, S)
+        n = q1 - q0
+        m = np.full((B, n, H), MASK_VALUE, dtype=np.float32)
+        l = np.zeros((B, n, H), dtype=np.float32)
+        o = np.zeros((B, n, H, D), dtype=np.float32)
+        limit = q1 if causal else S
+        for k0 in range(0, limit, block_kv):
+            k1 = min(k0 + block_kv, limit)
+            co, cm, cl = compute_chunk_attention(q[:, q0:q1], k[:, k0:k1], v[:, k0:k1], scale,
+                                                 causal=causal, q_offset=q0, kv_offset=k0)
+            o, m, l = online_softmax_merge(o, m, l, co, cm, cl)
+        outs.append(o / (l[..., None] + np.float32(SOFTMAX_EPS)))
+    return np.concatenate(outs, axis=1)
+
+
+def tiled_sliding_window_attention(q, k, v, window_size, scale, causal, block_q=32):
+    """sliding_window.py:363-511 — key range [max(0, q0 - W), q_end) (causal) or
+    [max(0, q0 - W), min(S, q_end + W)), exact |i - j| <= W (+ causal) mask per element."""
+    q, k, v = (np.asarray(t, dtype=np.float32) for t in (q, k, v))
+    B, S, H, D = q.shape
+    outs = []
+    for q0 in range(0, S, block_q):
+        q1 = min(q0 + block_q, S)
+        n = q1 - q0
+        m = np.full((B, n, H), MASK_VALUE, dtype=np.float32)
+        l = np.zeros((B, n, H), dtype=np.float32)
+        o = np.zeros((B, n, H, D), dtype=np.float32)
+        k_lo = max(0, q0 - window_size)
+        k_hi = q1 if causal else min(S, q1 + window_size)
+        for k0 in range(k_lo, k_hi, block_q):
+            k1 = min(k0 + block_q, k_hi)
+            s = np.einsum("bqhd,bkhd->bqhk", q[:, q0:q1], k[:, k0:k1]) * np.float32(scale)
+            qpos = np.arange(q0, q1)[:, None]
+            kpos = np.arange(k0, k1)[None, :]
+            ok = np.abs(qpos - kpos) <= window_size
+            if causal:
+                ok &= kpos <= qpos
+            s = np.where(ok[None, :, None, :], s, np.float32(MASK_VALUE))
+            cm = s.max(axis=-1)
+            e = np.exp(s - cm[..., None])
+            cl = e.sum(axis=-1)
+            co = np.einsum("bqhk,bkhd->bqhd", e, v[:, k0:k1])
+            o, m, l = online_softmax_merge(o, m, l, co, cm, cl)
+        outs.append(o / (l[..., None] + np.float32(SOFTMAX_EPS)))
+    return np.concatenate(outs, axis=1)
+
+
+def chunked_cross_attention_loop(q, k, v, chunk_size, scale, causal=False):
+    """chunked.py:129-169 — for each key chunk: compute_chunk_attention (q_offset 0,
+    kv_offset = chunk start), online_softmax_merge; finally / (l + 1e-6)."""
+    q, k, v = (np.asarray(t, dtype=np.float32) for t in (q, k, v))
+    B, Sq, H, D = q.shape
+    o = np.zeros((B, Sq, H, D), dtype=np.float32)
+    m = np.full((B, Sq, H), MASK_VALUE, dtype=np.float32)
+    l = np.zeros((B, Sq, H), dtype=np.float32)
+    for c0 in range(0, k.shape[1], chunk_size):
+        c1 = min(c0 + chunk_size, k.shape[1])
+        co, cm, cl = compute_chunk_attention(q, k[:, c0:c1], v[:, c0:c1], scale, causal=causal,
+                                             q_offset=0, kv_offset=c0)
+        o, m, l = online_softmax_merge(o, m, l, co, cm, cl)
+    return o / (l[..., None] + np.float32(SOFTMAX_EPS))
+
+
+# ----------------------------------------------------------------------------------------
+# LSE form of the merge (what the split-KV and ring kernels compute)
+# ----------------------------------------------------------------------------------------
+def lse_merge(o_parts, lse_parts):
+    """Merge normalised partials: w_i = exp(lse_i - max lse); O = sum w_i O_i / sum w_i."""
+    o_parts = np.asarray(o_parts, dtype=np.float64)
+    lse_parts = np.asarray(lse_parts, dtype=np.float64)
+    mx = lse_parts.max(axis=0)
+    safe = np.where(np.isfinite(mx), mx, 0.0)
+    w = np.exp(lse_parts - safe)
+    den = w.sum(axis=0)
+    o = (w[..., None] * o_parts).sum(axis=0) / np.where(den > 0, den, 1.0)[..., None]
+    with np.errstate(divide="ignore"):
+        lse = np.where(den > 0, safe + np.log(np.where(den > 0, den, 1.0)), -np.inf)
+    return o, lse
+
+
+# ----------------------------------------------------------------------------------------
+# Zig-zag ring schedule (the sequence-parallel split of the 128K-token causal config)
+# ----------------------------------------------------------------------------------------
+def zigzag_chunks(world: int, rank: int):
+    """Global chunk ids held by `rank` when the sequence is cut into 2*world chunks."""
+    return (rank, 2 * world - 1 - rank)
+
+
+def ring_reference(q, k, v, world: int, scale: float):
+    """Run the zig-zag ring schedule serially on CPU for BHSD q/k/v of the full sequence and
+    return the full output: every rank's local queries against every K/V block that reaches it,
+    each pair a partial (O, LSE) merged with lse_merge.  Must equal attention_bhsd(causal)."""
+    q, k, v = (np.asarray(t, dtype=np.float64) for t in (q, k, v))
+    B, H, S, D = q.shape
+    C = S // (2 * world)
+    out = np.zeros_like(q)
+    for r in range(world):
+        for qc in zigzag_chunks(world, r):
+            qs = q[:, :, qc * C:(qc + 1) * C]
+            parts_o, parts_l = [], []
+            for step in range(world):
+                src = (r - step) % world
+                for kc in zigzag_chunks(world, src):
+                    if kc > qc:
+                        continue  # entirely above the diagonal
+                    o, lse = attention_bhsd(qs, k[:, :, kc * C:(kc + 1) * C],
+                                            v[:, :, kc * C:(kc + 1) * C], scale, causal=True,
+                                            q_offset=qc * C, kv_offset=kc * C, return_lse=True)
+                    parts_o.append(o)
+                    parts_l.append(lse)
+            o, _ = lse_merge(np.stack(parts_o), np.stack(parts_l))
+            out[:, :, qc * C:(qc + 1) * C] = o
+    return out
+
+
+# ----------------------------------------------------------------------------------------
+# Seeded inputs (identical arrays feed the oracle and the GPU)
+# ----------------------------------------------------------------------------------------
+def make_qkv(shape_q, shape_kv, seed: int = 42, std: float = 1.0, dtype=np.float32):
+    """q, k, v ~ N(0, std^2) from numpy's legacy RandomState (stream frozen across numpy
+    versions): q from seed, k from seed + 1, v from seed + 2."""
+    q = np.random.RandomState(seed).standard_normal(shape_q).astype(np.float32) * np.float32(std)
+    k = np.random.RandomState(seed + 1).standard_normal(shape_kv).astype(np.float32) * np.float32(std)
+    v = np.random.RandomState(seed + 2).standard_normal(shape_kv).astype(np.float32) * np.float32(std)
+    return q.astype(dtype), k.astype(dtype), v.astype(dtype)
+
+
+def round_bf16(x: np.ndarray) -> np.ndarray:
+    """Round fp32 to the nearest bf16 value (ties to even), returned as fp32."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    u = x.view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)

@@ -1,0 +1,221 @@
+"""Generate tests/golden/reference_outputs.npz by running the REFERENCE's own Python code.
+
+zakkeown/mlx-primitives computes its attention with MLX (mlx >= 0.20; its benchmarks used
+0.30.3), which is not installed here and cannot be (no network).  Its attention modules only
+use a small set of mlx.core array functions on their CPU paths (full, zeros, arange, einsum,
+where, max, exp, sum, maximum, concatenate, abs, softmax, transpose, triu, matmul via @), so
+this script installs a numpy-backed stand-in for `mlx.core` with MLX's float32 defaults, loads
+the reference's modules from the reference checkout WITHOUT modification, disables its SDPA /
+Metal branches (as on an MLX build without them), and records what its own code returns:
+
+  flash.py:257-316       _tiled_flash_attention   (flash_attention BSHD, S > 512)
+  flash.py:479-525       _reference_flash_attention dense fallback (BSHD, short S)
+  flash.py:172-192       BHSD branch, dense fallback with create_causal_mask
+  sliding_window.py:363-511  _tiled_sliding_window_attention (causal and bidirectional)
+  sliding_window.py:514-560  _reference_sliding_window_attention (dense mask)
+  chunked.py:129-169     _chunked_cross_attention_impl (causal and not)
+  chunked.py:172-203     _reference_cross_attention (Skv <= chunk_size)
+  _online_softmax.py:42-176  online_softmax_merge / compute_chunk_attention
+  utils/masking.py:14-66 create_causal_mask; sliding_window.py:628-656 create_sliding_window_mask
+
+Inputs come from numpy's legacy RandomState (frozen stream) through
+oracle.attention_oracle.make_qkv, so tests regenerate them bit-for-bit from the seed; only the
+outputs (and a checksum of each input set) are stored.
+
+Run from the repository root, in a container that has the reference checkout:
+    python tests/golden/make_golden.py [--reference /path/to/mlx-primitives]
+"""
+
+from __future__ import annotations
+
+import argparse
+import hashlib
+import importlib
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parents[2]
+sys.path.insert(0, str(REPO))
+from oracle.attention_oracle import make_qkv  # noqa: E402
+
+OUT = Path(__file__).with_name("reference_outputs.npz")
+
+
+# ---------------------------------------------------------------------------------------
+# numpy stand-in for mlx.core (float32 defaults, like MLX)
+# ---------------------------------------------------------------------------------------
+def _stand_in_mlx() -> types.ModuleType:
+    mx = types.ModuleType("mlx.core")
+    f32 = np.float32
+
+    def _f(x):
+        return np.asarray(x)
+
+    def array(x, dtype=None):
+        a = np.asarray(x)
+        if dtype is not None:
+            return a.astype(dtype)
+        if a.dtype == np.float64:
+            return a.astype(f32)
+        return a
+
+    mx.array = array
+    mx.Dtype = type(np.dtype(f32))
+    mx.float32, mx.float16, mx.uint32, mx.int32 = f32, np.float16, np.uint32, np.int32
+    mx.bfloat16 = f32
+    mx.full = lambda shape, val, dtype=None: np.full(shape, val, dtype=dtype or f32)
+    mx.zeros = lambda shape, dtype=None: np.zeros(shape, dtype=dtype or f32)
+    mx.ones = lambda shape, dtype=None: np.ones(shape, dtype=dtype or f32)
+    mx.arange = lambda *a, **k: np.arange(*a, **k).astype(np.int32)
+    mx.einsum = lambda spec, *ops: np.einsum(spec, *ops).astype(np.result_type(*ops))
+    mx.where = lambda c, a, b: np.where(c, a, b).astype(np.result_type(_f(a), _f(b)))
+    mx.max = lambda x, axis=None, keepdims=False: np.max(x, axis=axis, keepdims=keepdims)
+    mx.exp = np.exp
+    mx.sum = lambda x, axis=None, keepdims=False: np.sum(x, axis=axis, keepdims=keepdims, dtype=x.dtype)
+    mx.maximum = np.maximum
+    mx.concatenate = lambda arrs, axis=0: np.concatenate(arrs, axis=axis)
+    mx.abs = np.abs
+    mx.transpose = lambda x, axes=None: np.transpose(x, axes)
+    mx.triu = lambda x, k=0: np.triu(x, k=k)
+    mx.contiguous = np.ascontiguousarray
+    mx.eval = lambda *a, **k: None
+
+    def softmax(x, axis=-1):
+        m = np.max(x, axis=axis, keepdims=True)
+        e = np.exp(x - m)
+        return e / np.sum(e, axis=axis, keepdims=True)
+
+    mx.softmax = softmax
+    # attributes the modules reference in annotations; the branches that would call them are
+    # disabled after import (module flags) and by use_metal=False.
+    fast = types.SimpleNamespace(metal_kernel=object, scaled_dot_product_attention=None)
+    mx.fast = fast
+    mx.random = types.SimpleNamespace()
+    mx.default_stream = lambda *a: None
+    mx.default_device = lambda: None
+    return mx
+
+
+def load_reference(ref_root: Path):
+    mlx = types.ModuleType("mlx")
+    core = _stand_in_mlx()
+    mlx.core = core
+    sys.modules["mlx"] = mlx
+    sys.modules["mlx.core"] = core
+    pkg_dir = ref_root / "mlx_primitives"
+    for name, sub in [("mlx_primitives", ""), ("mlx_primitives.attention", "attention"),
+                      ("mlx_primitives.kernels", "kernels"), ("mlx_primitives.utils", "utils")]:
+        m = types.ModuleType(name)
+        m.__path__ = [str(pkg_dir / sub) if sub else str(pkg_dir)]
+        sys.modules[name] = m
+    hw = types.ModuleType("mlx_primitives.hardware")
+    hw.get_chip_info = lambda *a, **k: None
+    hw.get_optimal_attention_config = lambda *a, **k: None
+    sys.modules["mlx_primitives.hardware"] = hw
+    mods = {}
+    for n in ["_online_softmax", "flash", "sliding_window", "chunked"]:
+        mods[n] = importlib.import_module(f"mlx_primitives.attention.{n}")
+    mods["masking"] = importlib.import_module("mlx_primitives.utils.masking")
+    for n in ["flash", "sliding_window", "chunked"]:
+        setattr(mods[n], "_HAS_SDPA", False)
+        setattr(mods[n], "_HAS_METAL", False)
+    return mods
+
+
+def digest(*arrs) -> str:
+    h = hashlib.sha256()
+    for a in arrs:
+        h.update(np.ascontiguousarray(a, dtype=np.float32).tobytes())
+    return h.hexdigest()[:16]
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    args = ap.parse_args()
+    mods = load_reference(Path(args.reference))
+    fl, sw, ch, osm, mk = (mods[n] for n in ["flash", "sliding_window", "chunked", "_online_softmax", "masking"])
+    out = {}
+
+    def case(name, seed, shape_q, shape_kv, fn, std=1.0):
+        q, k, v = make_qkv(shape_q, shape_kv, seed=seed, std=std)
+        res = np.asarray(fn(q, k, v), dtype=np.float32)
+        out[f"{name}__out"] = res
+        out[f"{name}__meta"] = np.array([seed, std] + list(shape_q) + list(shape_kv), dtype=np.float64)
+        out[f"{name}__digest"] = np.array(digest(q, k, v))
+        print(f"{name:34s} q{shape_q} kv{shape_kv} -> {res.shape}")
+
+    # flash_attention, BSHD, tiled path (S > 512): flash.py:257-316
+    case("flash_bshd_tiled_causal_d64", 101, (1, 520, 2, 64), (1, 520, 2, 64),
+         lambda q, k, v: fl.flash_attention(q, k, v, causal=True, use_metal=False))
+    case("flash_bshd_tiled_noncausal_d64", 102, (1, 530, 1, 64), (1, 530, 1, 64),
+         lambda q, k, v: fl.flash_attention(q, k, v, causal=False, use_metal=False))
+    case("flash_bshd_tiled_causal_d128_b16", 103, (1, 600, 1, 128), (1, 600, 1, 128),
+         lambda q, k, v: fl.flash_attention(q, k, v, causal=True, block_q=16, block_kv=16,
+                                            use_metal=False))
+    case("flash_bshd_tiled_causal_d32_ragged", 104, (6, 300, 1, 32), (6, 300, 1, 32),
+         lambda q, k, v: fl.flash_attention(q, k, v, causal=True, use_metal=False))
+    # flash_attention, BSHD, dense reference path (short S): flash.py:479-525
+    case("flash_bshd_dense_causal_d64", 105, (2, 64, 3, 64), (2, 64, 3, 64),
+         lambda q, k, v: fl.flash_attention(q, k, v, causal=True, use_metal=False))
+    case("flash_bshd_dense_scale_d64", 106, (1, 100, 2, 64), (1, 100, 2, 64),
+         lambda q, k, v: fl.flash_attention(q, k, v, scale=0.3, causal=False, use_metal=False))
+    case("flash_bshd_single_token", 107, (1, 1, 1, 64), (1, 1, 1, 64),
+         lambda q, k, v: fl.flash_attention(q, k, v, causal=True, use_metal=False))
+    case("flash_bshd_large_values", 108, (1, 130, 1, 64), (1, 130, 1, 64),
+         lambda q, k, v: fl.flash_attention(q, k, v, causal=True, use_metal=False), std=10.0)
+    # flash_attention, BHSD branch (dense fallback with create_causal_mask): flash.py:172-192
+    case("flash_bhsd_causal_d128", 109, (2, 2, 200, 128), (2, 2, 200, 128),
+         lambda q, k, v: fl.flash_attention(q, k, v, causal=True, use_metal=False, layout="BHSD"))
+    case("flash_bhsd_noncausal_d64", 110, (1, 3, 150, 64), (1, 3, 150, 64),
+         lambda q, k, v: fl.flash_attention(q, k, v, causal=False, use_metal=False, layout="BHSD"))
+    # sliding window: sliding_window.py:363-511 (tiled) and 514-560 (dense)
+    case("swa_tiled_causal_w37", 111, (1, 300, 2, 64), (1, 300, 2, 64),
+         lambda q, k, v: sw.sliding_window_attention(q, k, v, window_size=37, causal=True, use_metal=False))
+    case("swa_tiled_bidir_w20", 112, (1, 200, 1, 64), (1, 200, 1, 64),
+         lambda q, k, v: sw.sliding_window_attention(q, k, v, window_size=20, causal=False, use_metal=False))
+    case("swa_tiled_causal_w130_d128", 113, (1, 400, 1, 128), (1, 400, 1, 128),
+         lambda q, k, v: sw.sliding_window_attention(q, k, v, window_size=130, causal=True, use_metal=False))
+    case("swa_dense_causal_w5", 114, (1, 40, 1, 64), (1, 40, 1, 64),
+         lambda q, k, v: sw._reference_sliding_window_attention(q, k, v, 5, 0.125, True))
+    # chunked cross attention: chunked.py:129-169 and 172-203
+    case("chunked_loop_noncausal", 115, (2, 50, 2, 64), (2, 700, 2, 64),
+         lambda q, k, v: ch.chunked_cross_attention(q, k, v, chunk_size=128, use_metal=False),
+         std=0.5)
+    case("chunked_loop_causal", 116, (1, 300, 1, 64), (1, 300, 1, 64),
+         lambda q, k, v: ch.chunked_cross_attention(q, k, v, chunk_size=64, causal=True, use_metal=False))
+    case("chunked_loop_q_longer_causal", 117, (1, 260, 1, 64), (1, 200, 1, 64),
+         lambda q, k, v: ch.chunked_cross_attention(q, k, v, chunk_size=64, causal=True, use_metal=False))
+    case("chunked_dense_short_kv", 118, (1, 30, 2, 128), (1, 100, 2, 128),
+         lambda q, k, v: ch.chunked_cross_attention(q, k, v, chunk_size=1024, use_metal=False))
+
+    # _online_softmax: merge and chunk helpers
+    q, k, v = make_qkv((1, 16, 2, 64), (1, 48, 2, 64), seed=119)
+    o1, m1, l1 = osm.compute_chunk_attention(q, k[:, :24], v[:, :24], 0.125, causal=True,
+                                             q_offset=30, kv_offset=0)
+    o2, m2, l2 = osm.compute_chunk_attention(q, k[:, 24:], v[:, 24:], 0.125, causal=True,
+                                             q_offset=30, kv_offset=24)
+    om, mm, lm = osm.online_softmax_merge(o1, m1, l1, o2, m2, l2)
+    for nm, a in dict(o1=o1, m1=m1, l1=l1, o2=o2, m2=m2, l2=l2, om=om, mm=mm, lm=lm).items():
+        out[f"merge__{nm}"] = np.asarray(a, dtype=np.float32)
+    out["merge__digest"] = np.array(digest(q, k, v))
+
+    # masks
+    out["mask__causal_4x7"] = np.asarray(mk.create_causal_mask(4, 7), dtype=np.float32)
+    out["mask__causal_5x5"] = np.asarray(mk.create_causal_mask(5, 5), dtype=np.float32)
+    out["mask__window_causal_8_2"] = np.asarray(sw.create_sliding_window_mask(8, 2, causal=True))
+    out["mask__window_bidir_8_2"] = np.asarray(sw.create_sliding_window_mask(8, 2, causal=False))
+    out["api__flash_config"] = np.array([fl.get_optimal_flash_config(s, d, 8)
+                                         for s in (4, 64, 4096) for d in (32, 64, 128, 256)])
+    out["api__memory_savings"] = np.array(ch.estimate_memory_savings(512, 65536, 16, 64, 4096),
+                                          dtype=np.float64)
+
+    np.savez_compressed(OUT, **out)
+    print(f"wrote {OUT} ({OUT.stat().st_size / 1e6:.2f} MB)")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,134 @@
+"""CPU-only checks of the boundary: libmlxp_attn.so loads and exports every entry point
+include/mlxp_attn.h declares (no compute call — there is no GPU here), and the Python API
+validates its arguments exactly like the reference before touching the device."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+REPO = Path(__file__).resolve().parents[1]
+HEADER = REPO / "include" / "mlxp_attn.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(mlxp_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_boundary():
+    names = declared_functions()
+    for required in ("mlxp_attn_fwd", "mlxp_attn_workspace_size", "mlxp_attn_fwd_partial",
+                     "mlxp_lse_merge", "mlxp_last_error", "mlxp_version"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol():
+    from mlx_primitives import _lib
+
+    L = _lib.lib()
+    for name in declared_functions():
+        assert hasattr(L, name), f"{name} declared in mlxp_attn.h but not exported"
+    assert set(declared_functions()) == set(_lib.EXPORTED_SYMBOLS)
+
+
+def test_version_and_error_string_need_no_gpu():
+    from mlx_primitives import _lib
+
+    L = _lib.lib()
+    assert L.mlxp_version() == 100
+    assert isinstance(L.mlxp_last_error(), bytes)
+
+
+def test_workspace_size_is_zero_without_split():
+    from mlx_primitives import _lib
+
+    L = _lib.lib()
+    # kv_splits = 1: no workspace.  Pure host arithmetic, no device call.
+    assert L.mlxp_attn_workspace_size(1, 4, 32, 4096, 4096, 128, 1, -1, -1, 0, 0, 1) == 0
+    # explicit split: fp32 partial O + LSE for each split
+    n = L.mlxp_attn_workspace_size(1, 8, 16, 512, 65536, 64, 0, -1, -1, 0, 0, 4)
+    rows = 4 * 8 * 16 * 512
+    assert n >= rows * 64 * 4 + rows * 4
+
+
+def test_invalid_arguments_are_rejected_before_any_launch():
+    from mlx_primitives import _lib
+
+    L = _lib.lib()
+    st = (ctypes.c_int64 * 4)(0, 0, 0, 1)
+    # unsupported head_dim on the tensor-core path
+    rc = L.mlxp_attn_fwd(16, 16, 16, 16, None, 1, 1, 1, 8, 8, 96, st, st, st, st,
+                         ctypes.c_float(0.1), 1, -1, -1, 0, 0, 1, None, 0, None)
+    assert rc == _lib.MLXP_ERR_UNSUPPORTED and b"head_dim" in L.mlxp_last_error()
+    # non-positive scale
+    rc = L.mlxp_attn_fwd(16, 16, 16, 16, None, 1, 1, 1, 8, 8, 64, st, st, st, st,
+                         ctypes.c_float(-1.0), 1, -1, -1, 0, 0, 1, None, 0, None)
+    assert rc == _lib.MLXP_ERR_INVALID
+    # null pointers
+    rc = L.mlxp_attn_fwd(None, None, None, None, None, 1, 1, 1, 8, 8, 64, st, st, st, st,
+                         ctypes.c_float(0.1), 1, -1, -1, 0, 0, 1, None, 0, None)
+    assert rc == _lib.MLXP_ERR_INVALID
+
+
+# ---- API validation mirrors flash.py:123-169 (raised before any device work) ----
+def _t(*shape, dtype=torch.float32):
+    return torch.zeros(shape, dtype=dtype)
+
+
+def test_flash_validation_errors():
+    import mlx_primitives as mp
+
+    with pytest.raises(ValueError, match="Expected 4D"):
+        mp.flash_attention(_t(2, 3, 4), _t(2, 3, 4, 8), _t(2, 3, 4, 8))
+    with pytest.raises(ValueError, match="layout must be"):
+        mp.flash_attention(_t(1, 4, 2, 8), _t(1, 4, 2, 8), _t(1, 4, 2, 8), layout="SBHD")
+    with pytest.raises(ValueError, match="Batch size mismatch"):
+        mp.flash_attention(_t(1, 4, 2, 8), _t(2, 4, 2, 8), _t(1, 4, 2, 8))
+    with pytest.raises(ValueError, match="Number of heads mismatch"):
+        mp.flash_attention(_t(1, 4, 2, 8), _t(1, 4, 3, 8), _t(1, 4, 2, 8))
+    with pytest.raises(ValueError, match="Head dimension mismatch"):
+        mp.flash_attention(_t(1, 4, 2, 8), _t(1, 4, 2, 16), _t(1, 4, 2, 8))
+    with pytest.raises(ValueError, match="Sequence length mismatch"):
+        mp.flash_attention(_t(1, 4, 2, 8), _t(1, 4, 2, 8), _t(1, 5, 2, 8))
+    with pytest.raises(ValueError, match="dtype mismatch"):
+        mp.flash_attention(_t(1, 4, 2, 8), _t(1, 4, 2, 8, dtype=torch.bfloat16), _t(1, 4, 2, 8))
+    with pytest.raises(NotImplementedError, match="dropout"):
+        mp.flash_attention(_t(1, 4, 2, 8), _t(1, 4, 2, 8), _t(1, 4, 2, 8), dropout_p=0.1)
+
+
+def test_other_entry_points_validate():
+    import mlx_primitives as mp
+
+    with pytest.raises(ValueError, match="Expected 4D"):
+        mp.sliding_window_attention(_t(4, 2, 8), _t(1, 4, 2, 8), _t(1, 4, 2, 8), window_size=2)
+    with pytest.raises(ValueError, match="window_size"):
+        mp.sliding_window_attention(_t(1, 4, 2, 8), _t(1, 4, 2, 8), _t(1, 4, 2, 8), window_size=-1)
+    with pytest.raises(ValueError, match="chunk_size"):
+        mp.chunked_cross_attention(_t(1, 4, 2, 8), _t(1, 9, 2, 8), _t(1, 9, 2, 8), chunk_size=0)
+    with pytest.raises(ValueError, match="dtype mismatch"):
+        mp.chunked_cross_attention(_t(1, 4, 2, 8), _t(1, 9, 2, 8, dtype=torch.float16), _t(1, 9, 2, 8))
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-GPU error")
+def test_no_cpu_fallback():
+    import mlx_primitives as mp
+
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        mp.flash_attention(_t(1, 4, 2, 64), _t(1, 4, 2, 64), _t(1, 4, 2, 64))
+
+
+def test_modules_store_reference_attributes():
+    import mlx_primitives as mp
+
+    fa = mp.FlashAttention(num_heads=8, head_dim=64)
+    assert (fa.causal, fa.block_q, fa.block_kv, fa.scale) == (True, 32, 32, 0.125)
+    assert mp.FlashAttention(8, 128).block_q == 16
+    sw = mp.SlidingWindowAttention(8, 64, 128)
+    assert (sw.window_size, sw.causal, sw.scale) == (128, True, 0.125)
+    ca = mp.ChunkedCrossAttention(8, 64)
+    assert (ca.chunk_size, ca.causal) == (1024, False)
+    assert mp.Layout("BSHD") == "BSHD" and mp.Layout.BHSD == "BHSD"
