@@ -316,21 +316,24 @@ def main():
     achieved = flops / (ms_local * 1e-3) / 1e12  # this rank's work per step / its step time
 
     # ---- e2e: public API with pinned host tensors (H2D and D2H inside the timed region)
-    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
-    step(hq, hk, hv)
-    torch.cuda.synchronize(dev)
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.e2e_steps):
-        out_host = step(hq, hk, hv)
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    barrier()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.e2e_steps)
-    e2e_value = world * flops / (e2e_ms * 1e-3) / 1e12
-    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
-    d2h = out_host.numel() * out_host.element_size()
+    e2e = None
+    if args.e2e_steps > 0:
+        hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+        step(hq, hk, hv)
+        torch.cuda.synchronize(dev)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.e2e_steps):
+            out_host = step(hq, hk, hv)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.e2e_steps)
+        e2e = {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS",
+               "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in (hq, hk, hv)),
+               "d2h_bytes_per_step": out_host.numel() * out_host.element_size(),
+               "ms_per_step": e2e_ms}
 
     line = None
     if rank == 0:
@@ -351,12 +354,11 @@ def main():
                 "algorithmic_flops_per_launch": flops,
                 "hbm_gbs_at_min_bytes": config_bytes(c) / (ms_local * 1e-3) / 1e9,
             },
-            "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+            "e2e": e2e,
             "gpu_launches": args.steps * launches_per_step,
             "clocks": clocks.summary(),
         }
-        if world == 1:
+        if world == 1 and args.cpu_budget > 0:
             tf, units, secs, threads = cpu_oracle_tflops(c, budget_s=args.cpu_budget)
             line["cpu_baseline"] = {
                 "value": tf, "unit": "TFLOPS", "cores": threads, "kind": "port",

@@ -57,7 +57,13 @@ struct Sm100Cfg {
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16;
   static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024 B
-  static constexpr int THREADS = 320;
+  // Three warpgroups: WG0/WG1 softmax (tiles 0/1), WG2 = MMA warp, TMA warp, two spare warps.
+  // Registers are split per SM sub-partition, so the launch gets 65536/384 -> 168 per thread
+  // and setmaxnreg moves them to the softmax warpgroups: 2*128*208 + 128*80 = 63488 <= 384*168.
+  static constexpr int THREADS = 384;
+  static constexpr int REGS_SOFTMAX = 208;
+  static constexpr int REGS_CONTROL = 80;
+  static_assert(2 * 128 * REGS_SOFTMAX + 128 * REGS_CONTROL <= THREADS * 168, "register split");
   static constexpr uint32_t TM_S0 = 0, TM_S1 = 128, TM_O0 = 256, TM_O1 = 256 + D;
   static constexpr uint32_t TM_COLS = 512;
   static_assert(D == 64 || D == 128, "head_dim 64 or 128");
@@ -95,7 +101,7 @@ __device__ __forceinline__ void tma_coords(const TmaCoordMap& cm, int s, int h, 
 }
 
 template <int D, bool kBF16, int NSK, int NSV>
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(384, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                           const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
@@ -178,8 +184,10 @@ __global__ void __maxnreg__(200)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const WaitCtx wctx{abort_flag, p.status, p.timeout_ns};
-
-  if (warp == 9) {
+  if (warp >= 8) {
+    // ================================ control warpgroup ================================
+    setmaxnreg_dec<C::REGS_CONTROL>();
+    if (warp == 9) {
     // =================================== TMA producer ===================================
     if (lane == 0 && n_tiles > 0) {
       tma_prefetch_desc(&tm_q);
@@ -317,8 +325,18 @@ __global__ void __maxnreg__(200)
       tc_commit(BAR(C::B_DR));
       mbar_wait_drain(BAR(C::B_DR), 0, p.status, p.timeout_ns);
     }
+    }  // warps 10-11: spare
+    // ---- teardown: every role is done with TMEM and smem after this barrier
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 8) {
+      tc_fence_after();
+      tmem_dealloc(tmem, C::TM_COLS);
+    }
   } else {
     // ============================== softmax + epilogue (tile t) ==============================
+    setmaxnreg_inc<C::REGS_SOFTMAX>();
     const int t = warp >> 2;
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
@@ -380,8 +398,35 @@ __global__ void __maxnreg__(200)
         alpha = ex2_approx(m - m_new);
         m = m_new;
       }
+      const float neg_mu = (m == -INFINITY) ? 0.f : -m;
+      float rs0 = 0.f, rs1 = 0.f;
+      {
+        uint32_t pk[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const float a0 = ex2_approx(fmaf(s[2 * c], sl2, neg_mu));
+          const float a1 = ex2_approx(fmaf(s[2 * c + 1], sl2, neg_mu));
+          rs0 += a0;
+          rs1 += a1;
+          pk[c] = pack2<kBF16>(a0, a1);
+        }
+        tmem_st_x32(tS + 0, pk);
+      }
+      {
+        uint32_t pk[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const float a0 = ex2_approx(fmaf(s[64 + 2 * c], sl2, neg_mu));
+          const float a1 = ex2_approx(fmaf(s[64 + 2 * c + 1], sl2, neg_mu));
+          rs0 += a0;
+          rs1 += a1;
+          pk[c] = pack2<kBF16>(a0, a1);
+        }
+        tmem_st_x32(tS + 32, pk);
+      }
       if (it > 0 && __any_sync(0xffffffffu, resc)) {
-        // O_t holds PV_t(j-1) (complete: it was issued before QK_t(j), whose commit we saw).
+        // O_t holds PV_t(j-1) (complete: it was issued before QK_t(j), whose commit we saw);
+        // PV_t(j) is not issued before the arrive below, so it sees the rescaled O.
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
           uint32_t ov[32];
@@ -393,27 +438,6 @@ __global__ void __maxnreg__(200)
           tmem_st_x32(tO + c * 32, ov);
         }
       }
-      const float neg_mu = (m == -INFINITY) ? 0.f : -m;
-      float rs0 = 0.f, rs1 = 0.f;
-      uint32_t pk0[32], pk1[32];
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const float a0 = ex2_approx(fmaf(s[2 * c], sl2, neg_mu));
-        const float a1 = ex2_approx(fmaf(s[2 * c + 1], sl2, neg_mu));
-        rs0 += a0;
-        rs1 += a1;
-        pk0[c] = pack2<kBF16>(a0, a1);
-      }
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const float a0 = ex2_approx(fmaf(s[64 + 2 * c], sl2, neg_mu));
-        const float a1 = ex2_approx(fmaf(s[64 + 2 * c + 1], sl2, neg_mu));
-        rs0 += a0;
-        rs1 += a1;
-        pk1[c] = pack2<kBF16>(a0, a1);
-      }
-      tmem_st_x32(tS + 0, pk0);
-      tmem_st_x32(tS + 32, pk1);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(BAR(C::B_PF + t));
@@ -475,15 +499,8 @@ __global__ void __maxnreg__(200)
         }
       }
     }
-  }
-
-  // ---------------------------------- teardown ----------------------------------
-  __syncwarp();
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 8) {
-    tc_fence_after();
-    tmem_dealloc(tmem, C::TM_COLS);
+    tc_fence_before();
+    __syncthreads();  // teardown barrier (pairs with the control warpgroup's)
   }
 }
 

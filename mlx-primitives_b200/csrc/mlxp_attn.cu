@@ -266,7 +266,15 @@ struct TcKernel {
     if (grid <= 0) return MLXP_OK;
     kern<<<(unsigned)grid, Cfg::THREADS, Cfg::SMEM_ALLOC, stream>>>(mq, mk, mv, p);
     cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_fail(e, "attn_fwd_sm100 launch");
+    if (e != cudaSuccess) {
+      cudaFuncAttributes fa{};
+      cudaFuncGetAttributes(&fa, kern);
+      return fail(MLXP_ERR_CUDA,
+                  "attn_fwd_sm100 launch: %s (regs/thread %d, max threads/block %d, dynamic smem "
+                  "%d of max %d, threads %d, grid %lld)",
+                  cudaGetErrorString(e), fa.numRegs, fa.maxThreadsPerBlock, Cfg::SMEM_ALLOC,
+                  fa.maxDynamicSharedSizeBytes, Cfg::THREADS, grid);
+    }
     return MLXP_OK;
   }
 };
@@ -345,7 +353,9 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
   if (int rc = validate(pr)) return rc;
   if (!(scale > 0.f) || !std::isfinite(scale))
     return fail(MLXP_ERR_INVALID, "scale must be positive and finite");
-  if (!q || !k || !v) return fail(MLXP_ERR_INVALID, "q, k and v must be non-null");
+  // Empty tensors may have null data pointers: q only matters when Sq > 0, k/v when Skv > 0.
+  if ((pr.Sq > 0 && !q) || (pr.Skv > 0 && (!k || !v)))
+    return fail(MLXP_ERR_INVALID, "q, k and v must be non-null");
   if (!qs || !ks || !vs || !os) return fail(MLXP_ERR_INVALID, "stride arrays must be non-null");
   if (out_f32 && lse == nullptr) return fail(MLXP_ERR_INVALID, "partial output needs lse");
   const bool fp32 = pr.dtype == MLXP_DTYPE_FP32;

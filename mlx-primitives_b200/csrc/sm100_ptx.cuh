@@ -73,8 +73,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // the CTA's abort flag is up or when this wait exceeded the limit; in the latter case it raises
 // the abort flag and records (site << 8 | kDevTimeout) in the device status word.  Besides the
 // time limit a hard cap on the number of polls keeps the loop finite even if the global timer
-// were not advancing.
-__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, WaitCtx w, int site) {
+// were not advancing.  Inlined on purpose: kernels that rebalance registers with setmaxnreg
+// cannot call an out-of-line function from regions of different register budgets.
+__device__ __forceinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, WaitCtx w, int site) {
   const uint64_t t0 = global_timer_ns();
   for (uint32_t it = 1; it < (1u << 28); ++it) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -245,6 +246,16 @@ __device__ __forceinline__ void reg_fence(uint32_t (&r)[32]) {
                  "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
                :
                : "memory");
+}
+
+// Per-warpgroup register rebalancing (every warp of the warpgroup executes the same one).
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // ------------------------------------------------------------------------------------------

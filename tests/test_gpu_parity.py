@@ -105,7 +105,8 @@ def test_tc_position_offsets(q_off, kv_off):
     got_lse = lse.cpu().numpy()
     finite = np.isfinite(want_lse)
     assert np.array_equal(np.isfinite(got_lse), finite)
-    assert np.max(np.abs(got_lse[finite] - want_lse[finite])) < 1e-2
+    if finite.any():
+        assert np.max(np.abs(got_lse[finite] - want_lse[finite])) < 1e-2
 
 
 @pytest.mark.parametrize("splits", [1, 2, 3, 7, 0])
