@@ -109,6 +109,7 @@ struct FwdParams {
   int splits;           // >= 1 key-range splits
   int tiles_per_split;  // key tiles per split (splits > 1)
   int heavy_first;      // order query blocks by descending work (causal)
+  int group_bh;         // (batch, head) units per scheduling group (see decode_item)
   // output: normal (dtype, normalised) or fp32 (normalised, for merges)
   int out_f32;
   void* o;
@@ -120,6 +121,9 @@ struct FwdParams {
   TmaCoordMap cq, ck, cv;
   int* status;
   unsigned long long timeout_ns;
+  // Persistent scheduling: [next item, CTAs finished].  Zero at launch; the last CTA to finish
+  // resets both, so consecutive launches on one stream can reuse the pair.
+  unsigned* work_counter;
 };
 
 // Parameters of the CUDA-core fp32 kernel (plain pointers and strides).

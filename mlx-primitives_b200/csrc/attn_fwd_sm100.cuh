@@ -1,9 +1,14 @@
 // attn_fwd_sm100.cuh — bf16/fp16 attention forward on the 5th-generation tensor cores (sm_100a).
 //
-// One CTA computes 256 query rows (two 128-row Q tiles, "tile 0" and "tile 1") of one
-// (batch, head) against a range of 128-key K/V tiles:
+// Persistent kernel: one CTA per SM pulls work items from a device-wide counter.  A work item
+// is 256 query rows (two 128-row Q tiles, "tile 0" and "tile 1") of one (batch, head), against
+// a range of 128-key K/V tiles (optionally one of several key splits).  Items are numbered in
+// groups of (batch, head) units so that the CTAs running at the same time share K/V through
+// L2, heaviest query blocks of a group first when the mask is causal (see decode_item).
 //
-//   warp 9        TMA producer: Q once, then K and V tiles into two smem rings (128B swizzle).
+//   warp 9        TMA producer: fetches items, then loads Q once per item and K, V tiles into
+//                 two shared-memory rings (128-byte swizzle).  The rings, barriers and TMEM
+//                 persist across items, so the next item's loads overlap the current one.
 //   warp 8        MMA issuer (one thread): S_t = Q_t K^T (SS form, fp32 accumulate in TMEM),
 //                 then O_t += P_t V (TS form: P_t read from TMEM, V from smem).
 //   warps 0-3     softmax for tile 0, warps 4-7 softmax for tile 1: one thread owns one query
@@ -11,7 +16,9 @@
 //                 updates the running max/sum, writes P (bf16/fp16, packed two per 32-bit
 //                 column) back over the S columns with tcgen05.st, and rescales O in TMEM only
 //                 when the running max grew by more than 2^8 (exact: the final 1/l uses the
-//                 same stale max as the exponentials).  The same warps run the epilogue.
+//                 same stale max as the exponentials).  The same warps run the epilogue, which
+//                 overlaps the tensor core's first QK of the next item.
+//   warps 10-11   spare (the control warpgroup is register-starved by design).
 //
 // TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D); P_t aliases
 // the first 64 columns of S_t.  The two tiles ping-pong: while softmax works on S_0 the tensor
@@ -19,16 +26,40 @@
 // tcgen05.mma instructions from one thread execute in order, so QK_t(j+1) may overwrite the
 // S/P columns right after PV_t(j) is issued, and the commit after QK_t(j+1) also certifies that
 // PV_t(j) finished — which is what lets the softmax warps rescale O without another barrier.
+// Across items the same order holds (PV_t(last of i) before QK_t(first of i+1)), and the first
+// PV_t of item i+1 (which overwrites O_t) waits for P_t, which the softmax warps publish only
+// after their epilogue of item i has read O_t.
 //
 // Every wait is bounded (mbar_wait); when one gives up the CTA drains its in-flight TMA
 // loads and MMAs (bounded again), frees TMEM and returns, leaving the error in the device
 // status word.
 #pragma once
 
+#include <type_traits>
+
 #include "attn_common.cuh"
 #include "sm100_ptx.cuh"
 
 namespace mlxp {
+
+// Cycle-counter trace of CTA 0 for pipeline analysis: compiled in only with -DMLXP_TRACE=1
+// (roles 0/1 softmax tiles, 2 MMA issuer, 3 TMA producer; 64 iterations x 8 stamps each).
+#ifndef MLXP_TRACE
+#define MLXP_TRACE 0
+#endif
+#if MLXP_TRACE
+__device__ long long g_mlxp_trace[4 * 64 * 8];
+__device__ long long g_mlxp_cta_trace[8192 * 4];  // per item: start ns, end ns, SM id, key tiles
+#define MLXP_TR(cond, role, it, k)                                                    \
+  do {                                                                                \
+    if ((cond) && blockIdx.x == 0 && (it) < 64)                                       \
+      g_mlxp_trace[((role) * 64 + (it)) * 8 + (k)] = clock64();                       \
+  } while (0)
+#else
+#define MLXP_TR(cond, role, it, k) \
+  do {                             \
+  } while (0)
+#endif
 
 template <int D, int NSK, int NSV>
 struct Sm100Cfg {
@@ -44,17 +75,20 @@ struct Sm100Cfg {
   static constexpr int OFF_V = OFF_K + NSK * KV_TILE;
   static constexpr int OFF_BAR = OFF_V + NSV * KV_TILE;
   // barrier indices
-  static constexpr int B_Q = 0;
-  static constexpr int B_KF = 1;
+  static constexpr int B_QF = 0;           // Q loaded
+  static constexpr int B_QE = 1;           // Q buffer free (last QK of the item done)
+  static constexpr int B_KF = 2;
   static constexpr int B_KE = B_KF + NSK;
   static constexpr int B_VF = B_KE + NSK;
   static constexpr int B_VE = B_VF + NSV;
   static constexpr int B_SF = B_VE + NSV;  // 2: S_t ready
   static constexpr int B_PF = B_SF + 2;    // 2: P_t ready (128 arrivals)
-  static constexpr int B_OF = B_PF + 2;    // 2: final PV_t complete
-  static constexpr int B_DR = B_OF + 2;    // 1: MMA drain
+  static constexpr int B_OF = B_PF + 2;    // 2: last PV_t of an item complete
+  static constexpr int B_WF = B_OF + 2;    // 2: work-item slot filled
+  static constexpr int B_WE = B_WF + 2;    // 2: work-item slot read by every consumer
+  static constexpr int B_DR = B_WE + 2;    // 1: MMA drain
   static constexpr int NBAR = B_DR + 1;
-  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;  // tmem slot, abort flag, 2 item slots
   static constexpr int SMEM_BYTES = OFF_MISC + 16;
   static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024 B
   // Three warpgroups: WG0/WG1 softmax (tiles 0/1), WG2 = MMA warp, TMA warp, two spare warps.
@@ -64,6 +98,8 @@ struct Sm100Cfg {
   static constexpr int REGS_SOFTMAX = 208;
   static constexpr int REGS_CONTROL = 80;
   static_assert(2 * 128 * REGS_SOFTMAX + 128 * REGS_CONTROL <= THREADS * 168, "register split");
+  // consumers of a work-item slot: the MMA thread and the 256 softmax threads
+  static constexpr int WORK_READERS = 1 + 256;
   static constexpr uint32_t TM_S0 = 0, TM_S1 = 128, TM_O0 = 256, TM_O1 = 256 + D;
   static constexpr uint32_t TM_COLS = 512;
   static_assert(D == 64 || D == 128, "head_dim 64 or 128");
@@ -78,8 +114,21 @@ enum : int {
   kSiteSoftmaxS = 4,
   kSiteSoftmaxO = 5,
   kSiteDrain = 6,
-  kSiteSelfTest = 7
+  kSiteSelfTest = 7,
+  kSiteWork = 8
 };
+
+// Of every 8 column pairs of a score row, this many are exponentiated with exp2_poly2 (FMA pipe)
+// and the rest with ex2.approx (MUFU): splits the per-row exp2 work between the two units.
+// head_dim 64 has half the MMA work per score, so more of its exponentials go to the FMA pipe.
+#ifndef MLXP_POLY_D64
+#define MLXP_POLY_D64 3
+#endif
+#ifndef MLXP_POLY_D128
+#define MLXP_POLY_D128 2
+#endif
+template <int D>
+constexpr int kPolyPerOct = (D == 64) ? MLXP_POLY_D64 : MLXP_POLY_D128;
 
 // Wait without looking at the abort flag (used when draining after an abort).
 __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, int* status,
@@ -100,6 +149,56 @@ __device__ __forceinline__ void tma_coords(const TmaCoordMap& cm, int s, int h, 
   c3 = (cm.slot_s == 3) ? s : (cm.slot_h == 3) ? hh : bb;
 }
 
+// One work item, decoded identically by every role from its index.
+struct WorkItem {
+  int b, h, split, q0;
+  int lo0, hi0, lo1, hi1;  // key-tile ranges of Q tiles 0 and 1 (empty: lo == hi)
+  int lo, hi;              // union range
+};
+
+// Item order: (batch, head) units are taken in groups of p.group_bh; inside a group the query
+// blocks go heaviest first across the whole group (longest-processing-time order), then the
+// next group.  A group's K/V stays L2-resident while its items run, and the last items of the
+// launch are the lightest ones, which keeps the tail short.
+__device__ __forceinline__ WorkItem decode_item(const FwdParams& p, int idx, int BN) {
+  WorkItem w;
+  const int BH = p.B * p.H;
+  const int per_unit = p.n_qblk * p.splits;
+  const int grp = idx / (p.group_bh * per_unit);
+  const int g0 = grp * p.group_bh;
+  const int gsize = min(p.group_bh, BH - g0);
+  const int local = idx - g0 * per_unit;
+  const int qrank = local / (gsize * p.splits);
+  const int rem = local - qrank * gsize * p.splits;
+  const int bh = g0 + rem / p.splits;
+  w.split = rem % p.splits;
+  const int qb = p.heavy_first ? p.n_qblk - 1 - qrank : qrank;
+  w.h = bh % p.H;
+  w.b = bh / p.H;
+  w.q0 = qb * 256;
+  int lo_t[2], hi_t[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const long long r0 = w.q0 + t * 128;
+    const long long r1 = (r0 + 128 < p.Sq) ? r0 + 128 : p.Sq;
+    kv_tile_range(p.mask, r0, r1, BN, lo_t[t], hi_t[t]);
+    if (p.splits > 1) {
+      const int s_lo = w.split * p.tiles_per_split, s_hi = s_lo + p.tiles_per_split;
+      if (lo_t[t] < s_lo) lo_t[t] = s_lo;
+      if (hi_t[t] > s_hi) hi_t[t] = s_hi;
+      if (hi_t[t] < lo_t[t]) hi_t[t] = lo_t[t];
+    }
+  }
+  w.lo0 = lo_t[0];
+  w.hi0 = hi_t[0];
+  w.lo1 = lo_t[1];
+  w.hi1 = hi_t[1];
+  const bool a0 = w.hi0 > w.lo0, a1 = w.hi1 > w.lo1;
+  w.lo = (a0 && a1) ? min(w.lo0, w.lo1) : a0 ? w.lo0 : a1 ? w.lo1 : 0;
+  w.hi = (a0 && a1) ? max(w.hi0, w.hi1) : a0 ? w.hi0 : a1 ? w.hi1 : 0;
+  return w;
+}
+
 template <int D, bool kBF16, int NSK, int NSV>
 __global__ void __launch_bounds__(384, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -112,52 +211,16 @@ __global__ void __launch_bounds__(384, 1)
   const uint32_t sbase = smem_u32(smem);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   int* abort_flag = reinterpret_cast<int*>(smem + C::OFF_MISC + 4);
+  volatile int* work_slot = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8);
   auto BAR = [&](int i) -> uint32_t { return sbase + C::OFF_BAR + 8 * i; };
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-
-  // ---- work item: (b, h) major so that CTAs sharing K/V run together (L2 reuse); within a
-  // (b, h), the heaviest query block first when the mask is causal.
-  const int per_bh = p.n_qblk * p.splits;
-  const int bh = blockIdx.x / per_bh;
-  const int rem = blockIdx.x - bh * per_bh;
-  const int split = rem % p.splits;
-  int qb = rem / p.splits;
-  if (p.heavy_first) qb = p.n_qblk - 1 - qb;
-  const int h = bh % p.H;
-  const int b = bh / p.H;
-  const int q0 = qb * 256;
-
-  int lo_t[2], hi_t[2];
-#pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    const long long r0 = q0 + t * 128;
-    const long long r1 = (r0 + 128 < p.Sq) ? r0 + 128 : p.Sq;
-    kv_tile_range(p.mask, r0, r1, C::BN, lo_t[t], hi_t[t]);
-    if (p.splits > 1) {
-      const int s_lo = split * p.tiles_per_split, s_hi = s_lo + p.tiles_per_split;
-      if (lo_t[t] < s_lo) lo_t[t] = s_lo;
-      if (hi_t[t] > s_hi) hi_t[t] = s_hi;
-      if (hi_t[t] < lo_t[t]) hi_t[t] = lo_t[t];
-    }
-  }
-  const bool act0 = hi_t[0] > lo_t[0], act1 = hi_t[1] > lo_t[1];
-  int lo = 0, hi = 0;
-  if (act0 && act1) {
-    lo = min(lo_t[0], lo_t[1]);
-    hi = max(hi_t[0], hi_t[1]);
-  } else if (act0) {
-    lo = lo_t[0];
-    hi = hi_t[0];
-  } else if (act1) {
-    lo = lo_t[1];
-    hi = hi_t[1];
-  }
-  const int n_tiles = hi - lo;
+  const int n_items = p.n_qblk * p.B * p.H * p.splits;
 
   if (threadIdx.x == 0) {
-    mbar_init(BAR(C::B_Q), 1);
+    mbar_init(BAR(C::B_QF), 1);
+    mbar_init(BAR(C::B_QE), 1);
     for (int i = 0; i < NSK; ++i) {
       mbar_init(BAR(C::B_KF + i), 1);
       mbar_init(BAR(C::B_KE + i), 1);
@@ -170,6 +233,8 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(BAR(C::B_SF + t), 1);
       mbar_init(BAR(C::B_PF + t), 128);
       mbar_init(BAR(C::B_OF + t), 1);
+      mbar_init(BAR(C::B_WF + t), 1);
+      mbar_init(BAR(C::B_WE + t), C::WORK_READERS);
     }
     mbar_init(BAR(C::B_DR), 1);
     *abort_flag = 0;
@@ -184,147 +249,213 @@ __global__ void __launch_bounds__(384, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const WaitCtx wctx{abort_flag, p.status, p.timeout_ns};
+
   if (warp >= 8) {
     // ================================ control warpgroup ================================
     setmaxnreg_dec<C::REGS_CONTROL>();
     if (warp == 9) {
-    // =================================== TMA producer ===================================
-    if (lane == 0 && n_tiles > 0) {
-      tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
-      const uint32_t sQ = sbase + C::OFF_Q, sK = sbase + C::OFF_K, sV = sbase + C::OFF_V;
-      int c1, c2, c3;
-      mbar_arrive_expect_tx(BAR(C::B_Q), (act0 + act1) * C::Q_TILE);
-      for (int t = 0; t < 2; ++t) {
-        if (!(t ? act1 : act0)) continue;
-        tma_coords(p.cq, q0 + t * 128, h, b, c1, c2, c3);
+      // =================================== TMA producer ===================================
+      if (lane == 0) {
+        tma_prefetch_desc(&tm_q);
+        tma_prefetch_desc(&tm_k);
+        tma_prefetch_desc(&tm_v);
+        const uint32_t sQ = sbase + C::OFF_Q, sK = sbase + C::OFF_K, sV = sbase + C::OFF_V;
+        int fk = 0, fv = 0, n_q = 0;  // K / V fills and Q loads issued so far by this CTA
+        bool ok = true;
+        for (int item = 0; ok; ++item) {
+          const int slot = item & 1;
+          if (item >= 2) {
+            ok = mbar_wait(BAR(C::B_WE + slot), ((item >> 1) - 1) & 1, wctx, kSiteWork);
+            if (!ok) break;
+          }
+          const int idx = (int)atomicAdd(p.work_counter, 1u);
+          work_slot[slot] = idx;
+          mbar_arrive(BAR(C::B_WF + slot));  // release: the slot write is visible to waiters
+          if (idx >= n_items) break;
+          const WorkItem w = decode_item(p, idx, C::BN);
+          if (w.hi <= w.lo) continue;
+#if MLXP_TRACE
+          if (idx < 8192) {
+            uint32_t smid;
+            asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+            g_mlxp_cta_trace[idx * 4 + 0] = (long long)global_timer_ns();
+            g_mlxp_cta_trace[idx * 4 + 2] = smid;
+            g_mlxp_cta_trace[idx * 4 + 3] = w.hi - w.lo;
+          }
+#endif
+          int c1, c2, c3;
+          if (n_q > 0) {
+            ok = mbar_wait(BAR(C::B_QE), (n_q - 1) & 1, wctx, kSiteProducer);
+            if (!ok) break;
+          }
+          const bool a0 = w.hi0 > w.lo0, a1 = w.hi1 > w.lo1;
+          mbar_arrive_expect_tx(BAR(C::B_QF), (a0 + a1) * C::Q_TILE);
+          for (int t = 0; t < 2; ++t) {
+            if (!(t ? a1 : a0)) continue;
+            tma_coords(p.cq, w.q0 + t * 128, w.h, w.b, c1, c2, c3);
 #pragma unroll
-        for (int kb = 0; kb < C::KB; ++kb)
-          tma_load_4d(sQ + t * C::Q_TILE + kb * C::BOX_Q, &tm_q, BAR(C::B_Q), kb * 64, c1, c2,
-                      c3);
-      }
-      int issued_k = 0, issued_v = 0;
-      bool ok = true;
-      for (int f = 0; f < n_tiles && ok; ++f) {
-        const int j = lo + f;
-        const int ks = f % NSK;
-        if (f >= NSK) ok = mbar_wait(BAR(C::B_KE + ks), ((f / NSK) - 1) & 1, wctx, kSiteProducer);
-        if (!ok) break;
-        mbar_arrive_expect_tx(BAR(C::B_KF + ks), C::KV_TILE);
-        tma_coords(p.ck, j * C::BN, h, b, c1, c2, c3);
+            for (int kb = 0; kb < C::KB; ++kb)
+              tma_load_4d(sQ + t * C::Q_TILE + kb * C::BOX_Q, &tm_q, BAR(C::B_QF), kb * 64, c1,
+                          c2, c3);
+          }
+          ++n_q;
+          for (int j = w.lo; j < w.hi && ok; ++j) {
+            const int ks = fk % NSK;
+            if (fk >= NSK) ok = mbar_wait(BAR(C::B_KE + ks), ((fk / NSK) - 1) & 1, wctx, kSiteProducer);
+            if (!ok) break;
+            mbar_arrive_expect_tx(BAR(C::B_KF + ks), C::KV_TILE);
+            tma_coords(p.ck, j * C::BN, w.h, w.b, c1, c2, c3);
 #pragma unroll
-        for (int kb = 0; kb < C::KB; ++kb)
-          tma_load_4d(sK + ks * C::KV_TILE + kb * C::BOX_KV, &tm_k, BAR(C::B_KF + ks), kb * 64,
-                      c1, c2, c3);
-        issued_k = f + 1;
-        const int vs = f % NSV;
-        if (f >= NSV) ok = mbar_wait(BAR(C::B_VE + vs), ((f / NSV) - 1) & 1, wctx, kSiteProducer);
-        if (!ok) break;
-        mbar_arrive_expect_tx(BAR(C::B_VF + vs), C::KV_TILE);
-        tma_coords(p.cv, j * C::BN, h, b, c1, c2, c3);
+            for (int kb = 0; kb < C::KB; ++kb)
+              tma_load_4d(sK + ks * C::KV_TILE + kb * C::BOX_KV, &tm_k, BAR(C::B_KF + ks),
+                          kb * 64, c1, c2, c3);
+            ++fk;
+            const int vs = fv % NSV;
+            if (fv >= NSV) ok = mbar_wait(BAR(C::B_VE + vs), ((fv / NSV) - 1) & 1, wctx, kSiteProducer);
+            if (!ok) break;
+            mbar_arrive_expect_tx(BAR(C::B_VF + vs), C::KV_TILE);
+            tma_coords(p.cv, j * C::BN, w.h, w.b, c1, c2, c3);
 #pragma unroll
-        for (int kb = 0; kb < C::KB; ++kb)
-          tma_load_4d(sV + vs * C::KV_TILE + kb * C::BOX_KV, &tm_v, BAR(C::B_VF + vs), kb * 64,
-                      c1, c2, c3);
-        issued_v = f + 1;
-      }
-      if (!ok) {
-        // Abort: let every load already issued land before the CTA releases its smem.
-        mbar_wait_drain(BAR(C::B_Q), 0, p.status, p.timeout_ns);
-        for (int f = (issued_k > NSK ? issued_k - NSK : 0); f < issued_k; ++f)
-          mbar_wait_drain(BAR(C::B_KF + f % NSK), (f / NSK) & 1, p.status, p.timeout_ns);
-        for (int f = (issued_v > NSV ? issued_v - NSV : 0); f < issued_v; ++f)
-          mbar_wait_drain(BAR(C::B_VF + f % NSV), (f / NSV) & 1, p.status, p.timeout_ns);
-      }
-    }
-  } else if (warp == 8) {
-    // ==================================== MMA issuer ====================================
-    if (lane == 0 && n_tiles > 0) {
-      const uint32_t sQ = sbase + C::OFF_Q, sK = sbase + C::OFF_K, sV = sbase + C::OFF_V;
-      constexpr uint32_t idesc_qk = make_idesc_f16(128, C::BN, kBF16, false);
-      constexpr uint32_t idesc_pv = make_idesc_f16(128, D, kBF16, true);
-      auto issue_qk = [&](int t, int ks) {
-        const uint32_t d = tmem + (t ? C::TM_S1 : C::TM_S0);
-#pragma unroll
-        for (int kb = 0; kb < C::KB; ++kb) {
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t ad =
-                make_sdesc_sw128(sQ + t * C::Q_TILE + kb * C::BOX_Q + kk * 32, 16, 1024);
-            const uint64_t bd =
-                make_sdesc_sw128(sK + ks * C::KV_TILE + kb * C::BOX_KV + kk * 32, 16, 1024);
-            mma_ss(d, ad, bd, idesc_qk, (kb | kk) ? 1u : 0u);
+            for (int kb = 0; kb < C::KB; ++kb)
+              tma_load_4d(sV + vs * C::KV_TILE + kb * C::BOX_KV, &tm_v, BAR(C::B_VF + vs),
+                          kb * 64, c1, c2, c3);
+            ++fv;
           }
         }
-      };
-      auto issue_pv = [&](int t, int vs, bool acc) {
-        const uint32_t d = tmem + (t ? C::TM_O1 : C::TM_O0);
-        const uint32_t a = tmem + (t ? C::TM_S1 : C::TM_S0);
-#pragma unroll
-        for (int kk = 0; kk < C::BN / 16; ++kk) {
-          const uint64_t bd =
-              make_sdesc_sw128(sV + vs * C::KV_TILE + kk * 16 * 128, C::BOX_KV, 1024);
-          mma_ts(d, a + kk * 8, bd, idesc_pv, (acc || kk > 0) ? 1u : 0u);
+        if (!ok) {
+          // Abort: let every load already issued land before the CTA releases its smem.
+          if (n_q > 0) mbar_wait_drain(BAR(C::B_QF), (n_q - 1) & 1, p.status, p.timeout_ns);
+          for (int f = (fk > NSK ? fk - NSK : 0); f < fk; ++f)
+            mbar_wait_drain(BAR(C::B_KF + f % NSK), (f / NSK) & 1, p.status, p.timeout_ns);
+          for (int f = (fv > NSV ? fv - NSV : 0); f < fv; ++f)
+            mbar_wait_drain(BAR(C::B_VF + f % NSV), (f / NSV) & 1, p.status, p.timeout_ns);
         }
-      };
-      auto active = [&](int t, int j) { return j >= lo_t[t] && j < hi_t[t]; };
+      }
+    } else if (warp == 8) {
+      // ==================================== MMA issuer ====================================
+      if (lane == 0) {
+        constexpr uint32_t idesc_qk = make_idesc_f16(128, C::BN, kBF16, false);
+        constexpr uint32_t idesc_pv = make_idesc_f16(128, D, kBF16, true);
+        // Shared-memory descriptors are kept as (lo, hi) 32-bit words; between MMAs only the
+        // start-address field (lo bits 0-13, 16-byte units) moves, so issuing one MMA costs
+        // one 32-bit add.  K-major Q/K: LBO unused (16 B).  MN-major V: LBO = next 64 columns.
+        const uint32_t q_lo = ((sbase + C::OFF_Q) >> 4) | (1u << 16);
+        const uint32_t k_lo = ((sbase + C::OFF_K) >> 4) | (1u << 16);
+        const uint32_t v_lo = ((sbase + C::OFF_V) >> 4) | ((uint32_t)(C::BOX_KV >> 4) << 16);
 
-      int pcount[2] = {0, 0};
-      bool ok = mbar_wait(BAR(C::B_Q), 0, wctx, kSiteMmaLoad);
-      if (ok) ok = mbar_wait(BAR(C::B_KF + 0), 0, wctx, kSiteMmaLoad);
-      if (ok) {
-        tc_fence_after();
-        for (int t = 0; t < 2; ++t)
-          if (active(t, lo)) {
-            issue_qk(t, 0);
-            tc_commit(BAR(C::B_SF + t));
-          }
-        tc_commit(BAR(C::B_KE + 0));
-      }
-      for (int f = 0; f < n_tiles && ok; ++f) {
-        const int j = lo + f;
-        const int vs = f % NSV;
-        const bool has_next = f + 1 < n_tiles;
-        const int ksn = (f + 1) % NSK;
-        bool k_ready = false;
-        ok = mbar_wait(BAR(C::B_VF + vs), (f / NSV) & 1, wctx, kSiteMmaLoad);
-        if (!ok) break;
-        tc_fence_after();
-        for (int t = 0; t < 2 && ok; ++t) {
-          if (active(t, j)) {
-            ok = mbar_wait(BAR(C::B_PF + t), pcount[t] & 1, wctx, kSiteMmaP);
-            if (!ok) break;
-            ++pcount[t];
-            tc_fence_after();
-            issue_pv(t, vs, j > lo_t[t]);
-            if (j == hi_t[t] - 1) tc_commit(BAR(C::B_OF + t));
-          }
-          if (has_next && active(t, j + 1)) {
-            if (!k_ready) {
-              ok = mbar_wait(BAR(C::B_KF + ksn), ((f + 1) / NSK) & 1, wctx, kSiteMmaLoad);
-              if (!ok) break;
-              tc_fence_after();
-              k_ready = true;
+        auto issue_qk = [&](auto tile, int ks) {
+          constexpr int T = decltype(tile)::value;
+          const uint32_t d = tmem + (T ? C::TM_S1 : C::TM_S0);
+          const uint32_t a0 = q_lo + (uint32_t)(T * C::Q_TILE >> 4);
+          const uint32_t b0 = k_lo + (uint32_t)ks * (uint32_t)(C::KV_TILE >> 4);
+#pragma unroll
+          for (int kb = 0; kb < C::KB; ++kb) {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              mma_ss(d, sdesc(a0 + (uint32_t)((kb * C::BOX_Q + kk * 32) >> 4)),
+                     sdesc(b0 + (uint32_t)((kb * C::BOX_KV + kk * 32) >> 4)), idesc_qk,
+                     (kb | kk) ? 1u : 0u);
             }
-            issue_qk(t, ksn);
-            tc_commit(BAR(C::B_SF + t));
           }
-        }
-        if (!ok) break;
-        tc_commit(BAR(C::B_VE + vs));
-        if (has_next) {
-          if (!k_ready) {  // neither tile uses this key tile: consume it anyway
-            ok = mbar_wait(BAR(C::B_KF + ksn), ((f + 1) / NSK) & 1, wctx, kSiteMmaLoad);
+        };
+        auto issue_pv = [&](auto tile, int vs, bool acc) {
+          constexpr int T = decltype(tile)::value;
+          const uint32_t d = tmem + (T ? C::TM_O1 : C::TM_O0);
+          const uint32_t a = tmem + (T ? C::TM_S1 : C::TM_S0);
+          const uint32_t b0 = v_lo + (uint32_t)vs * (uint32_t)(C::KV_TILE >> 4);
+#pragma unroll
+          for (int kk = 0; kk < C::BN / 16; ++kk)
+            mma_ts(d, a + kk * 8, sdesc(b0 + (uint32_t)(kk * 16 * 128 >> 4)), idesc_pv,
+                   (acc || kk > 0) ? 1u : 0u);
+        };
+        using T0 = std::integral_constant<int, 0>;
+        using T1 = std::integral_constant<int, 1>;
+        int ck = 0, cv = 0, n_q = 0, pc0 = 0, pc1 = 0;  // consumed K / V fills, Q loads, P waits
+        int trace_f = 0;
+        bool ok = true;
+        for (int item = 0; ok; ++item) {
+          const int slot = item & 1;
+          ok = mbar_wait(BAR(C::B_WF + slot), (item >> 1) & 1, wctx, kSiteWork);
+          if (!ok) break;
+          const int idx = work_slot[slot];
+          mbar_arrive(BAR(C::B_WE + slot));
+          if (idx >= n_items) break;
+          const WorkItem w = decode_item(p, idx, C::BN);
+          if (w.hi <= w.lo) continue;
+          // One tile's share of key tile j: PV_t(j) once P_t(j) is ready, then QK_t(j+1).
+          auto tile_step = [&](auto tile, int j, int vs, bool has_next, int ksn,
+                               bool& k_ready) -> bool {
+            constexpr int T = decltype(tile)::value;
+            const int tlo = T ? w.lo1 : w.lo0, thi = T ? w.hi1 : w.hi0;
+            int& pc = T ? pc1 : pc0;
+            if (j >= tlo && j < thi) {
+              if (!mbar_wait(BAR(C::B_PF + T), pc & 1, wctx, kSiteMmaP)) return false;
+              MLXP_TR(true, 2, trace_f, 2 + 2 * T);
+              ++pc;
+              tc_fence_after();
+              issue_pv(tile, vs, j > tlo);
+              if (j == thi - 1) tc_commit(BAR(C::B_OF + T));
+            }
+            if (has_next && j + 1 >= tlo && j + 1 < thi) {
+              if (!k_ready) {
+                if (!mbar_wait(BAR(C::B_KF + ksn), (ck / NSK) & 1, wctx, kSiteMmaLoad))
+                  return false;
+                tc_fence_after();
+                k_ready = true;
+              }
+              issue_qk(tile, ksn);
+              tc_commit(BAR(C::B_SF + T));
+            }
+            MLXP_TR(true, 2, trace_f, 3 + 2 * T);
+            return true;
+          };
+
+          ok = mbar_wait(BAR(C::B_QF), n_q & 1, wctx, kSiteMmaLoad);
+          if (ok) ok = mbar_wait(BAR(C::B_KF + ck % NSK), (ck / NSK) & 1, wctx, kSiteMmaLoad);
+          if (!ok) break;
+          ++n_q;
+          tc_fence_after();
+          if (w.lo >= w.lo0 && w.lo < w.hi0) {
+            issue_qk(T0{}, ck % NSK);
+            tc_commit(BAR(C::B_SF + 0));
+          }
+          if (w.lo >= w.lo1 && w.lo < w.hi1) {
+            issue_qk(T1{}, ck % NSK);
+            tc_commit(BAR(C::B_SF + 1));
+          }
+          tc_commit(BAR(C::B_KE + ck % NSK));
+          ++ck;
+          if (w.hi - w.lo == 1) tc_commit(BAR(C::B_QE));  // every QK of this item is issued
+          for (int j = w.lo; j < w.hi && ok; ++j, ++trace_f) {
+            const int vs = cv % NSV;
+            const bool has_next = j + 1 < w.hi;
+            const int ksn = ck % NSK;
+            bool k_ready = false;
+            MLXP_TR(true, 2, trace_f, 0);
+            ok = mbar_wait(BAR(C::B_VF + vs), (cv / NSV) & 1, wctx, kSiteMmaLoad);
+            MLXP_TR(true, 2, trace_f, 1);
             if (!ok) break;
+            tc_fence_after();
+            ok = tile_step(T0{}, j, vs, has_next, ksn, k_ready);
+            if (ok) ok = tile_step(T1{}, j, vs, has_next, ksn, k_ready);
+            if (!ok) break;
+            tc_commit(BAR(C::B_VE + vs));
+            ++cv;
+            if (has_next) {
+              if (!k_ready) {  // neither tile uses this key tile: consume it anyway
+                ok = mbar_wait(BAR(C::B_KF + ksn), (ck / NSK) & 1, wctx, kSiteMmaLoad);
+                if (!ok) break;
+              }
+              tc_commit(BAR(C::B_KE + ksn));
+              ++ck;
+              if (j + 2 == w.hi) tc_commit(BAR(C::B_QE));  // the item's last QKs are issued
+            }
           }
-          tc_commit(BAR(C::B_KE + ksn));
         }
+        // Every MMA issued by this thread must finish before TMEM/smem are released.
+        tc_commit(BAR(C::B_DR));
+        mbar_wait_drain(BAR(C::B_DR), 0, p.status, p.timeout_ns);
       }
-      // Every MMA issued by this thread must finish before TMEM/smem are released.
-      tc_commit(BAR(C::B_DR));
-      mbar_wait_drain(BAR(C::B_DR), 0, p.status, p.timeout_ns);
-    }
     }  // warps 10-11: spare
     // ---- teardown: every role is done with TMEM and smem after this barrier
     __syncwarp();
@@ -340,124 +471,162 @@ __global__ void __launch_bounds__(384, 1)
     const int t = warp >> 2;
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
-    const int qrow = q0 + t * 128 + row;
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
     const uint32_t tS = tmem + lane_off + (t ? C::TM_S1 : C::TM_S0);
     const uint32_t tO = tmem + lane_off + (t ? C::TM_O1 : C::TM_O0);
-    const int tlo = lo_t[t], thi = hi_t[t];
-    const long long r0 = q0 + t * 128;
-    const long long r1 = (r0 + 128 < p.Sq) ? r0 + 128 : p.Sq;
     const float sl2 = p.scale_log2;
-    float m = -INFINITY, l = 0.f;
+    int n_s = 0, n_o = 0;  // S tiles and item epilogues consumed by this tile so far
     bool ok = true;
-
-    for (int it = 0; it < thi - tlo; ++it) {
-      const int j = tlo + it;
-      ok = mbar_wait(BAR(C::B_SF + t), it & 1, wctx, kSiteSoftmaxS);
+    for (int item = 0; ok; ++item) {
+      const int slot = item & 1;
+      ok = mbar_wait(BAR(C::B_WF + slot), (item >> 1) & 1, wctx, kSiteWork);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
-      tc_fence_after();
-      uint32_t r0v[32], r1v[32], r2v[32], r3v[32];
-      tmem_ld_x32(tS + 0, r0v);
-      tmem_ld_x32(tS + 32, r1v);
-      tmem_ld_x32(tS + 64, r2v);
-      tmem_ld_x32(tS + 96, r3v);
-      tmem_wait_ld();
-      reg_fence(r0v);
-      reg_fence(r1v);
-      reg_fence(r2v);
-      reg_fence(r3v);
-      float s[128];
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        s[c] = __uint_as_float(r0v[c]);
-        s[32 + c] = __uint_as_float(r1v[c]);
-        s[64 + c] = __uint_as_float(r2v[c]);
-        s[96 + c] = __uint_as_float(r3v[c]);
-      }
-      const long long c0 = (long long)j * C::BN;
-      if (!tile_is_full(p.mask, r0, r1, c0, c0 + C::BN)) {
-        int c_lo, c_hi;
-        row_col_interval(p.mask, qrow, c0, C::BN, c_lo, c_hi);
-#pragma unroll
-        for (int c = 0; c < 128; ++c) s[c] = (c < c_lo || c > c_hi) ? -INFINITY : s[c];
-      }
-      float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
-#pragma unroll
-      for (int c = 4; c < 128; c += 4) {
-        mx0 = fmaxf(mx0, s[c]);
-        mx1 = fmaxf(mx1, s[c + 1]);
-        mx2 = fmaxf(mx2, s[c + 2]);
-        mx3 = fmaxf(mx3, s[c + 3]);
-      }
-      const float mloc = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
-      const float m_new = fmaxf(m, mloc);
-      const bool resc = m_new > m + 8.0f;
-      float alpha = 1.f;
-      if (resc) {
-        alpha = ex2_approx(m - m_new);
-        m = m_new;
-      }
-      const float neg_mu = (m == -INFINITY) ? 0.f : -m;
-      float rs0 = 0.f, rs1 = 0.f;
-      {
-        uint32_t pk[32];
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float a0 = ex2_approx(fmaf(s[2 * c], sl2, neg_mu));
-          const float a1 = ex2_approx(fmaf(s[2 * c + 1], sl2, neg_mu));
-          rs0 += a0;
-          rs1 += a1;
-          pk[c] = pack2<kBF16>(a0, a1);
-        }
-        tmem_st_x32(tS + 0, pk);
-      }
-      {
-        uint32_t pk[32];
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float a0 = ex2_approx(fmaf(s[64 + 2 * c], sl2, neg_mu));
-          const float a1 = ex2_approx(fmaf(s[64 + 2 * c + 1], sl2, neg_mu));
-          rs0 += a0;
-          rs1 += a1;
-          pk[c] = pack2<kBF16>(a0, a1);
-        }
-        tmem_st_x32(tS + 32, pk);
-      }
-      if (it > 0 && __any_sync(0xffffffffu, resc)) {
-        // O_t holds PV_t(j-1) (complete: it was issued before QK_t(j), whose commit we saw);
-        // PV_t(j) is not issued before the arrive below, so it sees the rescaled O.
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t ov[32];
-          tmem_ld_x32(tO + c * 32, ov);
-          tmem_wait_ld();
-          reg_fence(ov);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-          tmem_st_x32(tO + c * 32, ov);
-        }
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(BAR(C::B_PF + t));
-      l = l * alpha + (rs0 + rs1);
-    }
+      const int idx = work_slot[slot];
+      mbar_arrive(BAR(C::B_WE + slot));
+      if (idx >= n_items) break;
+      const WorkItem w = decode_item(p, idx, C::BN);
+      const int tlo = t ? w.lo1 : w.lo0, thi = t ? w.hi1 : w.hi0;
+      const int qrow = w.q0 + t * 128 + row;
+      const long long r0 = w.q0 + t * 128;
+      const long long r1 = (r0 + 128 < p.Sq) ? r0 + 128 : p.Sq;
+      float m = -INFINITY, l = 0.f;
 
-    // ------------------------------------ epilogue ------------------------------------
-    const bool has_rows = qrow < p.Sq;
-    const int n_it = thi - tlo;
-    if (ok && n_it > 0) {
-      ok = mbar_wait(BAR(C::B_OF + t), 0, wctx, kSiteSoftmaxO);
-      ok = __all_sync(0xffffffffu, ok);
-    }
-    if (ok) {
-      if (n_it > 0) tc_fence_after();
-      const float inv_l = (n_it > 0 && l > 0.f) ? 1.0f / l : 0.f;
-      const float lse_v =
-          (n_it > 0 && l > 0.f) ? (m + log2f(l)) * 0.69314718055994531f : -INFINITY;
+      for (int it = 0; it < thi - tlo; ++it, ++n_s) {
+        const int j = tlo + it;
+        MLXP_TR(wq == 0 && lane == 0, t, it, 0);
+        ok = mbar_wait(BAR(C::B_SF + t), n_s & 1, wctx, kSiteSoftmaxS);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        MLXP_TR(wq == 0 && lane == 0, t, it, 1);
+        tc_fence_after();
+        // S row -> registers in two halves: masking the first half overlaps the second
+        // half's TMEM read.
+        float s[128];
+        {
+          uint32_t ra[32], rb[32];
+          tmem_ld_x32(tS + 0, ra);
+          tmem_ld_x32(tS + 32, rb);
+          tmem_wait_ld();
+          reg_fence(ra);
+          reg_fence(rb);
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            s[c] = __uint_as_float(ra[c]);
+            s[32 + c] = __uint_as_float(rb[c]);
+          }
+          tmem_ld_x32(tS + 64, ra);
+          tmem_ld_x32(tS + 96, rb);
+          const long long c0 = (long long)j * C::BN;
+          const bool full = tile_is_full(p.mask, r0, r1, c0, c0 + C::BN);
+          int c_lo = 0, c_hi = C::BN - 1;
+          if (!full) {
+            row_col_interval(p.mask, qrow, c0, C::BN, c_lo, c_hi);
+#pragma unroll
+            for (int c = 0; c < 64; ++c) s[c] = (c < c_lo || c > c_hi) ? -INFINITY : s[c];
+          }
+          tmem_wait_ld();
+          reg_fence(ra);
+          reg_fence(rb);
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            s[64 + c] = __uint_as_float(ra[c]);
+            s[96 + c] = __uint_as_float(rb[c]);
+          }
+          if (!full) {
+#pragma unroll
+            for (int c = 64; c < 128; ++c) s[c] = (c < c_lo || c > c_hi) ? -INFINITY : s[c];
+          }
+        }
+        // row max: 3-input max, four independent chains
+        float mx0 = max3(s[0], s[1], s[2]), mx1 = max3(s[3], s[4], s[5]);
+        float mx2 = max3(s[6], s[7], s[8]), mx3 = max3(s[9], s[10], s[11]);
+#pragma unroll
+        for (int c = 12; c < 124; c += 8) {
+          mx0 = max3(mx0, s[c], s[c + 1]);
+          mx1 = max3(mx1, s[c + 2], s[c + 3]);
+          mx2 = max3(mx2, s[c + 4], s[c + 5]);
+          mx3 = max3(mx3, s[c + 6], s[c + 7]);
+        }
+        mx0 = max3(mx0, s[124], s[125]);
+        mx1 = max3(mx1, s[126], s[127]);
+        const float mloc = max3(mx0, mx1, fmaxf(mx2, mx3)) * sl2;
+        MLXP_TR(wq == 0 && lane == 0, t, it, 2);
+        const float m_new = fmaxf(m, mloc);
+        const bool resc = m_new > m + 8.0f;
+        float alpha = 1.f;
+        if (resc) {
+          alpha = ex2_approx(m - m_new);
+          m = m_new;
+        }
+        const float neg_mu = (m == -INFINITY) ? 0.f : -m;
+        // p = 2^(s * scale * log2(e) - m): kPolyPerOct of every 8 column pairs on the FMA
+        // pipe (exp2_poly2), the rest on the MUFU unit, so neither unit limits the row.
+        const float2 sl2v = make_float2(sl2, sl2), negm = make_float2(neg_mu, neg_mu);
+        float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const float2 x =
+                fma2(make_float2(s[64 * hf + 2 * c], s[64 * hf + 2 * c + 1]), sl2v, negm);
+            float2 e;
+            if ((c & 7) < kPolyPerOct<D>) {
+              e = exp2_poly2(x);
+            } else {
+              e.x = ex2_approx(x.x);
+              e.y = ex2_approx(x.y);
+            }
+            if (c & 1)
+              acc1 = add2(acc1, e);
+            else
+              acc0 = add2(acc0, e);
+            pk[c] = pack2<kBF16>(e.x, e.y);
+          }
+          tmem_st_x32(tS + 32 * hf, pk);
+        }
+        MLXP_TR(wq == 0 && lane == 0, t, it, 3);
+        if (it > 0 && __any_sync(0xffffffffu, resc)) {
+          // O_t holds PV_t(j-1) (complete: it was issued before QK_t(j), whose commit we
+          // saw); PV_t(j) is not issued before the arrive below, so it sees the rescaled O.
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t ov[32];
+            tmem_ld_x32(tO + c * 32, ov);
+            tmem_wait_ld();
+            reg_fence(ov);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+            tmem_st_x32(tO + c * 32, ov);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(BAR(C::B_PF + t));
+        MLXP_TR(wq == 0 && lane == 0, t, it, 4);
+        l = l * alpha + ((acc0.x + acc1.x) + (acc0.y + acc1.y));
+      }
+      if (!ok) break;
+
+      // ------------------------------------ epilogue ------------------------------------
+      const bool has_rows = qrow < p.Sq;
+      const int n_it = thi - tlo;
+      if (n_it > 0) {
+        ok = mbar_wait(BAR(C::B_OF + t), n_o & 1, wctx, kSiteSoftmaxO);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        ++n_o;
+        tc_fence_after();
+      }
+      // A row that never saw an admissible key keeps m = -inf: it is empty (O = 0, LSE = -inf)
+      // even though the polynomial exp2 leaves ~2^-125 per masked element in l.
+      const bool valid = n_it > 0 && l > 0.f && m != -INFINITY;
+      const float inv_l = valid ? 1.0f / l : 0.f;
+      const float lse_v = valid ? (m + log2f(l)) * 0.69314718055994531f : -INFINITY;
       if (has_rows && p.lse != nullptr)
-        p.lse[(long long)split * p.lse_split + ((long long)b * p.H + h) * p.Sq + qrow] = lse_v;
+        p.lse[(long long)w.split * p.lse_split + ((long long)w.b * p.H + w.h) * p.Sq + qrow] =
+            lse_v;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t ov[32];
@@ -470,8 +639,8 @@ __global__ void __launch_bounds__(384, 1)
           for (int i = 0; i < 32; ++i) ov[i] = 0u;
         }
         if (has_rows) {
-          const long long off = (long long)split * p.o_split + (long long)b * p.o_sb +
-                                (long long)h * p.o_sh + (long long)qrow * p.o_ss + c * 32;
+          const long long off = (long long)w.split * p.o_split + (long long)w.b * p.o_sb +
+                                (long long)w.h * p.o_sh + (long long)qrow * p.o_ss + c * 32;
           if (p.out_f32) {
             float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.o) + off);
 #pragma unroll
@@ -484,23 +653,36 @@ __global__ void __launch_bounds__(384, 1)
             uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.o) + off);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              uint4 w;
-              w.x = pack2<kBF16>(__uint_as_float(ov[8 * i + 0]) * inv_l,
-                                 __uint_as_float(ov[8 * i + 1]) * inv_l);
-              w.y = pack2<kBF16>(__uint_as_float(ov[8 * i + 2]) * inv_l,
-                                 __uint_as_float(ov[8 * i + 3]) * inv_l);
-              w.z = pack2<kBF16>(__uint_as_float(ov[8 * i + 4]) * inv_l,
-                                 __uint_as_float(ov[8 * i + 5]) * inv_l);
-              w.w = pack2<kBF16>(__uint_as_float(ov[8 * i + 6]) * inv_l,
-                                 __uint_as_float(ov[8 * i + 7]) * inv_l);
-              dst[i] = w;
+              uint4 v4;
+              v4.x = pack2<kBF16>(__uint_as_float(ov[8 * i + 0]) * inv_l,
+                                  __uint_as_float(ov[8 * i + 1]) * inv_l);
+              v4.y = pack2<kBF16>(__uint_as_float(ov[8 * i + 2]) * inv_l,
+                                  __uint_as_float(ov[8 * i + 3]) * inv_l);
+              v4.z = pack2<kBF16>(__uint_as_float(ov[8 * i + 4]) * inv_l,
+                                  __uint_as_float(ov[8 * i + 5]) * inv_l);
+              v4.w = pack2<kBF16>(__uint_as_float(ov[8 * i + 6]) * inv_l,
+                                  __uint_as_float(ov[8 * i + 7]) * inv_l);
+              dst[i] = v4;
             }
           }
         }
       }
+#if MLXP_TRACE
+      if (t == 1 && wq == 0 && lane == 0 && idx < 8192)
+        g_mlxp_cta_trace[idx * 4 + 1] = (long long)global_timer_ns();
+#endif
     }
     tc_fence_before();
     __syncthreads();  // teardown barrier (pairs with the control warpgroup's)
+    // The last CTA to finish resets the launch's work counter for the next launch.
+    if (threadIdx.x == 0) {
+      __threadfence();
+      if (atomicAdd(p.work_counter + 1, 1u) == gridDim.x - 1) {
+        atomicExch(p.work_counter, 0u);
+        atomicExch(p.work_counter + 1, 0u);
+        __threadfence();
+      }
+    }
   }
 }
 

@@ -24,6 +24,11 @@
 namespace mlxp {
 
 __device__ int g_dev_status = 0;
+// Work counters of the persistent tensor-core kernel: kCounterSlots pairs per device, handed
+// out round-robin to launches so that launches in flight on different streams at the same time
+// do not share one (each pair is reset by the last CTA of the launch that used it).
+constexpr int kCounterSlots = 256;
+__device__ unsigned g_work_counters[2 * kCounterSlots];
 
 namespace {
 
@@ -48,6 +53,8 @@ std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
 constexpr int kMaxDevices = 64;
 std::mutex g_dev_mu;
 int* g_status_ptr[kMaxDevices] = {};
+unsigned* g_counter_ptr[kMaxDevices] = {};
+std::atomic<unsigned> g_counter_seq[kMaxDevices];
 int g_num_sms[kMaxDevices] = {};
 unsigned g_attr_done[kMaxDevices] = {};
 
@@ -70,7 +77,11 @@ int device_info(int** status, int* sms) {
     int n = 0;
     e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+    void* cptr = nullptr;
+    e = cudaGetSymbolAddress(&cptr, g_work_counters);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(work counters)");
     g_status_ptr[dev] = static_cast<int*>(ptr);
+    g_counter_ptr[dev] = static_cast<unsigned*>(cptr);
     g_num_sms[dev] = n;
   }
   if (status) *status = g_status_ptr[dev];
@@ -262,8 +273,11 @@ struct TcKernel {
                     const FwdParams& p, cudaStream_t stream) {
     auto kern = attn_fwd_sm100_kernel<D, BF16, NSK, NSV>;
     if (int rc = ensure_smem_attr(kern, Cfg::SMEM_ALLOC, kBit)) return rc;
-    const long long grid = (long long)p.n_qblk * p.B * p.H * p.splits;
-    if (grid <= 0) return MLXP_OK;
+    const long long items = (long long)p.n_qblk * p.B * p.H * p.splits;
+    if (items <= 0) return MLXP_OK;
+    int sms = 0;
+    if (int rc = device_info(nullptr, &sms)) return rc;
+    const long long grid = std::min<long long>(items, sms);  // persistent: one CTA per SM
     kern<<<(unsigned)grid, Cfg::THREADS, Cfg::SMEM_ALLOC, stream>>>(mq, mk, mv, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
@@ -422,10 +436,24 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
   const int kv_tiles = (int)((pr.Skv + kBN - 1) / kBN);
   p.tiles_per_split = (kv_tiles + splits - 1) / splits;
   p.heavy_first = pr.causal ? 1 : 0;
+  // About two waves of items per scheduling group: enough to balance, small enough that the
+  // group's K/V (2 * Skv * D * 2 bytes per unit) stays in L2.
+  {
+    const long long per_unit = (long long)p.n_qblk * splits;
+    long long g = (2LL * sms + per_unit - 1) / per_unit;
+    g = std::max<long long>(1, std::min<long long>(g, pr.B * pr.H));
+    p.group_bh = (int)g;
+  }
   p.scale_log2 = scale_log2;
   p.mask = mask_of(pr);
   p.status = status;
   p.timeout_ns = g_timeout_ns.load();
+  {
+    int dev;
+    if (int rc = current_device(dev)) return rc;
+    const unsigned slot = g_counter_seq[dev].fetch_add(1) % kCounterSlots;
+    p.work_counter = g_counter_ptr[dev] + 2 * slot;
+  }
 
   if (splits == 1) {
     p.out_f32 = out_f32 ? 1 : 0;
@@ -588,6 +616,20 @@ int mlxp_set_wait_timeout_ns(uint64_t ns) {
   g_timeout_ns.store(ns);
   return MLXP_OK;
 }
+
+#if MLXP_TRACE
+// Trace builds only: copies the cycle stamps of CTA 0 (see attn_fwd_sm100.cuh) to dst.
+int mlxp_trace_read(long long* dst, int n) {
+  const int cap = 4 * 64 * 8;
+  cudaError_t e = cudaMemcpyFromSymbol(dst, g_mlxp_trace, sizeof(long long) * (n < cap ? n : cap));
+  return e == cudaSuccess ? MLXP_OK : cuda_fail(e, "trace read");
+}
+int mlxp_cta_trace_read(long long* dst, int n) {
+  const int cap = 8192 * 4;
+  cudaError_t e = cudaMemcpyFromSymbol(dst, g_mlxp_cta_trace, sizeof(long long) * (n < cap ? n : cap));
+  return e == cudaSuccess ? MLXP_OK : cuda_fail(e, "cta trace read");
+}
+#endif
 
 int mlxp_selftest_wait_timeout(uint64_t timeout_ns, void* cuda_stream) {
   int* status = nullptr;

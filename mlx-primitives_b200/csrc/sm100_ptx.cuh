@@ -195,6 +195,14 @@ __device__ __forceinline__ uint64_t make_sdesc_sw128(uint32_t saddr, uint32_t lb
   return d;
 }
 
+// The same descriptor split into its two 32-bit words: sdesc(lo) joins a lo word (start address
+// >> 4 in bits 0-13, LBO >> 4 in bits 16-29) with the constant hi word of every descriptor
+// this library uses (SBO 1024 B, version 1, SWIZZLE_128B).
+constexpr uint32_t kDescHiSw128 = (1024u >> 4) | (1u << 14) | (2u << 29);
+__device__ __forceinline__ uint64_t sdesc(uint32_t lo) {
+  return ((uint64_t)kDescHiSw128 << 32) | lo;
+}
+
 // ------------------------------------------------------------------------------------------
 // TMEM <-> registers.  Shape 32x32b: thread t of the warp reads/writes TMEM lane
 // (32 * (warp % 4) + t); .xN = N consecutive 32-bit columns.
@@ -265,6 +273,66 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Packed two-lane fp32 arithmetic (sm_100: one instruction for both lanes).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "sub.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for two lanes on the FMA/ALU pipes instead of the MUFU unit.
+// Method: Cody-Waite range reduction x = j + f with j = round-to-nearest(x) (obtained by adding
+// and subtracting 1.5 * 2^23, which leaves j in the low mantissa bits of the sum) and
+// f in [-0.5, 0.5]; 2^f from a degree-3 polynomial fitted with the Remez exchange algorithm for
+// minimax relative error on [-0.5, 0.5] (max relative error 7.5e-5 evaluated in fp32 Horner
+// form, far below bf16's 3.9e-3); 2^j applied by adding j to the exponent field.  x is clamped
+// to -125 so that the result stays a normal number (2^-125 ~ 2.4e-38, zero for every purpose
+// here; rows that never see an admissible key are zeroed separately).
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kC0 = 0.99992805719375610f;  // 0x3f7ffb49
+  constexpr float kC1 = 0.69326096773147580f;  // 0x3f31798d
+  constexpr float kC2 = 0.24261112511157990f;  // 0x3e786f0d
+  constexpr float kC3 = 0.05517166852951050f;  // 0x3d61fbb0
+  constexpr float kRound = 12582912.0f;        // 1.5 * 2^23
+  x.x = fmaxf(x.x, -125.0f);
+  x.y = fmaxf(x.y, -125.0f);
+  const float2 t = add2(x, make_float2(kRound, kRound));
+  const float2 j = add2(t, make_float2(-kRound, -kRound));
+  const float2 f = sub2(x, j);
+  float2 p = fma2(make_float2(kC3, kC3), f, make_float2(kC2, kC2));
+  p = fma2(p, f, make_float2(kC1, kC1));
+  p = fma2(p, f, make_float2(kC0, kC0));
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
 }
 
 template <bool kBF16>
