@@ -97,6 +97,32 @@ size_t mlxp_attn_workspace_size(int dtype, int64_t B, int64_t H, int64_t Sq, int
                                 int64_t kv_pos_offset, int64_t kv_splits);
 
 /*
+ * Split-KV attention forward that allocates nothing.  No counterpart in the reference (MLX
+ * allocates every intermediate itself); this entry point exists for callers that cannot call
+ * cudaMalloc or hand out a workspace: code that is given only the input and output device
+ * pointers by a host framework it plugs into, and latency-critical loops that must not take a
+ * device allocation (cudaMalloc may synchronise the device and its caching allocators may
+ * block on a lock).
+ *
+ * Same arguments and results as mlxp_attn_fwd with kv_splits >= 2 (bf16/fp16 only), except that
+ * the per-split partial outputs live in a static device array of 32 MiB inside the library
+ * (held by every GPU that loads the library until process exit) instead of a workspace.
+ * Sizes whose partials need more than that (splits * B*H*Sq rows * (head_dim + 1) floats) are
+ * rejected with MLXP_ERR_WORKSPACE and a message; the caller can use fewer splits.
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress) and
+ * caches it; make that first call before any stream capture.  Every call shares the array:
+ * calls that overlap on the GPU (other streams, other threads) race on it and must be
+ * serialised by the caller.  Nothing in the array needs to start at zero.
+ */
+int mlxp_attn_fwd_split_noalloc(const void* q, const void* k, const void* v, void* o,
+                                float* lse, int dtype, int64_t B, int64_t H, int64_t Sq,
+                                int64_t Skv, int64_t D, const int64_t q_strides[4],
+                                const int64_t k_strides[4], const int64_t v_strides[4],
+                                const int64_t o_strides[4], float scale, int causal,
+                                int64_t window_left, int64_t window_right, int64_t q_pos_offset,
+                                int64_t kv_pos_offset, int64_t kv_splits, void* cuda_stream);
+
+/*
  * Partial attention forward: as mlxp_attn_fwd, but writes the NORMALISED output in fp32
  * (o_part, [B,H,Sq,D] with o_strides) and the natural-log LSE (lse_part, [B,H,Sq]
  * contiguous, required).  This is the (O, m, l) triple of compute_chunk_attention

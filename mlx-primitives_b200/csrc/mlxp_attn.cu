@@ -263,6 +263,27 @@ size_t split_workspace(const Problem& pr, int splits) {
   return o_bytes + rows * 4;
 }
 
+// Scratch of mlxp_attn_fwd_split_noalloc: a fixed array in the library's device image, so the
+// entry point needs no allocation.  Every GPU that loads the library holds it until exit.
+// Its device address is looked up once per device (the first call on that device).
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+int noalloc_scratch(void** out) {
+  int dev;
+  if (int rc = current_device(dev)) return rc;
+  std::lock_guard<std::mutex> g(g_dev_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-allocation scratch)");
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return MLXP_OK;
+}
+
 template <int D, bool BF16>
 struct TcKernel {
   static constexpr int NSK = (D == 128) ? 2 : 3;
@@ -529,6 +550,42 @@ size_t mlxp_attn_workspace_size(int dtype, int64_t B, int64_t H, int64_t Sq, int
     splits = (int)std::min<int64_t>(kv_splits, (Skv + kBN - 1) / kBN);
   }
   return split_workspace(pr, splits);
+}
+
+// Split-KV attention whose scratch (the per-split fp32 partial outputs and LSEs) lives in the
+// library's static device array instead of a caller-provided workspace; see mlxp_attn.h.
+// Nothing in the scratch needs to start at zero: every (split, row) partial is written by the
+// attention kernel (a split with no admissible keys writes O = 0, LSE = -inf) before the merge
+// kernel reads it, so the contents left by an earlier call are never used.
+int mlxp_attn_fwd_split_noalloc(const void* q, const void* k, const void* v, void* o,
+                                float* lse, int dtype, int64_t B, int64_t H, int64_t Sq,
+                                int64_t Skv, int64_t D, const int64_t q_strides[4],
+                                const int64_t k_strides[4], const int64_t v_strides[4],
+                                const int64_t o_strides[4], float scale, int causal,
+                                int64_t window_left, int64_t window_right, int64_t q_pos_offset,
+                                int64_t kv_pos_offset, int64_t kv_splits, void* cuda_stream) {
+  Problem pr{dtype, B, H, Sq, Skv, D, causal ? 1 : 0, window_left, window_right, q_pos_offset,
+             kv_pos_offset};
+  if (int rc = validate(pr)) return rc;
+  if (dtype == MLXP_DTYPE_FP32)
+    return fail(MLXP_ERR_UNSUPPORTED,
+                "mlxp_attn_fwd_split_noalloc runs the bf16/fp16 split-KV kernel");
+  if (kv_splits < 2)
+    return fail(MLXP_ERR_INVALID, "mlxp_attn_fwd_split_noalloc needs kv_splits >= 2, got %lld",
+                (long long)kv_splits);
+  const int splits = (int)std::min<int64_t>(kv_splits, std::max<int64_t>(1, (Skv + kBN - 1) / kBN));
+  const size_t need = split_workspace(pr, splits);
+  if (need > kNoAllocScratchBytes)
+    return fail(MLXP_ERR_WORKSPACE,
+                "mlxp_attn_fwd_split_noalloc: %d key splits of B*H*Sq = %lld rows x head_dim "
+                "%lld need %zu bytes of scratch; the static scratch holds %zu bytes (use fewer "
+                "splits, a smaller batch, or mlxp_attn_fwd with a workspace)",
+                splits, (long long)(B * H * Sq), (long long)D, need, kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  return attn_fwd_impl(q, k, v, o, lse, pr, q_strides, k_strides, v_strides, o_strides, scale,
+                       splits, scratch, kNoAllocScratchBytes, false,
+                       static_cast<cudaStream_t>(cuda_stream));
 }
 
 int mlxp_attn_fwd_partial(const void* q, const void* k, const void* v, float* o_part,
