@@ -49,6 +49,10 @@ CONFIGS = {
     "c4": dict(workload="ChunkedCrossAttention bf16 BSHD chunk4096 (config 4)", api="chunked",
                dtype="bf16", layout="BSHD", B=8, H=16, S=512, Skv=65536, D=64, causal=False,
                window=-1, std=0.5),
+    # total work fixed: one 128K-token sequence, sequence-parallel ring over the N GPUs
+    "c5": dict(workload="long-context flash_attention bf16 BHSD causal, zig-zag ring (config 5)",
+               api="ring", dtype="bf16", layout="BHSD", B=1, H=32, S=131072, Skv=131072,
+               D=128, causal=True, window=-1, std=1.0),
 }
 
 L2_BYTES = 126 * 1024 * 1024
@@ -217,6 +221,12 @@ def run_reference_arm(args, c, rank):
 
 
 def config_json(c, n):
+    if c["api"] == "ring":
+        par = (f"sequence-parallel zig-zag ring over {n} GPUs (NCCL send/recv of K/V, LSE merge)"
+               if n > 1 else "single GPU")
+        return {"workload": c["workload"], "global_batch": c["B"], "heads": c["H"],
+                "seq_len": c["S"], "head_dim": c["D"], "layout": c["layout"], "causal": True,
+                "parallelism": par, "l2": "inputs larger than L2"}
     return {"workload": c["workload"], "global_batch": c["B"] * n, "batch_per_gpu": c["B"],
             "heads": c["H"], "seq_len": c["S"], "kv_len": c["Skv"], "head_dim": c["D"],
             "layout": c["layout"], "causal": c["causal"], "window": c["window"],
@@ -263,20 +273,39 @@ def main():
     B, H, S, Skv, D = c["B"], c["H"], c["S"], c["Skv"], c["D"]
     shape_q = (B, H, S, D) if c["layout"] == "BHSD" else (B, S, H, D)
     shape_kv = (B, H, Skv, D) if c["layout"] == "BHSD" else (B, Skv, H, D)
+    ring = c["api"] == "ring" and world > 1
     g = torch.Generator(device=dev)
-    g.manual_seed(42 + rank)
+    g.manual_seed(42 + (0 if c["api"] == "ring" else rank))  # the ring shares one sequence
     q = (torch.randn(shape_q, generator=g, device=dev) * c["std"]).to(dtype)
     k = (torch.randn(shape_kv, generator=g, device=dev) * c["std"]).to(dtype)
     v = (torch.randn(shape_kv, generator=g, device=dev) * c["std"]).to(dtype)
+    if ring:
+        from mlx_primitives.attention.ring import ring_flash_attention, zigzag_shard
+        q, k, v = (zigzag_shard(t, world, rank).contiguous() for t in (q, k, v))
+        torch.cuda.empty_cache()
 
     def step(qq, kk, vv):
-        if c["api"] == "flash":
+        if ring:
+            host = qq.device.type == "cpu"
+            if host:
+                qq, kk, vv = (t.to(dev, non_blocking=True) for t in (qq, kk, vv))
+            o = ring_flash_attention(qq, kk, vv)
+            if host:
+                h = torch.empty(o.shape, dtype=o.dtype, pin_memory=True)
+                h.copy_(o, non_blocking=True)
+                torch.cuda.current_stream(dev).synchronize()
+                return h
+            return o
+        if c["api"] in ("flash", "ring"):
             return mp.flash_attention(qq, kk, vv, causal=c["causal"], layout=c["layout"])
         if c["api"] == "swa":
             return mp.sliding_window_attention(qq, kk, vv, window_size=c["window"], causal=c["causal"])
         return mp.chunked_cross_attention(qq, kk, vv, chunk_size=4096, causal=c["causal"])
 
-    launches_per_step = 2 if c["api"] == "chunked" else 1
+    if ring:  # per step and rank: partials + merges for the pairs below the diagonal, 2 casts
+        launches_per_step = 2 * (2 * world) + 2
+    else:
+        launches_per_step = 2 if c["api"] == "chunked" else 1
     flush = config_bytes(c) <= L2_BYTES
     scratch = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev) if flush else None
 
@@ -310,7 +339,9 @@ def main():
     ms_local = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
     ms = max_over_ranks(ms_local)
 
-    flops = config_flops(c)  # per GPU per step
+    flops = config_flops(c)  # per GPU per step (c5: the whole sequence, shared by the ranks)
+    if c["api"] == "ring":
+        flops = flops / world
     value = world * flops / (ms * 1e-3) / 1e12
     peak, peak_sus, hbm, peak_src = load_peaks()
     achieved = flops / (ms_local * 1e-3) / 1e12  # this rank's work per step / its step time
@@ -340,7 +371,8 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True,
+            "scaling": "strong" if c["api"] == "ring" else "weak", "vs_baseline": None,
             "dtype": "f32" if c["dtype"] == "fp32" else "bf16",
             "data": "synthetic: seeded N(0, std^2) tensors generated on device (seed 42 + rank)",
             "config": config_json(c, world),
