@@ -61,7 +61,7 @@ __device__ long long g_mlxp_cta_trace[8192 * 4];  // per item: start ns, end ns,
   } while (0)
 #endif
 
-template <int D, int NSK, int NSV>
+template <int D, int NS>
 struct Sm100Cfg {
   static constexpr int BM = 128;  // rows per Q tile (= TMEM lanes)
   static constexpr int BN = 128;  // keys per K/V tile
@@ -72,16 +72,18 @@ struct Sm100Cfg {
   static constexpr int BOX_KV = BN * 128;  // bytes of one 64-column box of a K/V tile
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + 2 * Q_TILE;
-  static constexpr int OFF_V = OFF_K + NSK * KV_TILE;
-  static constexpr int OFF_BAR = OFF_V + NSV * KV_TILE;
+  static constexpr int OFF_V = OFF_K + NS * KV_TILE;
+  static constexpr int OFF_BAR = OFF_V + NS * KV_TILE;
   // barrier indices
   static constexpr int B_QF = 0;           // Q loaded
   static constexpr int B_QE = 1;           // Q buffer free (last QK of the item done)
+  // K and V of one key tile share a ring stage: K and V each have a "loaded" barrier, and one
+  // "free" barrier per stage is committed once both have been consumed (one tcgen05.commit per
+  // key tile instead of two: commits interleaved with the MMA stream are not free).
   static constexpr int B_KF = 2;
-  static constexpr int B_KE = B_KF + NSK;
-  static constexpr int B_VF = B_KE + NSK;
-  static constexpr int B_VE = B_VF + NSV;
-  static constexpr int B_SF = B_VE + NSV;  // 2: S_t ready
+  static constexpr int B_VF = B_KF + NS;
+  static constexpr int B_E = B_VF + NS;
+  static constexpr int B_SF = B_E + NS;    // 2: S_t ready
   static constexpr int B_PF = B_SF + 2;    // 2: P_t ready (128 arrivals)
   static constexpr int B_OF = B_PF + 2;    // 2: last PV_t of an item complete
   static constexpr int B_WF = B_OF + 2;    // 2: work-item slot filled
@@ -156,23 +158,34 @@ struct WorkItem {
   int lo, hi;              // union range
 };
 
-// Item order: (batch, head) units are taken in groups of p.group_bh; inside a group the query
-// blocks go heaviest first across the whole group (longest-processing-time order), then the
-// next group.  A group's K/V stays L2-resident while its items run, and the last items of the
-// launch are the lightest ones, which keeps the tail short.
+// Item order.  Causal: (batch, head) units are taken in groups of p.group_bh; inside a group
+// the query blocks go heaviest first across the whole group (longest-processing-time order),
+// then the next group — a group's K/V stays L2-resident while its items run, and the last
+// items of the launch are the lightest ones, which keeps the tail short.  Otherwise every query
+// block costs the same and the query block is the innermost index, so the items that read the
+// same (unit, key split) K/V run side by side and share it through L2.
 __device__ __forceinline__ WorkItem decode_item(const FwdParams& p, int idx, int BN) {
   WorkItem w;
-  const int BH = p.B * p.H;
-  const int per_unit = p.n_qblk * p.splits;
-  const int grp = idx / (p.group_bh * per_unit);
-  const int g0 = grp * p.group_bh;
-  const int gsize = min(p.group_bh, BH - g0);
-  const int local = idx - g0 * per_unit;
-  const int qrank = local / (gsize * p.splits);
-  const int rem = local - qrank * gsize * p.splits;
-  const int bh = g0 + rem / p.splits;
-  w.split = rem % p.splits;
-  const int qb = p.heavy_first ? p.n_qblk - 1 - qrank : qrank;
+  int bh, qb;
+  if (p.heavy_first) {
+    const int BH = p.B * p.H;
+    const int per_unit = p.n_qblk * p.splits;
+    const int grp = idx / (p.group_bh * per_unit);
+    const int g0 = grp * p.group_bh;
+    const int gsize = min(p.group_bh, BH - g0);
+    const int local = idx - g0 * per_unit;
+    const int qrank = local / (gsize * p.splits);
+    const int rem = local - qrank * gsize * p.splits;
+    bh = g0 + rem / p.splits;
+    w.split = rem % p.splits;
+    qb = p.n_qblk - 1 - qrank;
+  } else {
+    const int per_unit = p.n_qblk * p.splits;
+    bh = idx / per_unit;
+    const int rem = idx - bh * per_unit;
+    w.split = rem / p.n_qblk;
+    qb = rem % p.n_qblk;
+  }
   w.h = bh % p.H;
   w.b = bh / p.H;
   w.q0 = qb * 256;
@@ -199,12 +212,12 @@ __device__ __forceinline__ WorkItem decode_item(const FwdParams& p, int idx, int
   return w;
 }
 
-template <int D, bool kBF16, int NSK, int NSV>
+template <int D, bool kBF16, int NS>
 __global__ void __launch_bounds__(384, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                           const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
-  using C = Sm100Cfg<D, NSK, NSV>;
+  using C = Sm100Cfg<D, NS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -221,13 +234,10 @@ __global__ void __launch_bounds__(384, 1)
   if (threadIdx.x == 0) {
     mbar_init(BAR(C::B_QF), 1);
     mbar_init(BAR(C::B_QE), 1);
-    for (int i = 0; i < NSK; ++i) {
+    for (int i = 0; i < NS; ++i) {
       mbar_init(BAR(C::B_KF + i), 1);
-      mbar_init(BAR(C::B_KE + i), 1);
-    }
-    for (int i = 0; i < NSV; ++i) {
       mbar_init(BAR(C::B_VF + i), 1);
-      mbar_init(BAR(C::B_VE + i), 1);
+      mbar_init(BAR(C::B_E + i), 1);
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(BAR(C::B_SF + t), 1);
@@ -260,7 +270,7 @@ __global__ void __launch_bounds__(384, 1)
         tma_prefetch_desc(&tm_k);
         tma_prefetch_desc(&tm_v);
         const uint32_t sQ = sbase + C::OFF_Q, sK = sbase + C::OFF_K, sV = sbase + C::OFF_V;
-        int fk = 0, fv = 0, n_q = 0;  // K / V fills and Q loads issued so far by this CTA
+        int fk = 0, n_q = 0;  // key-tile fills (K and V) and Q loads issued so far
         bool ok = true;
         for (int item = 0; ok; ++item) {
           const int slot = item & 1;
@@ -300,8 +310,8 @@ __global__ void __launch_bounds__(384, 1)
           }
           ++n_q;
           for (int j = w.lo; j < w.hi && ok; ++j) {
-            const int ks = fk % NSK;
-            if (fk >= NSK) ok = mbar_wait(BAR(C::B_KE + ks), ((fk / NSK) - 1) & 1, wctx, kSiteProducer);
+            const int ks = fk % NS;
+            if (fk >= NS) ok = mbar_wait(BAR(C::B_E + ks), ((fk / NS) - 1) & 1, wctx, kSiteProducer);
             if (!ok) break;
             mbar_arrive_expect_tx(BAR(C::B_KF + ks), C::KV_TILE);
             tma_coords(p.ck, j * C::BN, w.h, w.b, c1, c2, c3);
@@ -309,26 +319,22 @@ __global__ void __launch_bounds__(384, 1)
             for (int kb = 0; kb < C::KB; ++kb)
               tma_load_4d(sK + ks * C::KV_TILE + kb * C::BOX_KV, &tm_k, BAR(C::B_KF + ks),
                           kb * 64, c1, c2, c3);
-            ++fk;
-            const int vs = fv % NSV;
-            if (fv >= NSV) ok = mbar_wait(BAR(C::B_VE + vs), ((fv / NSV) - 1) & 1, wctx, kSiteProducer);
-            if (!ok) break;
-            mbar_arrive_expect_tx(BAR(C::B_VF + vs), C::KV_TILE);
+            mbar_arrive_expect_tx(BAR(C::B_VF + ks), C::KV_TILE);
             tma_coords(p.cv, j * C::BN, w.h, w.b, c1, c2, c3);
 #pragma unroll
             for (int kb = 0; kb < C::KB; ++kb)
-              tma_load_4d(sV + vs * C::KV_TILE + kb * C::BOX_KV, &tm_v, BAR(C::B_VF + vs),
+              tma_load_4d(sV + ks * C::KV_TILE + kb * C::BOX_KV, &tm_v, BAR(C::B_VF + ks),
                           kb * 64, c1, c2, c3);
-            ++fv;
+            ++fk;
           }
         }
         if (!ok) {
           // Abort: let every load already issued land before the CTA releases its smem.
           if (n_q > 0) mbar_wait_drain(BAR(C::B_QF), (n_q - 1) & 1, p.status, p.timeout_ns);
-          for (int f = (fk > NSK ? fk - NSK : 0); f < fk; ++f)
-            mbar_wait_drain(BAR(C::B_KF + f % NSK), (f / NSK) & 1, p.status, p.timeout_ns);
-          for (int f = (fv > NSV ? fv - NSV : 0); f < fv; ++f)
-            mbar_wait_drain(BAR(C::B_VF + f % NSV), (f / NSV) & 1, p.status, p.timeout_ns);
+          for (int f = (fk > NS ? fk - NS : 0); f < fk; ++f) {
+            mbar_wait_drain(BAR(C::B_KF + f % NS), (f / NS) & 1, p.status, p.timeout_ns);
+            mbar_wait_drain(BAR(C::B_VF + f % NS), (f / NS) & 1, p.status, p.timeout_ns);
+          }
         }
       }
     } else if (warp == 8) {
@@ -370,7 +376,7 @@ __global__ void __launch_bounds__(384, 1)
         };
         using T0 = std::integral_constant<int, 0>;
         using T1 = std::integral_constant<int, 1>;
-        int ck = 0, cv = 0, n_q = 0, pc0 = 0, pc1 = 0;  // consumed K / V fills, Q loads, P waits
+        int c = 0, n_q = 0, pc0 = 0, pc1 = 0;  // consumed key-tile fills, Q loads, P waits
         int trace_f = 0;
         bool ok = true;
         for (int item = 0; ok; ++item) {
@@ -383,6 +389,7 @@ __global__ void __launch_bounds__(384, 1)
           const WorkItem w = decode_item(p, idx, C::BN);
           if (w.hi <= w.lo) continue;
           // One tile's share of key tile j: PV_t(j) once P_t(j) is ready, then QK_t(j+1).
+          // The K of key tile j+1 is fill c+1 (ring stage ksn).
           auto tile_step = [&](auto tile, int j, int vs, bool has_next, int ksn,
                                bool& k_ready) -> bool {
             constexpr int T = decltype(tile)::value;
@@ -398,7 +405,7 @@ __global__ void __launch_bounds__(384, 1)
             }
             if (has_next && j + 1 >= tlo && j + 1 < thi) {
               if (!k_ready) {
-                if (!mbar_wait(BAR(C::B_KF + ksn), (ck / NSK) & 1, wctx, kSiteMmaLoad))
+                if (!mbar_wait(BAR(C::B_KF + ksn), ((c + 1) / NS) & 1, wctx, kSiteMmaLoad))
                   return false;
                 tc_fence_after();
                 k_ready = true;
@@ -411,45 +418,42 @@ __global__ void __launch_bounds__(384, 1)
           };
 
           ok = mbar_wait(BAR(C::B_QF), n_q & 1, wctx, kSiteMmaLoad);
-          if (ok) ok = mbar_wait(BAR(C::B_KF + ck % NSK), (ck / NSK) & 1, wctx, kSiteMmaLoad);
+          if (ok) ok = mbar_wait(BAR(C::B_KF + c % NS), (c / NS) & 1, wctx, kSiteMmaLoad);
           if (!ok) break;
           ++n_q;
           tc_fence_after();
           if (w.lo >= w.lo0 && w.lo < w.hi0) {
-            issue_qk(T0{}, ck % NSK);
+            issue_qk(T0{}, c % NS);
             tc_commit(BAR(C::B_SF + 0));
           }
           if (w.lo >= w.lo1 && w.lo < w.hi1) {
-            issue_qk(T1{}, ck % NSK);
+            issue_qk(T1{}, c % NS);
             tc_commit(BAR(C::B_SF + 1));
           }
-          tc_commit(BAR(C::B_KE + ck % NSK));
-          ++ck;
           if (w.hi - w.lo == 1) tc_commit(BAR(C::B_QE));  // every QK of this item is issued
-          for (int j = w.lo; j < w.hi && ok; ++j, ++trace_f) {
-            const int vs = cv % NSV;
+          for (int j = w.lo; j < w.hi && ok; ++j, ++trace_f, ++c) {
+            const int vs = c % NS;
             const bool has_next = j + 1 < w.hi;
-            const int ksn = ck % NSK;
+            const int ksn = (c + 1) % NS;
             bool k_ready = false;
             MLXP_TR(true, 2, trace_f, 0);
-            ok = mbar_wait(BAR(C::B_VF + vs), (cv / NSV) & 1, wctx, kSiteMmaLoad);
+            ok = mbar_wait(BAR(C::B_VF + vs), (c / NS) & 1, wctx, kSiteMmaLoad);
             MLXP_TR(true, 2, trace_f, 1);
             if (!ok) break;
             tc_fence_after();
             ok = tile_step(T0{}, j, vs, has_next, ksn, k_ready);
             if (ok) ok = tile_step(T1{}, j, vs, has_next, ksn, k_ready);
             if (!ok) break;
-            tc_commit(BAR(C::B_VE + vs));
-            ++cv;
-            if (has_next) {
-              if (!k_ready) {  // neither tile uses this key tile: consume it anyway
-                ok = mbar_wait(BAR(C::B_KF + ksn), (ck / NSK) & 1, wctx, kSiteMmaLoad);
-                if (!ok) break;
-              }
-              tc_commit(BAR(C::B_KE + ksn));
-              ++ck;
-              if (j + 2 == w.hi) tc_commit(BAR(C::B_QE));  // the item's last QKs are issued
+            if (has_next && !k_ready) {
+              // neither tile uses key tile j+1: its K load must still land before the stage
+              // is released at the end of the next iteration
+              ok = mbar_wait(BAR(C::B_KF + ksn), ((c + 1) / NS) & 1, wctx, kSiteMmaLoad);
+              if (!ok) break;
             }
+            // K(j) (last read by QK(j), one iteration ago) and V(j) (read by PV(j) above) are
+            // consumed: release their stage with a single commit.
+            tc_commit(BAR(C::B_E + vs));
+            if (j + 2 == w.hi) tc_commit(BAR(C::B_QE));  // the item's last QKs are issued
           }
         }
         // Every MMA issued by this thread must finish before TMEM/smem are released.

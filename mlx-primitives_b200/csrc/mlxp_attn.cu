@@ -232,28 +232,20 @@ int validate(const Problem& pr) {
 constexpr int kBM2 = 256;  // query rows per tensor-core CTA
 constexpr int kBN = 128;   // keys per tensor-core tile
 
-// Key-range split count: splits exist only to fill the machine when there are few CTAs.
+// Key-range split count for non-causal, unwindowed problems (the only ones with long uniform
+// key ranges).  The persistent kernel schedules items dynamically, so splits serve two ends:
+// enough items to fill every SM several times, and items short enough (<= 64 key tiles) that
+// the end-of-launch tail stays small; each split costs one fp32 partial write and read in
+// the LSE merge, so no more splits than that.
 int choose_splits(const Problem& pr, int sms) {
   const long long n_qblk = (pr.Sq + kBM2 - 1) / kBM2;
   const long long base = n_qblk * pr.B * pr.H;
   const long long kv_tiles = (pr.Skv + kBN - 1) / kBN;
   if (base <= 0 || kv_tiles < 16 || pr.causal || pr.wl >= 0 || pr.wr >= 0) return 1;
-  auto eff = [&](long long s) {
-    const long long ctas = base * s;
-    const long long waves = (ctas + sms - 1) / sms;
-    return double(ctas) / double(waves * sms);
-  };
-  int best = 1;
-  double best_eff = eff(1);
-  for (int s = 2; s <= 16; ++s) {
-    if (kv_tiles / s < 8) break;
-    const double e = eff(s);
-    if (e > best_eff + 0.05) {
-      best = s;
-      best_eff = e;
-    }
-  }
-  return best;
+  int s = 1;
+  while (s < 32 && ((kv_tiles + s - 1) / s > 64 || base * s < 4LL * sms) && kv_tiles / (2 * s) >= 8)
+    s *= 2;
+  return s;
 }
 
 size_t split_workspace(const Problem& pr, int splits) {
@@ -286,13 +278,12 @@ int noalloc_scratch(void** out) {
 
 template <int D, bool BF16>
 struct TcKernel {
-  static constexpr int NSK = (D == 128) ? 2 : 3;
-  static constexpr int NSV = (D == 128) ? 2 : 3;
-  using Cfg = Sm100Cfg<D, NSK, NSV>;
+  static constexpr int NS = (D == 128) ? 2 : 3;  // K/V ring stages
+  using Cfg = Sm100Cfg<D, NS>;
   static constexpr unsigned kBit = 1u << ((D == 128 ? 0 : 1) + (BF16 ? 0 : 2));
   static int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                     const FwdParams& p, cudaStream_t stream) {
-    auto kern = attn_fwd_sm100_kernel<D, BF16, NSK, NSV>;
+    auto kern = attn_fwd_sm100_kernel<D, BF16, NS>;
     if (int rc = ensure_smem_attr(kern, Cfg::SMEM_ALLOC, kBit)) return rc;
     const long long items = (long long)p.n_qblk * p.B * p.H * p.splits;
     if (items <= 0) return MLXP_OK;
