@@ -504,8 +504,38 @@ __global__ void __launch_bounds__(384, 1)
         if (!ok) break;
         MLXP_TR(wq == 0 && lane == 0, t, it, 1);
         tc_fence_after();
-        // S row -> registers in two halves: masking the first half overlaps the second
-        // half's TMEM read.
+        // Boundary tiles (rare) are masked in TMEM first, by a small rolled loop over 32-column
+        // chunks, so that the unrolled register path below carries no masking code.  Per warp,
+        // a chunk that is admissible for all 32 rows is left alone, one that is masked for all
+        // of them is overwritten with -inf without being read, and only a straddling chunk is
+        // read, masked element-wise and written back.
+        {
+          const long long c0 = (long long)j * C::BN;
+          if (!tile_is_full(p.mask, r0, r1, c0, c0 + C::BN)) {
+            int c_lo, c_hi;
+            row_col_interval(p.mask, qrow, c0, C::BN, c_lo, c_hi);
+            bool stored = false;
+#pragma unroll 1
+            for (int k = 0; k < C::BN / 32; ++k) {
+              const int lo = c_lo - 32 * k, hi = c_hi - 32 * k;
+              if (__all_sync(0xffffffffu, lo <= 0 && hi >= 31)) continue;
+              uint32_t r[32];
+              if (__all_sync(0xffffffffu, hi < 0 || lo > 31)) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) r[i] = 0xff800000u;
+              } else {
+                tmem_ld_x32(tS + 32 * k, r);
+                tmem_wait_ld();
+                reg_fence(r);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) r[i] = (i < lo || i > hi) ? 0xff800000u : r[i];
+              }
+              tmem_st_x32(tS + 32 * k, r);
+              stored = true;
+            }
+            if (stored) tmem_wait_st();
+          }
+        }
         float s[128];
         {
           uint32_t ra[32], rb[32];
@@ -521,14 +551,6 @@ __global__ void __launch_bounds__(384, 1)
           }
           tmem_ld_x32(tS + 64, ra);
           tmem_ld_x32(tS + 96, rb);
-          const long long c0 = (long long)j * C::BN;
-          const bool full = tile_is_full(p.mask, r0, r1, c0, c0 + C::BN);
-          int c_lo = 0, c_hi = C::BN - 1;
-          if (!full) {
-            row_col_interval(p.mask, qrow, c0, C::BN, c_lo, c_hi);
-#pragma unroll
-            for (int c = 0; c < 64; ++c) s[c] = (c < c_lo || c > c_hi) ? -INFINITY : s[c];
-          }
           tmem_wait_ld();
           reg_fence(ra);
           reg_fence(rb);
@@ -536,10 +558,6 @@ __global__ void __launch_bounds__(384, 1)
           for (int c = 0; c < 32; ++c) {
             s[64 + c] = __uint_as_float(ra[c]);
             s[96 + c] = __uint_as_float(rb[c]);
-          }
-          if (!full) {
-#pragma unroll
-            for (int c = 64; c < 128; ++c) s[c] = (c < c_lo || c > c_hi) ? -INFINITY : s[c];
           }
         }
         // row max: 3-input max, four independent chains
@@ -594,7 +612,7 @@ __global__ void __launch_bounds__(384, 1)
         if (it > 0 && __any_sync(0xffffffffu, resc)) {
           // O_t holds PV_t(j-1) (complete: it was issued before QK_t(j), whose commit we
           // saw); PV_t(j) is not issued before the arrive below, so it sees the rescaled O.
-#pragma unroll
+#pragma unroll 1
           for (int c = 0; c < D / 32; ++c) {
             uint32_t ov[32];
             tmem_ld_x32(tO + c * 32, ov);
@@ -631,7 +649,7 @@ __global__ void __launch_bounds__(384, 1)
       if (has_rows && p.lse != nullptr)
         p.lse[(long long)w.split * p.lse_split + ((long long)w.b * p.H + w.h) * p.Sq + qrow] =
             lse_v;
-#pragma unroll
+#pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         uint32_t ov[32];
         if (n_it > 0) {

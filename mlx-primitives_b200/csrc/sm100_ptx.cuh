@@ -114,6 +114,16 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* map, uint3
       : "memory");
 }
 
+// 4-D tiled prefetch of one box into L2 (no shared memory, no completion): a hint that warms
+// L2 for a load issued later.  Same coordinate rules as tma_load_4d.
+__device__ __forceinline__ void tma_prefetch_l2_4d(const void* map, int c0, int c1, int c2,
+                                                   int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+
 // ------------------------------------------------------------------------------------------
 // TMEM allocation and tcgen05 fences
 // ------------------------------------------------------------------------------------------
