@@ -13,6 +13,11 @@
 
 #include <cstdint>
 
+#ifndef __CUDACC__  // plain C++ (host-side checks of the mask arithmetic)
+#define __host__
+#define __device__
+#endif
+
 namespace mlxp {
 
 struct MaskSpec {
@@ -77,6 +82,36 @@ __host__ __device__ inline bool tile_is_full(const MaskSpec& m, long long r0, lo
   if (m.wl >= 0 && qmax - kmin > m.wl) return false;
   if (m.wr >= 0 && kmax - qmin > m.wr) return false;
   return true;
+}
+
+// floor(a / b) and ceil(a / b) for b > 0 and any sign of a.
+__host__ __device__ inline long long floor_div(long long a, long long b) {
+  return a >= 0 ? a / b : -((-a + b - 1) / b);
+}
+__host__ __device__ inline long long ceil_div(long long a, long long b) { return -floor_div(-a, b); }
+
+// The key tiles j (width BN) with tile_is_full(m, r0, r1, j*BN, j*BN + BN) form one contiguous
+// range [flo, fhi) (empty: flo == fhi): the interior of the causal/window band, cut at Skv.
+// Computed once per query tile so the per-key-tile test is two integer compares.
+__host__ __device__ inline void full_tile_range(const MaskSpec& m, long long r0, long long r1,
+                                                int BN, int& flo, int& fhi) {
+  const long long qmin = r0 + m.q_off, qmax = r1 - 1 + m.q_off;
+  long long lo = 0, hi = m.Skv / BN;
+  if (m.causal) {  // (j+1)*BN - 1 + kv_off <= qmin
+    const long long h = floor_div(qmin - m.kv_off + 1, BN);
+    if (h < hi) hi = h;
+  }
+  if (m.wr >= 0) {  // (j+1)*BN - 1 + kv_off - qmin <= wr
+    const long long h = floor_div(qmin + m.wr - m.kv_off + 1, BN);
+    if (h < hi) hi = h;
+  }
+  if (m.wl >= 0) {  // qmax - (j*BN + kv_off) <= wl
+    const long long l = ceil_div(qmax - m.wl - m.kv_off, BN);
+    if (l > lo) lo = l;
+  }
+  if (hi < lo) hi = lo;
+  flo = (int)lo;
+  fhi = (int)hi;
 }
 
 // Admissible columns [c_lo, c_hi] (inclusive, tile-local, clamped to [-1, BN]) of the tile

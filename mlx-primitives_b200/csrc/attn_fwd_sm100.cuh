@@ -122,12 +122,14 @@ enum : int {
 
 // Of every 8 column pairs of a score row, this many are exponentiated with exp2_poly2 (FMA pipe)
 // and the rest with ex2.approx (MUFU): splits the per-row exp2 work between the two units.
-// head_dim 64 has half the MMA work per score, so more of its exponentials go to the FMA pipe.
+// head_dim 64 has half the MMA work per score, so some of its exponentials go to the FMA pipe;
+// for head_dim 128 the measured optimum is MUFU only (the polynomial's extra instructions cost
+// more than the MUFU time they save).
 #ifndef MLXP_POLY_D64
-#define MLXP_POLY_D64 3
+#define MLXP_POLY_D64 2
 #endif
 #ifndef MLXP_POLY_D128
-#define MLXP_POLY_D128 2
+#define MLXP_POLY_D128 0
 #endif
 template <int D>
 constexpr int kPolyPerOct = (D == 64) ? MLXP_POLY_D64 : MLXP_POLY_D128;
@@ -494,6 +496,8 @@ __global__ void __launch_bounds__(384, 1)
       const int qrow = w.q0 + t * 128 + row;
       const long long r0 = w.q0 + t * 128;
       const long long r1 = (r0 + 128 < p.Sq) ? r0 + 128 : p.Sq;
+      int flo = 0, fhi = 0;  // key tiles that need no mask
+      if (r1 > r0) full_tile_range(p.mask, r0, r1, C::BN, flo, fhi);
       float m = -INFINITY, l = 0.f;
 
       for (int it = 0; it < thi - tlo; ++it, ++n_s) {
@@ -510,8 +514,8 @@ __global__ void __launch_bounds__(384, 1)
         // of them is overwritten with -inf without being read, and only a straddling chunk is
         // read, masked element-wise and written back.
         {
-          const long long c0 = (long long)j * C::BN;
-          if (!tile_is_full(p.mask, r0, r1, c0, c0 + C::BN)) {
+          if (j < flo || j >= fhi) {
+            const long long c0 = (long long)j * C::BN;
             int c_lo, c_hi;
             row_col_interval(p.mask, qrow, c0, C::BN, c_lo, c_hi);
             bool stored = false;
@@ -536,6 +540,7 @@ __global__ void __launch_bounds__(384, 1)
             if (stored) tmem_wait_st();
           }
         }
+        MLXP_TR(wq == 0 && lane == 0, t, it, 5);
         float s[128];
         {
           uint32_t ra[32], rb[32];
@@ -641,6 +646,7 @@ __global__ void __launch_bounds__(384, 1)
         ++n_o;
         tc_fence_after();
       }
+      MLXP_TR(wq == 0 && lane == 0 && n_it > 0, t, n_it - 1, 6);
       // A row that never saw an admissible key keeps m = -inf: it is empty (O = 0, LSE = -inf)
       // even though the polynomial exp2 leaves ~2^-125 per masked element in l.
       const bool valid = n_it > 0 && l > 0.f && m != -INFINITY;
@@ -689,6 +695,7 @@ __global__ void __launch_bounds__(384, 1)
           }
         }
       }
+      MLXP_TR(wq == 0 && lane == 0 && n_it > 0, t, n_it - 1, 7);
 #if MLXP_TRACE
       if (t == 1 && wq == 0 && lane == 0 && idx < 8192)
         g_mlxp_cta_trace[idx * 4 + 1] = (long long)global_timer_ns();
