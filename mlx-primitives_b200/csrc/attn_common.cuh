@@ -145,15 +145,16 @@ struct FwdParams {
   int tiles_per_split;  // key tiles per split (splits > 1)
   int heavy_first;      // order query blocks by descending work (causal)
   int group_bh;         // (batch, head) units per scheduling group (see decode_item)
-  // output: normal (dtype, normalised) or fp32 (normalised, for merges)
+  // Output, written through the O tensor map: normal (dtype, normalised) or fp32 (normalised,
+  // for merges).  Key split s of batch b is stored at batch coordinate s * o_split_b + b (the
+  // split workspace is [split][B][H][Sq][D], i.e. o_split_b = B; 0 without splits).
   int out_f32;
-  void* o;
-  long long o_sb, o_sh, o_ss, o_split;  // element strides; o_split = stride between splits
+  int o_split_b;
   float* lse;                           // [split][B][H][Sq] contiguous, nullable unless out_f32
   long long lse_split;
   float scale_log2;     // softmax scale * log2(e)
   MaskSpec mask;
-  TmaCoordMap cq, ck, cv;
+  TmaCoordMap cq, ck, cv, co;
   int* status;
   unsigned long long timeout_ns;
   // Persistent scheduling: [next item, CTAs finished].  Zero at launch; the last CTA to finish

@@ -73,7 +73,11 @@ struct Sm100Cfg {
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + 2 * Q_TILE;
   static constexpr int OFF_V = OFF_K + NS * KV_TILE;
-  static constexpr int OFF_BAR = OFF_V + NS * KV_TILE;
+  // Epilogue staging: one 128-row x 128-byte box (16 KB, 128-byte swizzle) per Q tile, from
+  // which O leaves through TMA stores (64 bf16/fp16 or 32 fp32 columns per box).
+  static constexpr int STAGE_BYTES = BM * 128;
+  static constexpr int OFF_STAGE = OFF_V + NS * KV_TILE;
+  static constexpr int OFF_BAR = OFF_STAGE + 2 * STAGE_BYTES;
   // barrier indices
   static constexpr int B_QF = 0;           // Q loaded
   static constexpr int B_QE = 1;           // Q buffer free (last QK of the item done)
@@ -218,7 +222,8 @@ template <int D, bool kBF16, int NS>
 __global__ void __launch_bounds__(384, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                           const __grid_constant__ CUtensorMap tm_k,
-                          const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
+                          const __grid_constant__ CUtensorMap tm_v,
+                          const __grid_constant__ CUtensorMap tm_o, const FwdParams p) {
   using C = Sm100Cfg<D, NS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -271,17 +276,20 @@ __global__ void __launch_bounds__(384, 1)
         tma_prefetch_desc(&tm_q);
         tma_prefetch_desc(&tm_k);
         tma_prefetch_desc(&tm_v);
+        tma_prefetch_desc(&tm_o);
         const uint32_t sQ = sbase + C::OFF_Q, sK = sbase + C::OFF_K, sV = sbase + C::OFF_V;
         int fk = 0, n_q = 0;  // key-tile fills (K and V) and Q loads issued so far
         bool ok = true;
         for (int item = 0; ok; ++item) {
           const int slot = item & 1;
+          MLXP_TR(true, 3, item, 0);
           if (item >= 2) {
             ok = mbar_wait(BAR(C::B_WE + slot), ((item >> 1) - 1) & 1, wctx, kSiteWork);
             if (!ok) break;
           }
           const int idx = (int)atomicAdd(p.work_counter, 1u);
           work_slot[slot] = idx;
+          MLXP_TR(true, 3, item, 1);
           mbar_arrive(BAR(C::B_WF + slot));  // release: the slot write is visible to waiters
           if (idx >= n_items) break;
           const WorkItem w = decode_item(p, idx, C::BN);
@@ -300,6 +308,7 @@ __global__ void __launch_bounds__(384, 1)
             ok = mbar_wait(BAR(C::B_QE), (n_q - 1) & 1, wctx, kSiteProducer);
             if (!ok) break;
           }
+          MLXP_TR(true, 3, item, 2);
           const bool a0 = w.hi0 > w.lo0, a1 = w.hi1 > w.lo1;
           mbar_arrive_expect_tx(BAR(C::B_QF), (a0 + a1) * C::Q_TILE);
           for (int t = 0; t < 2; ++t) {
@@ -327,6 +336,8 @@ __global__ void __launch_bounds__(384, 1)
             for (int kb = 0; kb < C::KB; ++kb)
               tma_load_4d(sV + ks * C::KV_TILE + kb * C::BOX_KV, &tm_v, BAR(C::B_VF + ks),
                           kb * 64, c1, c2, c3);
+            MLXP_TR(j == w.lo, 3, item, 3);
+            MLXP_TR(j == w.hi - 1, 3, item, 4);
             ++fk;
           }
         }
@@ -420,7 +431,9 @@ __global__ void __launch_bounds__(384, 1)
           };
 
           ok = mbar_wait(BAR(C::B_QF), n_q & 1, wctx, kSiteMmaLoad);
+          MLXP_TR(true, 2, trace_f, 6);
           if (ok) ok = mbar_wait(BAR(C::B_KF + c % NS), (c / NS) & 1, wctx, kSiteMmaLoad);
+          MLXP_TR(true, 2, trace_f, 7);
           if (!ok) break;
           ++n_q;
           tc_fence_after();
@@ -486,7 +499,7 @@ __global__ void __launch_bounds__(384, 1)
     for (int item = 0; ok; ++item) {
       const int slot = item & 1;
       ok = mbar_wait(BAR(C::B_WF + slot), (item >> 1) & 1, wctx, kSiteWork);
-      ok = __all_sync(0xffffffffu, ok);
+      ok = named_bar_and(1 + t, 128, ok);  // the tile's warps leave the item loop together
       if (!ok) break;
       const int idx = work_slot[slot];
       mbar_arrive(BAR(C::B_WE + slot));
@@ -634,6 +647,10 @@ __global__ void __launch_bounds__(384, 1)
         MLXP_TR(wq == 0 && lane == 0, t, it, 4);
         l = l * alpha + ((acc0.x + acc1.x) + (acc0.y + acc1.y));
       }
+      // The 128 threads of the tile go on together or not at all: a wait that gave up in one
+      // warp must not leave the others at the epilogue's barriers.  (A warp that left the loop
+      // early raised the abort flag, so the others' waits return at once.)
+      ok = named_bar_and(1 + t, 128, ok);
       if (!ok) break;
 
       // ------------------------------------ epilogue ------------------------------------
@@ -641,7 +658,7 @@ __global__ void __launch_bounds__(384, 1)
       const int n_it = thi - tlo;
       if (n_it > 0) {
         ok = mbar_wait(BAR(C::B_OF + t), n_o & 1, wctx, kSiteSoftmaxO);
-        ok = __all_sync(0xffffffffu, ok);
+        ok = named_bar_and(1 + t, 128, ok);
         if (!ok) break;
         ++n_o;
         tc_fence_after();
@@ -655,42 +672,64 @@ __global__ void __launch_bounds__(384, 1)
       if (has_rows && p.lse != nullptr)
         p.lse[(long long)w.split * p.lse_split + ((long long)w.b * p.H + w.h) * p.Sq + qrow] =
             lse_v;
+      // O leaves through the tile's staging box: each thread writes its row (128-byte swizzle:
+      // 16-byte chunk k of row r at chunk k ^ (r % 8), which spreads a warp's writes over all
+      // banks), then one thread stores the box with TMA, which writes whole lines of O (rows
+      // past Sq are clipped by the tensor map).  A box is 64 bf16/fp16 or 32 fp32 columns, so
+      // one 32-column TMEM chunk fills half a box (bf16/fp16) or a whole one (fp32).
+      {
+        const uint32_t stage = sbase + C::OFF_STAGE + t * C::STAGE_BYTES;
+        const uint32_t row_base = stage + (uint32_t)row * 128u;
+        const uint32_t sw = (uint32_t)(row & 7);
+        const bool elected = (wq == 0 && lane == 0);
+        const bool f32 = p.out_f32 != 0;
+        int c1, c2, c3;
+        tma_coords(p.co, w.q0 + t * 128, w.h, w.split * p.o_split_b + w.b, c1, c2, c3);
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t ov[32];
-        if (n_it > 0) {
-          tmem_ld_x32(tO + c * 32, ov);
-          tmem_wait_ld();
-          reg_fence(ov);
-        } else {
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t ov[32];
+          if (n_it > 0) {
+            tmem_ld_x32(tO + c * 32, ov);
+            tmem_wait_ld();
+            reg_fence(ov);
+          } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) ov[i] = 0u;
-        }
-        if (has_rows) {
-          const long long off = (long long)w.split * p.o_split + (long long)w.b * p.o_sb +
-                                (long long)w.h * p.o_sh + (long long)qrow * p.o_ss + c * 32;
-          if (p.out_f32) {
-            float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.o) + off);
+            for (int i = 0; i < 32; ++i) ov[i] = 0u;
+          }
+          if (f32 || !(c & 1)) {
+            // the previous store from this box has finished reading it
+            if (elected) bulk_wait_group_read0();
+            named_bar_sync(1 + t, 128);
+          }
+          if (f32) {
 #pragma unroll
             for (int i = 0; i < 8; ++i)
-              dst[i] = make_float4(__uint_as_float(ov[4 * i]) * inv_l,
-                                   __uint_as_float(ov[4 * i + 1]) * inv_l,
-                                   __uint_as_float(ov[4 * i + 2]) * inv_l,
-                                   __uint_as_float(ov[4 * i + 3]) * inv_l);
+              st_shared_v4(row_base + ((((uint32_t)i) ^ sw) << 4),
+                           __float_as_uint(__uint_as_float(ov[4 * i]) * inv_l),
+                           __float_as_uint(__uint_as_float(ov[4 * i + 1]) * inv_l),
+                           __float_as_uint(__uint_as_float(ov[4 * i + 2]) * inv_l),
+                           __float_as_uint(__uint_as_float(ov[4 * i + 3]) * inv_l));
           } else {
-            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.o) + off);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              uint4 v4;
-              v4.x = pack2<kBF16>(__uint_as_float(ov[8 * i + 0]) * inv_l,
-                                  __uint_as_float(ov[8 * i + 1]) * inv_l);
-              v4.y = pack2<kBF16>(__uint_as_float(ov[8 * i + 2]) * inv_l,
-                                  __uint_as_float(ov[8 * i + 3]) * inv_l);
-              v4.z = pack2<kBF16>(__uint_as_float(ov[8 * i + 4]) * inv_l,
-                                  __uint_as_float(ov[8 * i + 5]) * inv_l);
-              v4.w = pack2<kBF16>(__uint_as_float(ov[8 * i + 6]) * inv_l,
-                                  __uint_as_float(ov[8 * i + 7]) * inv_l);
-              dst[i] = v4;
+              const uint32_t k = (uint32_t)((c & 1) * 4 + i);
+              st_shared_v4(row_base + ((k ^ sw) << 4),
+                           pack2<kBF16>(__uint_as_float(ov[8 * i + 0]) * inv_l,
+                                        __uint_as_float(ov[8 * i + 1]) * inv_l),
+                           pack2<kBF16>(__uint_as_float(ov[8 * i + 2]) * inv_l,
+                                        __uint_as_float(ov[8 * i + 3]) * inv_l),
+                           pack2<kBF16>(__uint_as_float(ov[8 * i + 4]) * inv_l,
+                                        __uint_as_float(ov[8 * i + 5]) * inv_l),
+                           pack2<kBF16>(__uint_as_float(ov[8 * i + 6]) * inv_l,
+                                        __uint_as_float(ov[8 * i + 7]) * inv_l));
+            }
+          }
+          if (f32 || (c & 1)) {
+            fence_proxy_async_smem();
+            named_bar_sync(1 + t, 128);
+            if (elected) {
+              tma_store_4d(&tm_o, stage, f32 ? c * 32 : (c >> 1) * 64, c1, c2, c3);
+              bulk_commit_group();
             }
           }
         }
@@ -701,6 +740,8 @@ __global__ void __launch_bounds__(384, 1)
         g_mlxp_cta_trace[idx * 4 + 1] = (long long)global_timer_ns();
 #endif
     }
+    // every TMA store of O has completed before the CTA (and its staging smem) goes away
+    if (wq == 0 && lane == 0) bulk_wait_group0();
     tc_fence_before();
     __syncthreads();  // teardown barrier (pairs with the control warpgroup's)
     // The last CTA to finish resets the launch's work counter for the next launch.

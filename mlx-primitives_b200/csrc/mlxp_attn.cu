@@ -131,11 +131,10 @@ int get_encode_fn() {
 // whatever the layout (BHSD: s,h,b; BSHD: h,s,b); size-1 and stride-0 (broadcast) dims are
 // given coordinate 0.  The box lands in shared memory as box_rows rows of 128 bytes, 128-byte
 // swizzled, for every layout.
-int make_tmap(const void* ptr, bool bf16, int64_t B, int64_t H, int64_t S, int64_t D,
-              const int64_t st[4], int box_rows, const char* name, CUtensorMap* map,
-              TmaCoordMap* cm) {
+int make_tmap(const void* ptr, CUtensorMapDataType dt, int es, int64_t B, int64_t H, int64_t S,
+              int64_t D, const int64_t st[4], int box_rows, int box_cols, const char* name,
+              CUtensorMap* map, TmaCoordMap* cm) {
   if (int rc = get_encode_fn()) return rc;
-  const int es = 2;
   if (reinterpret_cast<uintptr_t>(ptr) % 16)
     return fail(MLXP_ERR_INVALID, "%s: base address must be 16-byte aligned", name);
   if (st[3] != 1) return fail(MLXP_ERR_INVALID, "%s: head_dim stride must be 1", name);
@@ -175,12 +174,11 @@ int make_tmap(const void* ptr, bool bf16, int64_t B, int64_t H, int64_t S, int64
                         (cuuint64_t)dims[2].size};
   cuuint64_t gstride[3] = {(cuuint64_t)(dims[0].stride * es), (cuuint64_t)(dims[1].stride * es),
                            (cuuint64_t)(dims[2].stride * es)};
-  cuuint32_t box[4] = {64, 1, 1, 1};
+  cuuint32_t box[4] = {(cuuint32_t)box_cols, 1, 1, 1};
   for (int i = 0; i < 3; ++i)
     if (dims[i].which == 0) box[1 + i] = box_rows;
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = g_encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                        4, const_cast<void*>(ptr), gdim, gstride, box, estr,
+  CUresult r = g_encode(map, dt, 4, const_cast<void*>(ptr), gdim, gstride, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
@@ -282,7 +280,7 @@ struct TcKernel {
   using Cfg = Sm100Cfg<D, NS>;
   static constexpr unsigned kBit = 1u << ((D == 128 ? 0 : 1) + (BF16 ? 0 : 2));
   static int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                    const FwdParams& p, cudaStream_t stream) {
+                    const CUtensorMap& mo, const FwdParams& p, cudaStream_t stream) {
     auto kern = attn_fwd_sm100_kernel<D, BF16, NS>;
     if (int rc = ensure_smem_attr(kern, Cfg::SMEM_ALLOC, kBit)) return rc;
     const long long items = (long long)p.n_qblk * p.B * p.H * p.splits;
@@ -290,7 +288,7 @@ struct TcKernel {
     int sms = 0;
     if (int rc = device_info(nullptr, &sms)) return rc;
     const long long grid = std::min<long long>(items, sms);  // persistent: one CTA per SM
-    kern<<<(unsigned)grid, Cfg::THREADS, Cfg::SMEM_ALLOC, stream>>>(mq, mk, mv, p);
+    kern<<<(unsigned)grid, Cfg::THREADS, Cfg::SMEM_ALLOC, stream>>>(mq, mk, mv, mo, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
       cudaFuncAttributes fa{};
@@ -306,11 +304,11 @@ struct TcKernel {
 };
 
 int launch_tc(int D, bool bf16, const CUtensorMap& mq, const CUtensorMap& mk,
-              const CUtensorMap& mv, const FwdParams& p, cudaStream_t s) {
-  if (D == 128) return bf16 ? TcKernel<128, true>::launch(mq, mk, mv, p, s)
-                            : TcKernel<128, false>::launch(mq, mk, mv, p, s);
-  return bf16 ? TcKernel<64, true>::launch(mq, mk, mv, p, s)
-              : TcKernel<64, false>::launch(mq, mk, mv, p, s);
+              const CUtensorMap& mv, const CUtensorMap& mo, const FwdParams& p, cudaStream_t s) {
+  if (D == 128) return bf16 ? TcKernel<128, true>::launch(mq, mk, mv, mo, p, s)
+                            : TcKernel<128, false>::launch(mq, mk, mv, mo, p, s);
+  return bf16 ? TcKernel<64, true>::launch(mq, mk, mv, mo, p, s)
+              : TcKernel<64, false>::launch(mq, mk, mv, mo, p, s);
 }
 
 template <int D>
@@ -430,9 +428,14 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
   const bool bf16 = pr.dtype == MLXP_DTYPE_BF16;
   CUtensorMap mq, mk, mv;
   FwdParams p{};
-  if (int rc = make_tmap(q, bf16, pr.B, pr.H, pr.Sq, pr.D, qs, 128, "q", &mq, &p.cq)) return rc;
-  if (int rc = make_tmap(k, bf16, pr.B, pr.H, pr.Skv, pr.D, ks, kBN, "k", &mk, &p.ck)) return rc;
-  if (int rc = make_tmap(v, bf16, pr.B, pr.H, pr.Skv, pr.D, vs, kBN, "v", &mv, &p.cv)) return rc;
+  const CUtensorMapDataType dt16 =
+      bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  if (int rc = make_tmap(q, dt16, 2, pr.B, pr.H, pr.Sq, pr.D, qs, 128, 64, "q", &mq, &p.cq))
+    return rc;
+  if (int rc = make_tmap(k, dt16, 2, pr.B, pr.H, pr.Skv, pr.D, ks, kBN, 64, "k", &mk, &p.ck))
+    return rc;
+  if (int rc = make_tmap(v, dt16, 2, pr.B, pr.H, pr.Skv, pr.D, vs, kBN, 64, "v", &mv, &p.cv))
+    return rc;
 
   int splits = 1;
   if (!out_f32) {
@@ -467,16 +470,20 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
     p.work_counter = g_counter_ptr[dev] + 2 * slot;
   }
 
+  // O is written through a tensor map: 128-row boxes of 128 bytes (64 bf16/fp16 or 32 fp32
+  // columns).  The output was validated above (16-byte aligned base, 16-byte strides).
+  CUtensorMap mo;
   if (splits == 1) {
     p.out_f32 = out_f32 ? 1 : 0;
-    p.o = o;
-    p.o_sb = os[0];
-    p.o_sh = os[1];
-    p.o_ss = os[2];
-    p.o_split = 0;
+    p.o_split_b = 0;
     p.lse = lse;
     p.lse_split = 0;
-    return launch_tc((int)pr.D, bf16, mq, mk, mv, p, stream);
+    if (int rc = out_f32 ? make_tmap(o, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, pr.B, pr.H, pr.Sq,
+                                     pr.D, os, 128, 32, "o", &mo, &p.co)
+                         : make_tmap(o, dt16, 2, pr.B, pr.H, pr.Sq, pr.D, os, 128, 64, "o", &mo,
+                                     &p.co))
+      return rc;
+    return launch_tc((int)pr.D, bf16, mq, mk, mv, mo, p, stream);
   }
   const size_t need = split_workspace(pr, splits);
   if (ws == nullptr || ws_bytes < need)
@@ -489,14 +496,16 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
   float* lse_parts = reinterpret_cast<float*>(static_cast<char*>(ws) +
                                               ((size_t)splits * rows * pr.D * 4 + 255) / 256 * 256);
   p.out_f32 = 1;
-  p.o = o_parts;
-  p.o_sb = pr.H * pr.Sq * pr.D;
-  p.o_sh = pr.Sq * pr.D;
-  p.o_ss = pr.D;
-  p.o_split = rows * pr.D;
+  p.o_split_b = (int)pr.B;  // [split][B][H][Sq][D]: split s of batch b is batch s * B + b
   p.lse = lse_parts;
   p.lse_split = rows;
-  if (int rc = launch_tc((int)pr.D, bf16, mq, mk, mv, p, stream)) return rc;
+  {
+    const int64_t ws_st[4] = {pr.H * pr.Sq * pr.D, pr.Sq * pr.D, pr.D, 1};
+    if (int rc = make_tmap(o_parts, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (int64_t)splits * pr.B,
+                           pr.H, pr.Sq, pr.D, ws_st, 128, 32, "split workspace", &mo, &p.co))
+      return rc;
+  }
+  if (int rc = launch_tc((int)pr.D, bf16, mq, mk, mv, mo, p, stream)) return rc;
   return merge_dispatch(o_parts, lse_parts, splits, o, lse, pr, os, stream);
 }
 
