@@ -38,6 +38,11 @@ for _p in (REPO, REPO / "mlx-primitives_b200"):
 
 METRIC = "attention fwd TFLOPS/GPU and % of BF16 tensor peak at 1/2/4/8 B200"
 
+# DRAM bytes (read + write) of one attention-kernel launch at N=1, from one ncu capture of the
+# same command (profiles/attn_fwd_sm100_c2_full.md, profiles/attn_fwd_sm100_c4_full.md);
+# null where no capture of that configuration has been summarised.
+NCU_TRAFFIC_BYTES = {"c2": 522.9e6, "c4": 2.409e9}
+
 CONFIGS = {
     "c1": dict(workload="flash_attention fp32 BSHD causal (config 1)", api="flash", dtype="fp32",
                layout="BSHD", B=2, H=12, S=1024, Skv=1024, D=64, causal=True, window=-1, std=1.0),
@@ -380,7 +385,10 @@ def main():
             "pct_of_bf16_peak": 100.0 * (value / world) / peak,
             "roofline": {
                 "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak, "traffic": None,
+                "frac": achieved / peak,
+                # per-rank launches are the N=1 workload except for the ring
+                "traffic": NCU_TRAFFIC_BYTES.get(args.config) if c["api"] != "ring" else None,
+                "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + write.sum)",
                 "kernel": "attn_fwd_fp32_kernel" if c["dtype"] == "fp32" else "attn_fwd_sm100_kernel",
                 "peak_source": f"{peak_src}: bf16_tflops (burst); sustained {peak_sus}",
                 "algorithmic_flops_per_launch": flops,
