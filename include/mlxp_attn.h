@@ -180,6 +180,44 @@ int mlxp_set_wait_timeout_ns(uint64_t ns);
  */
 int mlxp_selftest_wait_timeout(uint64_t timeout_ns, void* cuda_stream);
 
+/*
+ * Sequence-parallel causal attention over NCCL (one process per GPU), for callers that are not
+ * Python; the reference is single-device, so these have no counterpart there: they are the
+ * ring entry points the long-context configuration needs (the Python API runs the same schedule
+ * over torch.distributed in mlx_primitives/attention/ring.py).
+ *
+ * The full sequence of S = nranks * S_local tokens is cut into 2 * nranks chunks of
+ * C = S_local / 2; rank r holds chunks r and 2*nranks-1-r of Q, K and V back to back (zig-zag)
+ * and receives the same chunks of O.  NCCL is loaded at run time (libnccl.so.2); when it cannot
+ * be, these return MLXP_ERR_NCCL.  Each rank calls them on its own device (the current device at
+ * mlxp_ring_init).  A rank that never joins leaves the others blocked inside NCCL, as with any
+ * NCCL collective: a process-level watchdog is the caller's.
+ */
+
+/* A new 128-byte NCCL unique id: created on one rank and shared with the others out of band. */
+int mlxp_ring_unique_id(void* id_out);
+
+/* Joins the ring of nranks ranks as `rank`; *comm receives the handle. */
+int mlxp_ring_init(const void* nccl_unique_id, int nranks, int rank, void** comm);
+
+/* Bytes of device workspace mlxp_ring_attn_fwd needs (0 for an invalid shape). */
+size_t mlxp_ring_workspace_size(int dtype, int64_t B, int64_t H, int64_t S_local, int64_t D);
+
+/*
+ * o = causal softmax(scale * q k^T) v of this rank's zig-zag shard, against the whole
+ * sequence.  q, k, v, o: [B][H][S_local][D] with element strides (BHSD or BSHD), bf16/fp16,
+ * D in {64, 128}, S_local even.  Collective: every rank calls it with the same shapes, in the
+ * same order.  workspace: >= mlxp_ring_workspace_size bytes, 256-byte aligned.
+ */
+int mlxp_ring_attn_fwd(void* comm, const void* q, const void* k, const void* v, void* o,
+                       int dtype, int64_t B, int64_t H, int64_t S_local, int64_t D,
+                       const int64_t q_strides[4], const int64_t k_strides[4],
+                       const int64_t v_strides[4], const int64_t o_strides[4], float scale,
+                       void* workspace, size_t ws_bytes, void* cuda_stream);
+
+/* Leaves the ring and frees the handle (NULL is a no-op). */
+int mlxp_ring_destroy(void* comm);
+
 #ifdef __cplusplus
 }
 #endif

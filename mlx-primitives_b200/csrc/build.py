@@ -35,7 +35,7 @@ def command(debug: bool = False, verbose_ptxas: bool = False) -> list[str]:
     cmd = [nvcc_path(), *ARCH, "-std=c++17", "-O3", "-lineinfo", "-shared",
            "-Xcompiler", "-fPIC", "-cudart", "shared",
            "-Xlinker", "-rpath,/usr/local/cuda/lib64",
-           "-I", str(INCLUDE), "-o", str(OUT)]
+           "-I", str(INCLUDE), "-o", str(OUT), "-ldl"]
     if debug:
         cmd += ["-DMLXP_DEBUG_CHECKS=1"]
     if verbose_ptxas:

@@ -709,3 +709,6 @@ int mlxp_selftest_wait_timeout(uint64_t timeout_ns, void* cuda_stream) {
 }
 
 }  // extern "C"
+
+// The NCCL ring (mlxp_ring_*): drives the entry points above.
+#include "ring_nccl.cuh"

@@ -59,6 +59,13 @@ _SIGNATURES = {
     "mlxp_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
     "mlxp_set_wait_timeout_ns": (ctypes.c_int, [ctypes.c_uint64]),
     "mlxp_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_uint64, _p]),
+    "mlxp_ring_unique_id": (ctypes.c_int, [_p]),
+    "mlxp_ring_init": (ctypes.c_int, [_p, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_p)]),
+    "mlxp_ring_workspace_size": (ctypes.c_size_t, [ctypes.c_int, _i64, _i64, _i64, _i64]),
+    "mlxp_ring_attn_fwd": (ctypes.c_int, [
+        _p, _p, _p, _p, _p, ctypes.c_int, _i64, _i64, _i64, _i64,
+        _i64x4, _i64x4, _i64x4, _i64x4, ctypes.c_float, _p, ctypes.c_size_t, _p]),
+    "mlxp_ring_destroy": (ctypes.c_int, [_p]),
 }
 
 EXPORTED_SYMBOLS = tuple(_SIGNATURES)

@@ -27,7 +27,7 @@ import torch.distributed as dist
 from .. import _lib
 
 __all__ = ["zigzag_chunks", "zigzag_shard", "zigzag_unshard", "ring_flash_attention",
-           "CudaRingBackend"]
+           "CudaRingBackend", "nccl_unique_id", "NcclRing"]
 
 
 def zigzag_chunks(world: int, rank: int) -> Tuple[int, int]:
@@ -144,3 +144,64 @@ def ring_flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     backend.finish(o_acc[0], out[:, :, :C])
     backend.finish(o_acc[1], out[:, :, C:])
     return out
+
+
+def nccl_unique_id() -> bytes:
+    """A new 128-byte NCCL unique id for NcclRing (create on one rank, share with the others)."""
+    buf = ctypes.create_string_buffer(128)
+    _lib.check(_lib.lib().mlxp_ring_unique_id(ctypes.cast(buf, ctypes.c_void_p)),
+               "mlxp_ring_unique_id")
+    return buf.raw
+
+
+class NcclRing:
+    """The same zig-zag ring run entirely by the C library (mlxp_ring_*) over its own NCCL
+    communicator, without torch.distributed: the path a non-Python caller of the C ABI takes.
+    Construct on every rank with the same id and nranks, on the rank's current CUDA device."""
+
+    def __init__(self, unique_id: bytes, nranks: int, rank: int):
+        if len(unique_id) != 128:
+            raise ValueError("an NCCL unique id is 128 bytes")
+        self._comm = ctypes.c_void_p()
+        idbuf = ctypes.create_string_buffer(unique_id, 128)
+        _lib.check(_lib.lib().mlxp_ring_init(ctypes.cast(idbuf, ctypes.c_void_p), nranks, rank,
+                                             ctypes.byref(self._comm)), "mlxp_ring_init")
+        self.nranks, self.rank = nranks, rank
+
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                scale: Optional[float] = None, layout: str = "BHSD") -> torch.Tensor:
+        """Causal attention of this rank's zig-zag shard (q, k, v: [B, H, S_local, D] for
+        BHSD or [B, S_local, H, D] for BSHD); returns this rank's shard of the output."""
+        if self._comm.value is None:
+            raise RuntimeError("the ring has been closed")
+        if q.shape != k.shape or k.shape != v.shape or q.ndim != 4:
+            raise ValueError("q, k, v must be 4-D shards of equal shape")
+        if layout == "BHSD":
+            B, H, S, D = q.shape
+        else:
+            B, S, H, D = q.shape
+        if scale is None:
+            scale = 1.0 / math.sqrt(D)
+        L = _lib.lib()
+        code = _lib.DTYPE_CODES[q.dtype]
+        nbytes = L.mlxp_ring_workspace_size(code, B, H, S, D)
+        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
+        out = torch.empty_like(q)
+        rc = L.mlxp_ring_attn_fwd(self._comm, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                  out.data_ptr(), code, B, H, S, D, _lib.strides4(q, layout),
+                                  _lib.strides4(k, layout), _lib.strides4(v, layout),
+                                  _lib.strides4(out, layout), ctypes.c_float(scale),
+                                  ws.data_ptr(), nbytes, _lib.stream_handle(q.device))
+        _lib.check(rc, "mlxp_ring_attn_fwd")
+        return out
+
+    def close(self) -> None:
+        if self._comm.value is not None:
+            _lib.check(_lib.lib().mlxp_ring_destroy(self._comm), "mlxp_ring_destroy")
+            self._comm = ctypes.c_void_p()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
