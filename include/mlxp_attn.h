@@ -87,6 +87,22 @@ int mlxp_attn_fwd(const void* q, const void* k, const void* v, void* o, float* l
                   int64_t kv_splits, void* workspace, size_t ws_bytes, void* cuda_stream);
 
 /*
+ * Grouped-query / multi-query attention: as mlxp_attn_fwd, with H_kv K/V heads shared by the H
+ * query heads (H % H_kv == 0; query head h reads K/V head h / (H / H_kv), the head repetition of
+ * the reference's gqa_attention and mqa_attention).  k and v are [B][H_kv][Skv][D] through their
+ * strides.  The workspace is the same as mlxp_attn_fwd's for the query shape.
+ * Replaces: mlx_primitives/attention/grouped_query.py:195-261 (gqa_attention),
+ *           mlx_primitives/attention/multi_query.py:161-225 (mqa_attention).
+ */
+int mlxp_attn_fwd_gqa(const void* q, const void* k, const void* v, void* o, float* lse,
+                      int dtype, int64_t B, int64_t H, int64_t H_kv, int64_t Sq, int64_t Skv,
+                      int64_t D, const int64_t q_strides[4], const int64_t k_strides[4],
+                      const int64_t v_strides[4], const int64_t o_strides[4], float scale,
+                      int causal, int64_t window_left, int64_t window_right, int64_t q_pos_offset,
+                      int64_t kv_pos_offset, int64_t kv_splits, void* workspace, size_t ws_bytes,
+                      void* cuda_stream);
+
+/*
  * Bytes of workspace mlxp_attn_fwd needs for these arguments (0 when no split is used).
  * kv_splits as for mlxp_attn_fwd (0 = the automatic choice mlxp_attn_fwd would make).
  * Replaces the reference's implicit MLX allocation of intermediate arrays (chunked.py:142-166).

@@ -145,6 +145,7 @@ struct FwdParams {
   int tiles_per_split;  // key tiles per split (splits > 1)
   int heavy_first;      // order query blocks by descending work (causal)
   int group_bh;         // (batch, head) units per scheduling group (see decode_item)
+  int kv_group;         // query heads per K/V head (grouped / multi-query attention; 1 = MHA)
   // Output, written through the O tensor map: normal (dtype, normalised) or fp32 (normalised,
   // for merges).  Key split s of batch b is stored at batch coordinate s * o_split_b + b (the
   // split workspace is [split][B][H][Sq][D], i.e. o_split_b = B; 0 without splits).
@@ -165,6 +166,7 @@ struct FwdParams {
 // Parameters of the CUDA-core fp32 kernel (plain pointers and strides).
 struct FwdParamsF32 {
   int B, H, Sq, Skv;
+  int kv_group;  // query heads per K/V head (1 = MHA)
   const float* q;
   const float* k;
   const float* v;

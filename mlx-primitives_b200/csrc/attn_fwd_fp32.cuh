@@ -52,8 +52,9 @@ __global__ void __launch_bounds__(256) attn_fwd_fp32_kernel(const FwdParamsF32 p
   const int q0 = qb * C::BM;
 
   const float* qg = p.q + (long long)b * p.q_sb + (long long)h * p.q_sh;
-  const float* kg = p.k + (long long)b * p.k_sb + (long long)h * p.k_sh;
-  const float* vg = p.v + (long long)b * p.v_sb + (long long)h * p.v_sh;
+  const int hk = h / p.kv_group;  // K/V head of this query head
+  const float* kg = p.k + (long long)b * p.k_sb + (long long)hk * p.k_sh;
+  const float* vg = p.v + (long long)b * p.v_sb + (long long)hk * p.v_sh;
 
   // Q tile -> smem (rows past Sq are zero)
   for (int i = tid; i < C::BM * (D / 4); i += 256) {

@@ -325,13 +325,13 @@ __global__ void __launch_bounds__(384, 1)
             if (fk >= NS) ok = mbar_wait(BAR(C::B_E + ks), ((fk / NS) - 1) & 1, wctx, kSiteProducer);
             if (!ok) break;
             mbar_arrive_expect_tx(BAR(C::B_KF + ks), C::KV_TILE);
-            tma_coords(p.ck, j * C::BN, w.h, w.b, c1, c2, c3);
+            tma_coords(p.ck, j * C::BN, w.h / p.kv_group, w.b, c1, c2, c3);
 #pragma unroll
             for (int kb = 0; kb < C::KB; ++kb)
               tma_load_4d(sK + ks * C::KV_TILE + kb * C::BOX_KV, &tm_k, BAR(C::B_KF + ks),
                           kb * 64, c1, c2, c3);
             mbar_arrive_expect_tx(BAR(C::B_VF + ks), C::KV_TILE);
-            tma_coords(p.cv, j * C::BN, w.h, w.b, c1, c2, c3);
+            tma_coords(p.cv, j * C::BN, w.h / p.kv_group, w.b, c1, c2, c3);
 #pragma unroll
             for (int kb = 0; kb < C::KB; ++kb)
               tma_load_4d(sV + ks * C::KV_TILE + kb * C::BOX_KV, &tm_v, BAR(C::B_VF + ks),

@@ -198,6 +198,8 @@ struct Problem {
   int64_t B, H, Sq, Skv, D;
   int causal;
   int64_t wl, wr, qoff, kvoff;
+  int64_t Hkv = 0;  // K/V heads (grouped / multi-query attention); 0 = H
+  int64_t kv_heads() const { return Hkv ? Hkv : H; }
 };
 
 MaskSpec mask_of(const Problem& pr) {
@@ -213,6 +215,9 @@ int validate(const Problem& pr) {
   if (pr.Sq > (1ll << 30) || pr.Skv > (1ll << 30) || pr.B * pr.H > (1ll << 24))
     return fail(MLXP_ERR_INVALID, "shape too large");
   if (pr.wl < -1 || pr.wr < -1) return fail(MLXP_ERR_INVALID, "window must be >= 0 or -1");
+  if (pr.kv_heads() < 1 || pr.H % pr.kv_heads())
+    return fail(MLXP_ERR_INVALID, "num_heads (%lld) must be divisible by num_kv_heads (%lld)",
+                (long long)pr.H, (long long)pr.kv_heads());
   if (pr.dtype == MLXP_DTYPE_BF16 || pr.dtype == MLXP_DTYPE_FP16) {
     if (pr.D != 64 && pr.D != 128)
       return fail(MLXP_ERR_UNSUPPORTED, "bf16/fp16 attention supports head_dim 64 and 128, got %lld",
@@ -405,6 +410,7 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
     FwdParamsF32 p{};
     p.B = (int)pr.B;
     p.H = (int)pr.H;
+    p.kv_group = (int)(pr.H / pr.kv_heads());
     p.Sq = (int)pr.Sq;
     p.Skv = (int)pr.Skv;
     p.q = (const float*)q;
@@ -432,10 +438,13 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
       bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   if (int rc = make_tmap(q, dt16, 2, pr.B, pr.H, pr.Sq, pr.D, qs, 128, 64, "q", &mq, &p.cq))
     return rc;
-  if (int rc = make_tmap(k, dt16, 2, pr.B, pr.H, pr.Skv, pr.D, ks, kBN, 64, "k", &mk, &p.ck))
+  if (int rc = make_tmap(k, dt16, 2, pr.B, pr.kv_heads(), pr.Skv, pr.D, ks, kBN, 64, "k", &mk,
+                         &p.ck))
     return rc;
-  if (int rc = make_tmap(v, dt16, 2, pr.B, pr.H, pr.Skv, pr.D, vs, kBN, 64, "v", &mv, &p.cv))
+  if (int rc = make_tmap(v, dt16, 2, pr.B, pr.kv_heads(), pr.Skv, pr.D, vs, kBN, 64, "v", &mv,
+                         &p.cv))
     return rc;
+  p.kv_group = (int)(pr.H / pr.kv_heads());
 
   int splits = 1;
   if (!out_f32) {
@@ -529,6 +538,21 @@ int mlxp_attn_fwd(const void* q, const void* k, const void* v, void* o, float* l
                   void* cuda_stream) {
   Problem pr{dtype, B, H, Sq, Skv, D, causal ? 1 : 0, window_left, window_right, q_pos_offset,
              kv_pos_offset};
+  return attn_fwd_impl(q, k, v, o, lse, pr, q_strides, k_strides, v_strides, o_strides, scale,
+                       kv_splits, workspace, ws_bytes, false,
+                       static_cast<cudaStream_t>(cuda_stream));
+}
+
+int mlxp_attn_fwd_gqa(const void* q, const void* k, const void* v, void* o, float* lse,
+                      int dtype, int64_t B, int64_t H, int64_t H_kv, int64_t Sq, int64_t Skv,
+                      int64_t D, const int64_t q_strides[4], const int64_t k_strides[4],
+                      const int64_t v_strides[4], const int64_t o_strides[4], float scale,
+                      int causal, int64_t window_left, int64_t window_right, int64_t q_pos_offset,
+                      int64_t kv_pos_offset, int64_t kv_splits, void* workspace, size_t ws_bytes,
+                      void* cuda_stream) {
+  Problem pr{dtype, B, H, Sq, Skv, D, causal ? 1 : 0, window_left, window_right, q_pos_offset,
+             kv_pos_offset, H_kv};
+  if (H_kv < 1) return fail(MLXP_ERR_INVALID, "num_kv_heads must be >= 1");
   return attn_fwd_impl(q, k, v, o, lse, pr, q_strides, k_strides, v_strides, o_strides, scale,
                        kv_splits, workspace, ws_bytes, false,
                        static_cast<cudaStream_t>(cuda_stream));

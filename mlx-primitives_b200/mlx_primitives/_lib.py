@@ -42,6 +42,10 @@ _SIGNATURES = {
         _p, _p, _p, _p, _p, ctypes.c_int, _i64, _i64, _i64, _i64, _i64,
         _i64x4, _i64x4, _i64x4, _i64x4, ctypes.c_float, ctypes.c_int, _i64, _i64, _i64, _i64,
         _i64, _p, ctypes.c_size_t, _p]),
+    "mlxp_attn_fwd_gqa": (ctypes.c_int, [
+        _p, _p, _p, _p, _p, ctypes.c_int, _i64, _i64, _i64, _i64, _i64, _i64,
+        _i64x4, _i64x4, _i64x4, _i64x4, ctypes.c_float, ctypes.c_int, _i64, _i64, _i64, _i64,
+        _i64, _p, ctypes.c_size_t, _p]),
     "mlxp_attn_workspace_size": (ctypes.c_size_t, [
         ctypes.c_int, _i64, _i64, _i64, _i64, _i64, ctypes.c_int, _i64, _i64, _i64, _i64, _i64]),
     "mlxp_attn_fwd_split_noalloc": (ctypes.c_int, [

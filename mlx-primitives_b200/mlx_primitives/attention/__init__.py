@@ -1,12 +1,15 @@
 """Attention forward path of mlx_primitives, rebuilt for B200 (sm_100a).
 
 The public names match mlx_primitives/attention/__init__.py of the reference for the attention
-kernels: flash, sliding-window and chunked cross-attention, plus the sequence-parallel ring
-pass that runs the causal long-context case over several GPUs.
+kernels: flash, sliding-window and chunked cross-attention, grouped-query and multi-query
+attention, plus the sequence-parallel ring pass that runs the causal long-context case over
+several GPUs.
 """
 
 from .chunked import ChunkedCrossAttention, chunked_cross_attention, estimate_memory_savings
 from .flash import FlashAttention, flash_attention, get_optimal_flash_config
+from .grouped_query import GroupedQueryAttention, gqa_attention
+from .multi_query import MultiQueryAttention, mqa_attention
 from .sliding_window import (SlidingWindowAttention, create_sliding_window_mask,
                              sliding_window_attention)
 
@@ -20,4 +23,8 @@ __all__ = [
     "chunked_cross_attention",
     "ChunkedCrossAttention",
     "estimate_memory_savings",
+    "GroupedQueryAttention",
+    "gqa_attention",
+    "MultiQueryAttention",
+    "mqa_attention",
 ]

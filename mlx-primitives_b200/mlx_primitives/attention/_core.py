@@ -62,7 +62,9 @@ def attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, layo
         raise ValueError("q, k and v must be on the same device")
 
     B, H, Sq, D = _dims(q, layout)
-    _, _, Skv, _ = _dims(k, layout)
+    _, Hkv, Skv, _ = _dims(k, layout)
+    if Hkv != H and (Hkv < 1 or H % Hkv):
+        raise ValueError(f"num_heads ({H}) must be divisible by num_kv_heads ({Hkv})")
     Dp = _padded_head_dim(D, q.dtype)
     if Dp != D:
         # Zero-padding the head dimension leaves Q K^T unchanged; the extra output columns
@@ -81,15 +83,21 @@ def attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, layo
         ws_bytes = L.mlxp_attn_workspace_size(dt, B, H, Sq, Skv, Dp, int(causal), window_left,
                                               window_right, q_offset, kv_offset, kv_splits)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
-        rc = L.mlxp_attn_fwd(
-            q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
-            lse.data_ptr() if lse is not None else None, dt, B, H, Sq, Skv, Dp,
-            _lib.strides4(q, layout), _lib.strides4(k, layout), _lib.strides4(v, layout),
-            _lib.strides4(out, layout), ctypes.c_float(scale), int(causal), window_left,
-            window_right, q_offset, kv_offset, kv_splits,
-            ws.data_ptr() if ws is not None else None, ws_bytes,
-            _lib.stream_handle(q.device))
-    _lib.check(rc, "mlxp_attn_fwd")
+        common = (_lib.strides4(q, layout), _lib.strides4(k, layout), _lib.strides4(v, layout),
+                  _lib.strides4(out, layout), ctypes.c_float(scale), int(causal), window_left,
+                  window_right, q_offset, kv_offset, kv_splits,
+                  ws.data_ptr() if ws is not None else None, ws_bytes,
+                  _lib.stream_handle(q.device))
+        lse_ptr = lse.data_ptr() if lse is not None else None
+        if Hkv == H:
+            rc = L.mlxp_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                 lse_ptr, dt, B, H, Sq, Skv, Dp, *common)
+            what = "mlxp_attn_fwd"
+        else:  # grouped-query / multi-query: H_kv K/V heads shared by the H query heads
+            rc = L.mlxp_attn_fwd_gqa(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                     lse_ptr, dt, B, H, Hkv, Sq, Skv, Dp, *common)
+            what = "mlxp_attn_fwd_gqa"
+    _lib.check(rc, what)
     if Dp != D:
         out = out[..., :D]
     if host:

@@ -179,6 +179,31 @@ def chunked_cross_attention(q, k, v, chunk_size=1024, scale=None, causal=False, 
     return from_bhsd(o, "BSHD")
 
 
+def gqa_attention(q, k, v, num_kv_groups, scale=None, mask=None, causal=False, dtype=np.float64):
+    """grouped_query.py:195-261 semantics (BSHD): K/V head j serves query heads
+    j*num_kv_groups .. (j+1)*num_kv_groups-1 (broadcast + reshape in the reference); causal
+    aligned bottom-right (triu(k = seq_kv - seq_q + 1)).  Rows with no admissible key give 0
+    (the library's convention; the reference's -inf mask would give NaN there)."""
+    if mask is not None:
+        raise NotImplementedError("custom masks are not part of the oracle")
+    q, k, v = (np.asarray(t) for t in (q, k, v))
+    if q.shape[2] != k.shape[2] * num_kv_groups:
+        raise ValueError("num_heads must equal num_kv_heads * num_kv_groups")
+    k = np.repeat(k, num_kv_groups, axis=2)
+    v = np.repeat(v, num_kv_groups, axis=2)
+    return flash_attention(q, k, v, scale=scale, causal=causal, layout="BSHD", dtype=dtype)
+
+
+def mqa_attention(q, k, v, scale=None, mask=None, causal=False, dtype=np.float64):
+    """multi_query.py:161-225 semantics: one K/V head ((B, Skv, D) or (B, Skv, 1, D)) for all
+    query heads."""
+    k, v = np.asarray(k), np.asarray(v)
+    if k.ndim == 3:
+        k, v = k[:, :, None, :], v[:, :, None, :]
+    return gqa_attention(q, k, v, np.asarray(q).shape[2], scale=scale, mask=mask, causal=causal,
+                         dtype=dtype)
+
+
 # ----------------------------------------------------------------------------------------
 # The reference's own blockwise algorithms (fp32, as MLX computes them)
 # ----------------------------------------------------------------------------------------

@@ -17,6 +17,7 @@ Metal branches (as on an MLX build without them), and records what its own code 
   chunked.py:172-203     _reference_cross_attention (Skv <= chunk_size)
   _online_softmax.py:42-176  online_softmax_merge / compute_chunk_attention
   utils/masking.py:14-66 create_causal_mask; sliding_window.py:628-656 create_sliding_window_mask
+  grouped_query.py:195-261  gqa_attention;  multi_query.py:161-225  mqa_attention
 
 Inputs come from numpy's legacy RandomState (frozen stream) through
 oracle.attention_oracle.make_qkv, so tests regenerate them bit-for-bit from the seed; only the
@@ -81,6 +82,7 @@ def _stand_in_mlx() -> types.ModuleType:
     mx.transpose = lambda x, axes=None: np.transpose(x, axes)
     mx.triu = lambda x, k=0: np.triu(x, k=k)
     mx.contiguous = np.ascontiguousarray
+    mx.broadcast_to = lambda x, shape: np.broadcast_to(x, shape)
     mx.eval = lambda *a, **k: None
 
     def softmax(x, axis=-1):
@@ -103,8 +105,15 @@ def load_reference(ref_root: Path):
     mlx = types.ModuleType("mlx")
     core = _stand_in_mlx()
     mlx.core = core
+    # mlx.nn only provides base classes for the module definitions; the functional entry points
+    # recorded below (gqa_attention, mqa_attention) do not touch it.
+    nn = types.ModuleType("mlx.nn")
+    nn.Module = type("Module", (), {"__init__": lambda self, *a, **k: None})
+    nn.Linear = lambda *a, **k: None
+    mlx.nn = nn
     sys.modules["mlx"] = mlx
     sys.modules["mlx.core"] = core
+    sys.modules["mlx.nn"] = nn
     pkg_dir = ref_root / "mlx_primitives"
     for name, sub in [("mlx_primitives", ""), ("mlx_primitives.attention", "attention"),
                       ("mlx_primitives.kernels", "kernels"), ("mlx_primitives.utils", "utils")]:
@@ -119,6 +128,8 @@ def load_reference(ref_root: Path):
     for n in ["_online_softmax", "flash", "sliding_window", "chunked"]:
         mods[n] = importlib.import_module(f"mlx_primitives.attention.{n}")
     mods["masking"] = importlib.import_module("mlx_primitives.utils.masking")
+    mods["grouped_query"] = importlib.import_module("mlx_primitives.attention.grouped_query")
+    mods["multi_query"] = importlib.import_module("mlx_primitives.attention.multi_query")
     for n in ["flash", "sliding_window", "chunked"]:
         setattr(mods[n], "_HAS_SDPA", False)
         setattr(mods[n], "_HAS_METAL", False)
@@ -191,6 +202,19 @@ def main() -> None:
          lambda q, k, v: ch.chunked_cross_attention(q, k, v, chunk_size=64, causal=True, use_metal=False))
     case("chunked_dense_short_kv", 118, (1, 30, 2, 128), (1, 100, 2, 128),
          lambda q, k, v: ch.chunked_cross_attention(q, k, v, chunk_size=1024, use_metal=False))
+
+    # grouped-query / multi-query functional forms: grouped_query.py:195-261, multi_query.py:161-225
+    gq, mq = mods["grouped_query"], mods["multi_query"]
+    case("gqa_g4_causal_d64", 120, (2, 96, 8, 64), (2, 96, 2, 64),
+         lambda q, k, v: gq.gqa_attention(q, k, v, num_kv_groups=4, causal=True))
+    case("gqa_g2_noncausal_d128", 121, (1, 70, 4, 128), (1, 90, 2, 128),
+         lambda q, k, v: gq.gqa_attention(q, k, v, num_kv_groups=2, causal=False))
+    case("gqa_g2_causal_kv_longer_d64", 122, (1, 40, 6, 64), (1, 130, 3, 64),
+         lambda q, k, v: gq.gqa_attention(q, k, v, num_kv_groups=2, scale=0.2, causal=True))
+    case("mqa_causal_d64", 123, (2, 80, 4, 64), (2, 80, 1, 64),
+         lambda q, k, v: mq.mqa_attention(q, k, v, causal=True))
+    case("mqa_3d_kv_noncausal_d128", 124, (1, 50, 3, 128), (1, 75, 1, 128),
+         lambda q, k, v: mq.mqa_attention(q, k[:, :, 0], v[:, :, 0], causal=False))
 
     # _online_softmax: merge and chunk helpers
     q, k, v = make_qkv((1, 16, 2, 64), (1, 48, 2, 64), seed=119)

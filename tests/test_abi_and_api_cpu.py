@@ -100,6 +100,22 @@ def test_flash_validation_errors():
         mp.flash_attention(_t(1, 4, 2, 8), _t(1, 4, 2, 8), _t(1, 4, 2, 8), dropout_p=0.1)
 
 
+def test_grouped_query_validation():
+    from mlx_primitives.attention import (GroupedQueryAttention, gqa_attention, mqa_attention)
+
+    with pytest.raises(ValueError, match="num_kv_heads"):
+        gqa_attention(_t(1, 4, 6, 8), _t(1, 4, 4, 8), _t(1, 4, 4, 8), num_kv_groups=2)
+    with pytest.raises(NotImplementedError, match="mask"):
+        gqa_attention(_t(1, 4, 4, 8), _t(1, 4, 2, 8), _t(1, 4, 2, 8), num_kv_groups=2,
+                      mask=_t(4, 4))
+    with pytest.raises(ValueError, match="one K/V head"):
+        mqa_attention(_t(1, 4, 4, 8), _t(1, 4, 2, 8), _t(1, 4, 2, 8))
+    with pytest.raises(ValueError, match="divisible"):
+        GroupedQueryAttention(64, 6, num_kv_heads=4)
+    m = GroupedQueryAttention(64, 8, num_kv_heads=2, causal=True)
+    assert (m.num_groups, m.head_dim) == (4, 8) and m.scale == pytest.approx(8 ** -0.5)
+
+
 def test_other_entry_points_validate():
     import mlx_primitives as mp
 

@@ -242,6 +242,11 @@ GOLDEN_CALLS = {
     "chunked_loop_causal": ("chunked", dict(chunk_size=64, causal=True)),
     "chunked_loop_q_longer_causal": ("chunked", dict(chunk_size=64, causal=True)),
     "chunked_dense_short_kv": ("chunked", dict(chunk_size=1024)),
+    "gqa_g4_causal_d64": ("gqa", dict(num_kv_groups=4, causal=True)),
+    "gqa_g2_noncausal_d128": ("gqa", dict(num_kv_groups=2, causal=False)),
+    "gqa_g2_causal_kv_longer_d64": ("gqa", dict(num_kv_groups=2, scale=0.2, causal=True)),
+    "mqa_causal_d64": ("mqa", dict(causal=True)),
+    "mqa_3d_kv_noncausal_d128": ("mqa3d", dict(causal=False)),
 }
 
 
@@ -250,6 +255,13 @@ def _call(api, mod, q, k, v, kw):
         return mod.flash_attention(q, k, v, **kw)
     if api == "swa":
         return mod.sliding_window_attention(q, k, v, **kw)
+    if api in ("gqa", "mqa", "mqa3d"):
+        m = getattr(mod, "attention", mod)  # the package keeps them in mlx_primitives.attention
+        if api == "gqa":
+            return m.gqa_attention(q, k, v, **kw)
+        if api == "mqa3d":
+            k, v = k[:, :, 0], v[:, :, 0]
+        return m.mqa_attention(q, k, v, **kw)
     return mod.chunked_cross_attention(q, k, v, **kw)
 
 

@@ -50,6 +50,13 @@ SEMANTIC = {
         lambda q, k, v: O.chunked_cross_attention(q, k, v, 64, causal=True),
         lambda q, k, v: O.chunked_cross_attention_loop(q, k, v, 64, 0.125, True)),
     "chunked_dense_short_kv": (lambda q, k, v: O.chunked_cross_attention(q, k, v, 1024), None),
+    "gqa_g4_causal_d64": (lambda q, k, v: O.gqa_attention(q, k, v, 4, causal=True), None),
+    "gqa_g2_noncausal_d128": (lambda q, k, v: O.gqa_attention(q, k, v, 2, causal=False), None),
+    "gqa_g2_causal_kv_longer_d64": (
+        lambda q, k, v: O.gqa_attention(q, k, v, 2, scale=0.2, causal=True), None),
+    "mqa_causal_d64": (lambda q, k, v: O.mqa_attention(q, k, v, causal=True), None),
+    "mqa_3d_kv_noncausal_d128": (
+        lambda q, k, v: O.mqa_attention(q, k[:, :, 0], v[:, :, 0], causal=False), None),
 }
 
 
