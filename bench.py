@@ -54,6 +54,11 @@ CONFIGS = {
     "c4": dict(workload="ChunkedCrossAttention bf16 BSHD chunk4096 (config 4)", api="chunked",
                dtype="bf16", layout="BSHD", B=8, H=16, S=512, Skv=65536, D=64, causal=False,
                window=-1, std=0.5),
+    # grouped-query variant of config 2 (32 query heads sharing 8 K/V heads), not a BASELINE
+    # config: the measurement of the gqa_attention entry point
+    "g2": dict(workload="gqa_attention bf16 BSHD causal, 32 query / 8 K/V heads", api="gqa",
+               dtype="bf16", layout="BSHD", B=4, H=32, Hkv=8, S=4096, Skv=4096, D=128,
+               causal=True, window=-1, std=1.0),
     # total work fixed: one 128K-token sequence, sequence-parallel ring over the N GPUs
     "c5": dict(workload="long-context flash_attention bf16 BHSD causal, zig-zag ring (config 5)",
                api="ring", dtype="bf16", layout="BHSD", B=1, H=32, S=131072, Skv=131072,
@@ -87,7 +92,7 @@ def config_flops(c) -> float:
 
 def config_bytes(c) -> float:
     es = 4 if c["dtype"] == "fp32" else 2
-    return es * c["B"] * c["H"] * c["D"] * (2 * c["S"] + 2 * c["Skv"])
+    return es * c["B"] * c["D"] * (2 * c["H"] * c["S"] + 2 * c.get("Hkv", c["H"]) * c["Skv"])
 
 
 def load_peaks():
@@ -233,7 +238,8 @@ def config_json(c, n):
                 "seq_len": c["S"], "head_dim": c["D"], "layout": c["layout"], "causal": True,
                 "parallelism": par, "l2": "inputs larger than L2"}
     return {"workload": c["workload"], "global_batch": c["B"] * n, "batch_per_gpu": c["B"],
-            "heads": c["H"], "seq_len": c["S"], "kv_len": c["Skv"], "head_dim": c["D"],
+            "heads": c["H"], "kv_heads": c.get("Hkv", c["H"]), "seq_len": c["S"],
+            "kv_len": c["Skv"], "head_dim": c["D"],
             "layout": c["layout"], "causal": c["causal"], "window": c["window"],
             "parallelism": f"dp{n} over (batch, head) units, no collective",
             "l2": ("inputs larger than L2" if config_bytes(c) > L2_BYTES
@@ -277,7 +283,8 @@ def main():
     dtype = torch.float32 if c["dtype"] == "fp32" else torch.bfloat16
     B, H, S, Skv, D = c["B"], c["H"], c["S"], c["Skv"], c["D"]
     shape_q = (B, H, S, D) if c["layout"] == "BHSD" else (B, S, H, D)
-    shape_kv = (B, H, Skv, D) if c["layout"] == "BHSD" else (B, Skv, H, D)
+    Hkv = c.get("Hkv", H)
+    shape_kv = (B, Hkv, Skv, D) if c["layout"] == "BHSD" else (B, Skv, Hkv, D)
     ring = c["api"] == "ring" and world > 1
     g = torch.Generator(device=dev)
     g.manual_seed(42 + (0 if c["api"] == "ring" else rank))  # the ring shares one sequence
@@ -305,6 +312,9 @@ def main():
             return mp.flash_attention(qq, kk, vv, causal=c["causal"], layout=c["layout"])
         if c["api"] == "swa":
             return mp.sliding_window_attention(qq, kk, vv, window_size=c["window"], causal=c["causal"])
+        if c["api"] == "gqa":
+            return mp.attention.gqa_attention(qq, kk, vv, num_kv_groups=H // Hkv,
+                                              causal=c["causal"])
         return mp.chunked_cross_attention(qq, kk, vv, chunk_size=4096, causal=c["causal"])
 
     if ring:  # per step and rank: partials + merges for the pairs below the diagonal, 2 casts
