@@ -531,23 +531,30 @@ __global__ void __launch_bounds__(384, 1)
             const long long c0 = (long long)j * C::BN;
             int c_lo, c_hi;
             row_col_interval(p.mask, qrow, c0, C::BN, c_lo, c_hi);
+            // the warp's extreme bounds decide each chunk's case once for all 32 rows
+            const int lo_min = __reduce_min_sync(0xffffffffu, c_lo);
+            const int lo_max = __reduce_max_sync(0xffffffffu, c_lo);
+            const int hi_min = __reduce_min_sync(0xffffffffu, c_hi);
+            const int hi_max = __reduce_max_sync(0xffffffffu, c_hi);
+            const int width = (c_hi >= c_lo) ? c_hi - c_lo + 1 : 0;  // admissible columns
             bool stored = false;
 #pragma unroll 1
             for (int k = 0; k < C::BN / 32; ++k) {
-              const int lo = c_lo - 32 * k, hi = c_hi - 32 * k;
-              if (__all_sync(0xffffffffu, lo <= 0 && hi >= 31)) continue;
-              uint32_t r[32];
-              if (__all_sync(0xffffffffu, hi < 0 || lo > 31)) {
-#pragma unroll
-                for (int i = 0; i < 32; ++i) r[i] = 0xff800000u;
+              const int k0 = 32 * k, k1 = 32 * k + 31;
+              if (lo_max <= k0 && hi_min >= k1) continue;  // admissible for every row
+              if (hi_max < k0 || lo_min > k1) {            // masked for every row
+                tmem_fill_x32(tS + k0, 0xff800000u);
               } else {
-                tmem_ld_x32(tS + 32 * k, r);
+                uint32_t r[32];
+                tmem_ld_x32(tS + k0, r);
                 tmem_wait_ld();
                 reg_fence(r);
+                const int lo = c_lo - k0;
 #pragma unroll
-                for (int i = 0; i < 32; ++i) r[i] = (i < lo || i > hi) ? 0xff800000u : r[i];
+                for (int i = 0; i < 32; ++i)  // i in [lo, lo + width) <=> (unsigned)(i - lo) < width
+                  r[i] = ((unsigned)(i - lo) < (unsigned)width) ? r[i] : 0xff800000u;
+                tmem_st_x32(tS + k0, r);
               }
-              tmem_st_x32(tS + 32 * k, r);
               stored = true;
             }
             if (stored) tmem_wait_st();
