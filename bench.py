@@ -365,7 +365,10 @@ def main():
     e2e = None
     if args.e2e_steps > 0:
         hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
-        step(hq, hk, hv)
+        # warm-up in the timed loop's own pattern (the previous result is still held while
+        # the next call runs), so the pinned-memory cache holds both result buffers
+        for _ in range(3):
+            out_host = step(hq, hk, hv)
         torch.cuda.synchronize(dev)
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -4,7 +4,8 @@ It replaces the reference's three-way dispatch (MLX SDPA -> Metal kernel -> Pyth
 mlx_primitives/attention/flash.py:172-254, sliding_window.py:288-312, chunked.py:113-126) with
 a single call into libmlxp_attn.so: bf16/fp16 inputs run the tcgen05 tensor-core kernel, fp32
 inputs the CUDA-core kernel.  Nothing here computes attention on the CPU; host tensors are
-staged through the current CUDA device and the result is copied back.
+staged through the current CUDA device (pipelined in batch chunks) and the result is copied
+back into pinned host memory.
 """
 
 from __future__ import annotations
@@ -50,13 +51,12 @@ def attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, layo
     """
     if q.dtype not in _lib.DTYPE_CODES:
         raise ValueError(f"unsupported dtype {q.dtype}; expected float32, bfloat16 or float16")
-    host = q.device.type == "cpu"
-    if host:
-        if not torch.cuda.is_available():
-            raise RuntimeError("attention requires a CUDA device (there is no CPU fallback)")
-        dev = torch.device("cuda", torch.cuda.current_device())
-        q, k, v = (t.to(dev, non_blocking=True) for t in (q, k, v))
-    elif q.device.type != "cuda":
+    if q.device.type == "cpu":
+        return _host_attention(q, k, v, layout=layout, scale=scale, causal=causal,
+                               window_left=window_left, window_right=window_right,
+                               q_offset=q_offset, kv_offset=kv_offset, kv_splits=kv_splits,
+                               return_lse=return_lse)
+    if q.device.type != "cuda":
         raise ValueError(f"tensors must be on a CUDA device (or the host), got {q.device}")
     if k.device != q.device or v.device != q.device:
         raise ValueError("q, k and v must be on the same device")
@@ -100,18 +100,75 @@ def attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, layo
     _lib.check(rc, what)
     if Dp != D:
         out = out[..., :D]
-    if host:
-        out = _to_host(out)
-        lse = _to_host(lse) if lse is not None else None
     return (out, lse) if return_lse else out
 
 
-def _to_host(t: torch.Tensor) -> torch.Tensor:
-    """Device -> pinned host copy on the current stream, then wait for it."""
-    h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
-    h.copy_(t, non_blocking=True)
-    torch.cuda.current_stream(t.device).synchronize()
-    return h
+_HOST_CHUNKS = 4
+_copy_streams = {}
+
+
+def _streams(dev: torch.device):
+    """Two copy streams per device (host-to-device, device-to-host), created once."""
+    if dev.index not in _copy_streams:
+        _copy_streams[dev.index] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+    return _copy_streams[dev.index]
+
+
+def _host_attention(q, k, v, *, layout, scale, causal, window_left, window_right, q_offset,
+                    kv_offset, kv_splits, return_lse):
+    """Host tensors: staged through the current CUDA device in batch chunks, pipelined so
+    that the copy of chunk i+1 to the device, the kernel of chunk i and the copy of chunk i-1's
+    result back run at the same time (two copy streams, the two copy engines of the GPU, and
+    the compute stream).  The result lands in pinned host memory."""
+    if not torch.cuda.is_available():
+        raise RuntimeError("attention requires a CUDA device (there is no CPU fallback)")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    B = q.shape[0]
+    kv_whole = k.shape[0] != B  # a broadcast K/V batch is copied once, whole
+    n = max(1, min(B, _HOST_CHUNKS))
+    bounds = [(B * i // n, B * (i + 1) // n) for i in range(n)]
+    cur = torch.cuda.current_stream(dev)
+    s_in, s_out = _streams(dev)
+    s_in.wait_stream(cur)
+    with torch.cuda.device(dev):
+        dq = torch.empty(q.shape, dtype=q.dtype, device=dev)
+        dk = torch.empty(k.shape, dtype=k.dtype, device=dev)
+        dv = torch.empty(v.shape, dtype=v.dtype, device=dev)
+    out_host = torch.empty(q.shape[:-1] + (v.shape[-1],), dtype=q.dtype, pin_memory=True)
+    lse_host = None
+    if return_lse:
+        _, H, Sq, _ = _dims(q, layout)
+        lse_host = torch.empty((B, H, Sq), dtype=torch.float32, pin_memory=True)
+    for t in (dq, dk, dv):
+        t.record_stream(s_in)
+    if kv_whole:
+        with torch.cuda.stream(s_in):
+            dk.copy_(k, non_blocking=True)
+            dv.copy_(v, non_blocking=True)
+    for b0, b1 in bounds:
+        with torch.cuda.stream(s_in):
+            dq[b0:b1].copy_(q[b0:b1], non_blocking=True)
+            if not kv_whole:
+                dk[b0:b1].copy_(k[b0:b1], non_blocking=True)
+                dv[b0:b1].copy_(v[b0:b1], non_blocking=True)
+        cur.wait_stream(s_in)
+        kk, vv = (dk, dv) if kv_whole else (dk[b0:b1], dv[b0:b1])
+        res = attention_forward(dq[b0:b1], kk, vv, layout=layout, scale=scale, causal=causal,
+                                window_left=window_left, window_right=window_right,
+                                q_offset=q_offset, kv_offset=kv_offset, kv_splits=kv_splits,
+                                return_lse=return_lse)
+        o, lse = res if return_lse else (res, None)
+        s_out.wait_stream(cur)
+        with torch.cuda.stream(s_out):
+            out_host[b0:b1].copy_(o, non_blocking=True)
+            if lse is not None:
+                lse_host[b0:b1].copy_(lse, non_blocking=True)
+        o.record_stream(s_out)
+        if lse is not None:
+            lse.record_stream(s_out)
+    cur.wait_stream(s_out)
+    s_out.synchronize()
+    return (out_host, lse_host) if return_lse else out_host
 
 
 def default_scale(head_dim: int) -> float:
