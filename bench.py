@@ -59,6 +59,11 @@ CONFIGS = {
     "g2": dict(workload="gqa_attention bf16 BSHD causal, 32 query / 8 K/V heads", api="gqa",
                dtype="bf16", layout="BSHD", B=4, H=32, Hkv=8, S=4096, Skv=4096, D=128,
                causal=True, window=-1, std=1.0),
+    # RoPE + attention (kernels.fused_rope_attention) on the config-2 shape, BSHD: the RoPE
+    # launch for Q and K is inside the timed step; not a BASELINE config
+    "r2": dict(workload="fused_rope_attention bf16 BSHD causal (config-2 shape)", api="frope",
+               dtype="bf16", layout="BSHD", B=4, H=32, S=4096, Skv=4096, D=128, causal=True,
+               window=-1, std=1.0),
     # total work fixed: one 128K-token sequence, sequence-parallel ring over the N GPUs
     "c5": dict(workload="long-context flash_attention bf16 BHSD causal, zig-zag ring (config 5)",
                api="ring", dtype="bf16", layout="BHSD", B=1, H=32, S=131072, Skv=131072,
@@ -273,6 +278,7 @@ def main():
     import torch.distributed as dist
 
     import mlx_primitives as mp
+    import mlx_primitives.kernels  # noqa: F401  (RoPE entry points, config r2)
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
@@ -312,6 +318,8 @@ def main():
             return mp.flash_attention(qq, kk, vv, causal=c["causal"], layout=c["layout"])
         if c["api"] == "swa":
             return mp.sliding_window_attention(qq, kk, vv, window_size=c["window"], causal=c["causal"])
+        if c["api"] == "frope":
+            return mp.kernels.fused_rope_attention(qq, kk, vv, causal=c["causal"])
         if c["api"] == "gqa":
             return mp.attention.gqa_attention(qq, kk, vv, num_kv_groups=H // Hkv,
                                               causal=c["causal"])
@@ -320,7 +328,7 @@ def main():
     if ring:  # per step and rank: partials + merges for the pairs below the diagonal, 2 casts
         launches_per_step = 2 * (2 * world) + 2
     else:
-        launches_per_step = 2 if c["api"] == "chunked" else 1
+        launches_per_step = 2 if c["api"] in ("chunked", "frope") else 1
     flush = config_bytes(c) <= L2_BYTES
     scratch = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev) if flush else None
 

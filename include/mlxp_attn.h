@@ -180,6 +180,31 @@ int mlxp_cast_output(const float* o_acc, void* o, int dtype, int64_t B, int64_t 
                      int64_t D, const int64_t o_strides[4], void* cuda_stream);
 
 /*
+ * Rotary position embedding, the half-split rotation of the reference's rope
+ * (mlx_primitives/kernels/rope.py:451-496, fast_rope :350-381): with h = D/2 and the row's
+ * position p = pos_offset + s,  y[:h] = x[:h]*cos[p] - x[h:]*sin[p],
+ * y[h:] = x[:h]*sin[p] + x[h:]*cos[p].  cos_cache/sin_cache: fp32 [n_pos][D/2] contiguous
+ * (precompute_rope_cache, rope.py:223-255); positions past n_pos are rejected.  x and y are
+ * [B][H][S][D] through their strides (y may alias x); fp32/bf16/fp16, computed in fp32.
+ */
+int mlxp_rope(const void* x, void* y, int dtype, int64_t B, int64_t H, int64_t S, int64_t D,
+              const int64_t x_strides[4], const int64_t y_strides[4], const float* cos_cache,
+              const float* sin_cache, int64_t n_pos, int64_t pos_offset, void* cuda_stream);
+
+/*
+ * RoPE of Q and K in one launch (rope.py:384-448, fast_rope_qk), with their own head counts,
+ * lengths and position offsets (grouped K/V heads, a KV cache longer than the queries).
+ * This is the rotation step of fused_rope_attention (kernels/fused_rope_attention.py:939-985),
+ * which then runs mlxp_attn_fwd on the rotated tensors.
+ */
+int mlxp_rope_qk(const void* q, const void* k, void* q_out, void* k_out, int dtype, int64_t B,
+                 int64_t Hq, int64_t Hk, int64_t Sq, int64_t Sk, int64_t D,
+                 const int64_t q_strides[4], const int64_t k_strides[4],
+                 const int64_t qo_strides[4], const int64_t ko_strides[4],
+                 const float* cos_cache, const float* sin_cache, int64_t n_pos,
+                 int64_t q_pos_offset, int64_t k_pos_offset, void* cuda_stream);
+
+/*
  * Device-side status word of the current device: 0 when every bounded wait completed,
  * otherwise MLXP_ERR_TIMEOUT | (site << 8).  Synchronises the device.  reset != 0 clears it.
  */

@@ -20,6 +20,7 @@
 #include "attn_common.cuh"
 #include "attn_fwd_fp32.cuh"
 #include "attn_fwd_sm100.cuh"
+#include "rope.cuh"
 
 namespace mlxp {
 
@@ -518,6 +519,53 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
   return merge_dispatch(o_parts, lse_parts, splits, o, lse, pr, os, stream);
 }
 
+// RoPE of one or two tensors ([B][H][S][D] in element strides) in one launch.
+int rope_launch(int dtype, int64_t D, RopeParams& rp, const int64_t* const xs[2],
+                const int64_t* const ys[2], cudaStream_t stream) {
+  if (D < 2 || (D % 2)) return fail(MLXP_ERR_INVALID, "head_dim must be even for RoPE, got %lld", (long long)D);
+  if (!rp.cosc || !rp.sinc) return fail(MLXP_ERR_INVALID, "cos/sin caches must be non-null");
+  if (dtype < 0 || dtype > 2) return fail(MLXP_ERR_INVALID, "unknown dtype %d", dtype);
+  const int es = dtype == MLXP_DTYPE_FP32 ? 4 : 2;
+  const int vec = 16 / es;
+  rp.half = (int)(D / 2);
+  bool vec_ok = (rp.half % vec) == 0 && ((rp.half * es) % 16) == 0;
+  long long total = 0;
+  for (int i = 0; i < rp.n; ++i) {
+    RopeTensor& t = rp.t[i];
+    if (!t.x || !t.y || !xs[i] || !ys[i]) return fail(MLXP_ERR_INVALID, "rope tensors must be non-null");
+    if (xs[i][3] != 1 || ys[i][3] != 1) return fail(MLXP_ERR_INVALID, "head_dim stride must be 1");
+    if (t.pos_offset < 0 || t.pos_offset + t.S > rp.n_pos)
+      return fail(MLXP_ERR_INVALID,
+                  "positions [%lld, %lld) exceed the cos/sin cache of %lld positions",
+                  (long long)t.pos_offset, (long long)(t.pos_offset + t.S), (long long)rp.n_pos);
+    for (int d = 0; d < 3; ++d) {
+      t.xs[d] = xs[i][d];
+      t.ys[d] = ys[i][d];
+      if ((xs[i][d] * es) % 16 || (ys[i][d] * es) % 16) vec_ok = false;
+    }
+    if (reinterpret_cast<uintptr_t>(t.x) % 16 || reinterpret_cast<uintptr_t>(t.y) % 16) vec_ok = false;
+    total += t.rows;
+  }
+  if (total == 0) return MLXP_OK;
+  int sms = 148;
+  if (int rc = device_info(nullptr, &sms)) return rc;
+  long long tokens = 0;  // one block per token (batch, position) at a time
+  for (int i = 0; i < rp.n; ++i) tokens += rp.t[i].H > 0 ? rp.t[i].rows / rp.t[i].H : 0;
+  const unsigned grid = (unsigned)std::max<long long>(1, std::min<long long>(tokens, 16LL * sms));
+  if (dtype == MLXP_DTYPE_BF16) {
+    if (vec_ok) rope_kernel<__nv_bfloat16, 8><<<grid, 256, 0, stream>>>(rp);
+    else rope_kernel<__nv_bfloat16, 1><<<grid, 256, 0, stream>>>(rp);
+  } else if (dtype == MLXP_DTYPE_FP16) {
+    if (vec_ok) rope_kernel<__half, 8><<<grid, 256, 0, stream>>>(rp);
+    else rope_kernel<__half, 1><<<grid, 256, 0, stream>>>(rp);
+  } else {
+    if (vec_ok) rope_kernel<float, 4><<<grid, 256, 0, stream>>>(rp);
+    else rope_kernel<float, 1><<<grid, 256, 0, stream>>>(rp);
+  }
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MLXP_OK : cuda_fail(e, "rope launch");
+}
+
 }  // namespace
 }  // namespace mlxp
 
@@ -673,6 +721,43 @@ int mlxp_cast_output(const float* o_acc, void* o, int dtype, int64_t B, int64_t 
     return fail(MLXP_ERR_INVALID, "unknown dtype %d", dtype);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? MLXP_OK : cuda_fail(e, "cast_output launch");
+}
+
+int mlxp_rope(const void* x, void* y, int dtype, int64_t B, int64_t H, int64_t S, int64_t D,
+              const int64_t x_strides[4], const int64_t y_strides[4], const float* cos_cache,
+              const float* sin_cache, int64_t n_pos, int64_t pos_offset, void* cuda_stream) {
+  if (B < 0 || H < 0 || S < 0) return fail(MLXP_ERR_INVALID, "invalid rope shape");
+  RopeParams rp{};
+  rp.n = 1;
+  rp.cosc = cos_cache;
+  rp.sinc = sin_cache;
+  rp.n_pos = n_pos;
+  rp.t[0] = RopeTensor{x, y, {0, 0, 0}, {0, 0, 0}, (int)H, (int)S, (long long)B * H * S,
+                       (long long)pos_offset};
+  const int64_t* xs[2] = {x_strides, nullptr};
+  const int64_t* ys[2] = {y_strides, nullptr};
+  return rope_launch(dtype, D, rp, xs, ys, static_cast<cudaStream_t>(cuda_stream));
+}
+
+int mlxp_rope_qk(const void* q, const void* k, void* q_out, void* k_out, int dtype, int64_t B,
+                 int64_t Hq, int64_t Hk, int64_t Sq, int64_t Sk, int64_t D,
+                 const int64_t q_strides[4], const int64_t k_strides[4],
+                 const int64_t qo_strides[4], const int64_t ko_strides[4],
+                 const float* cos_cache, const float* sin_cache, int64_t n_pos,
+                 int64_t q_pos_offset, int64_t k_pos_offset, void* cuda_stream) {
+  if (B < 0 || Hq < 0 || Hk < 0 || Sq < 0 || Sk < 0) return fail(MLXP_ERR_INVALID, "invalid rope shape");
+  RopeParams rp{};
+  rp.n = 2;
+  rp.cosc = cos_cache;
+  rp.sinc = sin_cache;
+  rp.n_pos = n_pos;
+  rp.t[0] = RopeTensor{q, q_out, {0, 0, 0}, {0, 0, 0}, (int)Hq, (int)Sq, (long long)B * Hq * Sq,
+                       (long long)q_pos_offset};
+  rp.t[1] = RopeTensor{k, k_out, {0, 0, 0}, {0, 0, 0}, (int)Hk, (int)Sk, (long long)B * Hk * Sk,
+                       (long long)k_pos_offset};
+  const int64_t* xs[2] = {q_strides, k_strides};
+  const int64_t* ys[2] = {qo_strides, ko_strides};
+  return rope_launch(dtype, D, rp, xs, ys, static_cast<cudaStream_t>(cuda_stream));
 }
 
 int mlxp_device_status(int* status_out, int reset) {

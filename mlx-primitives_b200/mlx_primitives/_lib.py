@@ -63,6 +63,11 @@ _SIGNATURES = {
     "mlxp_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
     "mlxp_set_wait_timeout_ns": (ctypes.c_int, [ctypes.c_uint64]),
     "mlxp_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_uint64, _p]),
+    "mlxp_rope": (ctypes.c_int, [_p, _p, ctypes.c_int, _i64, _i64, _i64, _i64, _i64x4, _i64x4,
+                                 _p, _p, _i64, _i64, _p]),
+    "mlxp_rope_qk": (ctypes.c_int, [_p, _p, _p, _p, ctypes.c_int, _i64, _i64, _i64, _i64, _i64,
+                                    _i64, _i64x4, _i64x4, _i64x4, _i64x4, _p, _p, _i64, _i64,
+                                    _i64, _p]),
     "mlxp_ring_unique_id": (ctypes.c_int, [_p]),
     "mlxp_ring_init": (ctypes.c_int, [_p, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_p)]),
     "mlxp_ring_workspace_size": (ctypes.c_size_t, [ctypes.c_int, _i64, _i64, _i64, _i64]),

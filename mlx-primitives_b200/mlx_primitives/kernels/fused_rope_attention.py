@@ -1,0 +1,138 @@
+"""RoPE + flash attention on B200 (drop-in for mlx_primitives/kernels/fused_rope_attention.py).
+
+``fused_rope_attention`` (fused_rope_attention.py:939-985), ``fast_fused_rope_attention``
+(:637-733) and ``FusedRoPEFlashAttention`` (:988-1080): the reference rotates Q and K with its
+RoPE kernel and then runs scaled-dot-product attention.  Here one launch rotates Q and K
+(mlxp_rope_qk, memory-bound) and the tcgen05 attention kernel runs on the rotated tensors.
+Q/K/V are (batch, seq, heads, head_dim); Q positions start at ``q_offset``, K positions at
+``kv_offset``; the causal mask is the reference's: bottom-right aligned (SDPA "causal"),
+independent of the offsets.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import torch
+from torch import nn
+
+from ..attention._core import attention_forward
+from .rope import fast_rope_qk, precompute_rope_cache
+
+__all__ = ["fused_rope_attention", "fast_fused_rope_attention", "FusedRoPEFlashAttention"]
+
+_CACHE_LIMIT = 8
+_rope_caches = {}
+
+
+def _default_cache(max_pos: int, head_dim: int, base: float, device):
+    """fp32 cos/sin tables, kept per (length, head_dim, base, device) like the reference's
+    automatic cache management, so repeated calls do not recompute them."""
+    key = (max_pos, head_dim, float(base), str(device))
+    hit = _rope_caches.get(key)
+    if hit is None:
+        if len(_rope_caches) >= _CACHE_LIMIT:
+            _rope_caches.pop(next(iter(_rope_caches)))
+        hit = _rope_caches[key] = precompute_rope_cache(max_pos, head_dim, base=base,
+                                                        device=device)
+    return hit
+
+
+def fast_fused_rope_attention(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    scale: Optional[float] = None,
+    cos_cache: Optional[torch.Tensor] = None,
+    sin_cache: Optional[torch.Tensor] = None,
+    rope_base: float = 10000.0,
+    q_offset: int = 0,
+    kv_offset: int = 0,
+    causal: bool = False,
+    use_tiled: Optional[bool] = None,
+) -> torch.Tensor:
+    """RoPE on Q and K, then attention (fused_rope_attention.py:637-733)."""
+    if q.ndim != 4:
+        raise ValueError(f"Q must be 4D (batch, seq_q, num_heads, head_dim), got {q.ndim}D")
+    if k.ndim != 4:
+        raise ValueError(f"K must be 4D (batch, seq_kv, num_heads, head_dim), got {k.ndim}D")
+    if v.ndim != 4:
+        raise ValueError(f"V must be 4D (batch, seq_kv, num_heads, head_dim), got {v.ndim}D")
+    _, seq_q, _, head_dim = q.shape
+    seq_kv = k.shape[1]
+    if head_dim % 2 != 0:
+        raise ValueError(f"head_dim must be even for RoPE, got {head_dim}")
+    if scale is None:
+        scale = 1.0 / math.sqrt(head_dim)
+    if cos_cache is None or sin_cache is None:
+        max_pos = max(seq_q + q_offset, seq_kv + kv_offset)
+        dev = q.device if q.device.type == "cuda" else torch.device(
+            "cuda", torch.cuda.current_device())
+        cos_cache, sin_cache = _default_cache(max_pos, head_dim, rope_base, dev)
+    q_rot, k_rot = fast_rope_qk(q, k, cos_cache, sin_cache, q_offset, k_offset=kv_offset)
+    return attention_forward(q_rot, k_rot, v, layout="BSHD", scale=float(scale),
+                             causal=bool(causal), q_offset=(seq_kv - seq_q) if causal else 0)
+
+
+def fused_rope_attention(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    scale: Optional[float] = None,
+    cos_cache: Optional[torch.Tensor] = None,
+    sin_cache: Optional[torch.Tensor] = None,
+    rope_base: float = 10000.0,
+    q_offset: int = 0,
+    kv_offset: int = 0,
+    causal: bool = False,
+    use_metal: bool = True,
+) -> torch.Tensor:
+    """fused_rope_attention.py:939-985 (``use_metal`` accepted for API compatibility)."""
+    return fast_fused_rope_attention(q, k, v, scale, cos_cache, sin_cache, rope_base, q_offset,
+                                     kv_offset, causal)
+
+
+class FusedRoPEFlashAttention(nn.Module):
+    """Attention module with Q/K/V/out projections, RoPE and a KV cache
+    (fused_rope_attention.py:988-1080)."""
+
+    def __init__(self, dims: int, num_heads: int, head_dim: Optional[int] = None,
+                 max_seq_len: int = 8192, rope_base: float = 10000.0, causal: bool = False,
+                 bias: bool = False):
+        super().__init__()
+        self.dims = dims
+        self.num_heads = num_heads
+        self.head_dim = head_dim or dims // num_heads
+        self.max_seq_len = max_seq_len
+        self.rope_base = rope_base
+        self.causal = causal
+        self.scale = 1.0 / math.sqrt(self.head_dim)
+        inner = self.num_heads * self.head_dim
+        self.q_proj = nn.Linear(dims, inner, bias=bias)
+        self.k_proj = nn.Linear(dims, inner, bias=bias)
+        self.v_proj = nn.Linear(dims, inner, bias=bias)
+        self.out_proj = nn.Linear(inner, dims, bias=bias)
+
+    def forward(self, queries: torch.Tensor, keys: Optional[torch.Tensor] = None,
+                values: Optional[torch.Tensor] = None,
+                cache: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+                offset: int = 0) -> Tuple[torch.Tensor, Tuple[torch.Tensor, torch.Tensor]]:
+        """(batch, seq_q, dims) -> ((batch, seq_q, dims), (k, v) cache).  As in the reference,
+        queries start at position ``offset`` and the (cached + new) keys at position 0."""
+        if keys is None:
+            keys = queries
+        if values is None:
+            values = keys
+        B, Sq, _ = queries.shape
+        Skv = keys.shape[1]
+        q = self.q_proj(queries).reshape(B, Sq, self.num_heads, self.head_dim)
+        k = self.k_proj(keys).reshape(B, Skv, self.num_heads, self.head_dim)
+        v = self.v_proj(values).reshape(B, Skv, self.num_heads, self.head_dim)
+        if cache is not None:
+            k = torch.cat([cache[0], k], dim=1)
+            v = torch.cat([cache[1], v], dim=1)
+        new_cache = (k, v)
+        out = fused_rope_attention(q, k, v, scale=self.scale, rope_base=self.rope_base,
+                                   q_offset=offset, kv_offset=0, causal=self.causal)
+        return self.out_proj(out.reshape(B, Sq, -1)), new_cache

@@ -204,6 +204,39 @@ def mqa_attention(q, k, v, scale=None, mask=None, causal=False, dtype=np.float64
                          dtype=dtype)
 
 
+def precompute_rope_cache(seq_len, head_dim, base=10000.0):
+    """kernels/rope.py:223-255: theta_i = base^(-i/(head_dim/2)) and position angles in fp32,
+    cos/sin (seq_len, head_dim // 2) in fp32."""
+    half = head_dim // 2
+    inv_freq = np.float32(base) ** (-np.arange(0, half, dtype=np.float32) / np.float32(half))
+    freqs = np.outer(np.arange(seq_len, dtype=np.float32), inv_freq.astype(np.float32))
+    return np.cos(freqs).astype(np.float32), np.sin(freqs).astype(np.float32)
+
+
+def rope(x, cos, sin, offset=0, dtype=np.float64):
+    """kernels/rope.py:477-496 (BSHD): half-split rotation at positions offset + s."""
+    x = np.asarray(x, dtype=dtype)
+    s = x.shape[1]
+    h = x.shape[-1] // 2
+    c = np.asarray(cos, dtype=dtype)[offset:offset + s][None, :, None, :]
+    sn = np.asarray(sin, dtype=dtype)[offset:offset + s][None, :, None, :]
+    x1, x2 = x[..., :h], x[..., h:]
+    return np.concatenate([x1 * c - x2 * sn, x1 * sn + x2 * c], axis=-1)
+
+
+def fused_rope_attention(q, k, v, scale=None, cos_cache=None, sin_cache=None, rope_base=10000.0,
+                         q_offset=0, kv_offset=0, causal=False, dtype=np.float64):
+    """kernels/fused_rope_attention.py:766-800 semantics: RoPE on Q (positions from q_offset)
+    and K (from kv_offset), then flash_attention (BSHD, causal bottom-right)."""
+    q, k, v = (np.asarray(t) for t in (q, k, v))
+    if cos_cache is None or sin_cache is None:
+        max_pos = max(q.shape[1] + q_offset, k.shape[1] + kv_offset)
+        cos_cache, sin_cache = precompute_rope_cache(max_pos, q.shape[-1], rope_base)
+    qr = rope(q, cos_cache, sin_cache, q_offset, dtype)
+    kr = rope(k, cos_cache, sin_cache, kv_offset, dtype)
+    return flash_attention(qr, kr, v, scale=scale, causal=causal, layout="BSHD", dtype=dtype)
+
+
 # ----------------------------------------------------------------------------------------
 # The reference's own blockwise algorithms (fp32, as MLX computes them)
 # ----------------------------------------------------------------------------------------

@@ -18,6 +18,8 @@ Metal branches (as on an MLX build without them), and records what its own code 
   _online_softmax.py:42-176  online_softmax_merge / compute_chunk_attention
   utils/masking.py:14-66 create_causal_mask; sliding_window.py:628-656 create_sliding_window_mask
   grouped_query.py:195-261  gqa_attention;  multi_query.py:161-225  mqa_attention
+  kernels/rope.py:223-255, 451-496  precompute_rope_cache, rope (Python path)
+  kernels/fused_rope_attention.py:766-800, 939-985  fused_rope_attention (use_metal=False)
 
 Inputs come from numpy's legacy RandomState (frozen stream) through
 oracle.attention_oracle.make_qkv, so tests regenerate them bit-for-bit from the seed; only the
@@ -70,7 +72,26 @@ def _stand_in_mlx() -> types.ModuleType:
     mx.full = lambda shape, val, dtype=None: np.full(shape, val, dtype=dtype or f32)
     mx.zeros = lambda shape, dtype=None: np.zeros(shape, dtype=dtype or f32)
     mx.ones = lambda shape, dtype=None: np.ones(shape, dtype=dtype or f32)
-    mx.arange = lambda *a, **k: np.arange(*a, **k).astype(np.int32)
+    def arange(*a, dtype=None, **k):
+        r = np.arange(*a, **k)
+        return r.astype(dtype) if dtype is not None else r.astype(np.int32)
+
+    mx.arange = arange
+    mx.outer = np.outer
+    mx.cos = np.cos
+    mx.sin = np.sin
+
+    class _CustomFunction:  # @mx.custom_function: the recorded paths only call it
+        def __init__(self, f):
+            self.f = f
+
+        def __call__(self, *a, **k):
+            return self.f(*a, **k)
+
+        def vjp(self, g):
+            return g
+
+    mx.custom_function = _CustomFunction
     mx.einsum = lambda spec, *ops: np.einsum(spec, *ops).astype(np.result_type(*ops))
     mx.where = lambda c, a, b: np.where(c, a, b).astype(np.result_type(_f(a), _f(b)))
     mx.max = lambda x, axis=None, keepdims=False: np.max(x, axis=axis, keepdims=keepdims)
@@ -130,6 +151,11 @@ def load_reference(ref_root: Path):
     mods["masking"] = importlib.import_module("mlx_primitives.utils.masking")
     mods["grouped_query"] = importlib.import_module("mlx_primitives.attention.grouped_query")
     mods["multi_query"] = importlib.import_module("mlx_primitives.attention.multi_query")
+    mods["rope"] = importlib.import_module("mlx_primitives.kernels.rope")
+    mods["fused_rope"] = importlib.import_module("mlx_primitives.kernels.fused_rope_attention")
+    for n in ["rope", "fused_rope"]:
+        setattr(mods[n], "_USE_METAL_KERNELS", False)
+    setattr(mods["fused_rope"], "_HAS_SDPA", False)
     for n in ["flash", "sliding_window", "chunked"]:
         setattr(mods[n], "_HAS_SDPA", False)
         setattr(mods[n], "_HAS_METAL", False)
@@ -215,6 +241,23 @@ def main() -> None:
          lambda q, k, v: mq.mqa_attention(q, k, v, causal=True))
     case("mqa_3d_kv_noncausal_d128", 124, (1, 50, 3, 128), (1, 75, 1, 128),
          lambda q, k, v: mq.mqa_attention(q, k[:, :, 0], v[:, :, 0], causal=False))
+
+    # RoPE (kernels/rope.py:223-255, 451-496) and RoPE + attention
+    # (kernels/fused_rope_attention.py:766-800 via fused_rope_attention(use_metal=False))
+    ro, fr = mods["rope"], mods["fused_rope"]
+    cos, sin = ro.precompute_rope_cache(80, 64, base=10000.0)
+    out["rope__cos_80x64"] = np.asarray(cos, dtype=np.float32)
+    out["rope__sin_80x64"] = np.asarray(sin, dtype=np.float32)
+    case("rope_only_offset7_d64", 125, (1, 50, 2, 64), (1, 50, 2, 64),
+         lambda q, k, v: ro.rope(q, cos, sin, 7))
+    case("fused_rope_causal_d64", 126, (1, 96, 2, 64), (1, 96, 2, 64),
+         lambda q, k, v: fr.fused_rope_attention(q, k, v, causal=True, use_metal=False))
+    case("fused_rope_offsets_noncausal_d128", 127, (1, 40, 2, 128), (1, 70, 2, 128),
+         lambda q, k, v: fr.fused_rope_attention(q, k, v, q_offset=30, kv_offset=0,
+                                                 causal=False, use_metal=False))
+    case("fused_rope_decode_causal_base500", 128, (2, 1, 4, 64), (2, 33, 4, 64),
+         lambda q, k, v: fr.fused_rope_attention(q, k, v, rope_base=500.0, q_offset=32,
+                                                 causal=True, use_metal=False))
 
     # _online_softmax: merge and chunk helpers
     q, k, v = make_qkv((1, 16, 2, 64), (1, 48, 2, 64), seed=119)

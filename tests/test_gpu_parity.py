@@ -247,6 +247,10 @@ GOLDEN_CALLS = {
     "gqa_g2_causal_kv_longer_d64": ("gqa", dict(num_kv_groups=2, scale=0.2, causal=True)),
     "mqa_causal_d64": ("mqa", dict(causal=True)),
     "mqa_3d_kv_noncausal_d128": ("mqa3d", dict(causal=False)),
+    "rope_only_offset7_d64": ("rope", dict(offset=7)),
+    "fused_rope_causal_d64": ("frope", dict(causal=True)),
+    "fused_rope_offsets_noncausal_d128": ("frope", dict(q_offset=30, kv_offset=0, causal=False)),
+    "fused_rope_decode_causal_base500": ("frope", dict(rope_base=500.0, q_offset=32, causal=True)),
 }
 
 
@@ -255,6 +259,17 @@ def _call(api, mod, q, k, v, kw):
         return mod.flash_attention(q, k, v, **kw)
     if api == "swa":
         return mod.sliding_window_attention(q, k, v, **kw)
+    if api == "rope":
+        if mod is O:
+            return O.rope(q, *O.precompute_rope_cache(80, 64), **kw)
+        from mlx_primitives.kernels import precompute_rope_cache, rope
+        cos, sin = precompute_rope_cache(80, 64)
+        return rope(q, cos, sin, **kw)
+    if api == "frope":
+        if mod is O:
+            return O.fused_rope_attention(q, k, v, **kw)
+        from mlx_primitives.kernels import fused_rope_attention
+        return fused_rope_attention(q, k, v, **kw)
     if api in ("gqa", "mqa", "mqa3d"):
         m = getattr(mod, "attention", mod)  # the package keeps them in mlx_primitives.attention
         if api == "gqa":

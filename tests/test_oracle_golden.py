@@ -57,6 +57,15 @@ SEMANTIC = {
     "mqa_causal_d64": (lambda q, k, v: O.mqa_attention(q, k, v, causal=True), None),
     "mqa_3d_kv_noncausal_d128": (
         lambda q, k, v: O.mqa_attention(q, k[:, :, 0], v[:, :, 0], causal=False), None),
+    "rope_only_offset7_d64": (
+        lambda q, k, v: O.rope(q, *O.precompute_rope_cache(80, 64), offset=7), None),
+    "fused_rope_causal_d64": (lambda q, k, v: O.fused_rope_attention(q, k, v, causal=True), None),
+    "fused_rope_offsets_noncausal_d128": (
+        lambda q, k, v: O.fused_rope_attention(q, k, v, q_offset=30, kv_offset=0, causal=False),
+        None),
+    "fused_rope_decode_causal_base500": (
+        lambda q, k, v: O.fused_rope_attention(q, k, v, rope_base=500.0, q_offset=32, causal=True),
+        None),
 }
 
 
@@ -113,6 +122,12 @@ def test_online_softmax_merge_and_chunk_helpers():
     full = O.attention_bhsd(np.swapaxes(q, 1, 2), np.swapaxes(k, 1, 2), np.swapaxes(v, 1, 2),
                             0.125, causal=True, q_offset=30)
     np.testing.assert_allclose(np.swapaxes(om / lm[..., None], 1, 2), full, rtol=1e-4, atol=1e-5)
+
+
+def test_rope_cache_matches_reference():
+    cos, sin = O.precompute_rope_cache(80, 64)
+    np.testing.assert_allclose(cos, GOLDEN["rope__cos_80x64"], atol=1e-6)
+    np.testing.assert_allclose(sin, GOLDEN["rope__sin_80x64"], atol=1e-6)
 
 
 def test_masks_match_reference():
