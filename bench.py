@@ -64,6 +64,12 @@ CONFIGS = {
     "r2": dict(workload="fused_rope_attention bf16 BSHD causal (config-2 shape)", api="frope",
                dtype="bf16", layout="BSHD", B=4, H=32, S=4096, Skv=4096, D=128, causal=True,
                window=-1, std=1.0),
+    # paged-KV decode (cache.paged_attention): the reference cache benchmark's largest shape
+    # (benchmarks/suites/cache.py:64-80, 204-234: batch 8, 4096 cached tokens, 32 heads,
+    # head_dim 128, block 16, sequential block tables); HBM-bound, not a BASELINE config
+    "p4": dict(workload="paged_attention decode bf16, 8 sequences x 4096 cached tokens, block 16",
+               api="paged", dtype="bf16", layout="BSHD", B=8, H=32, S=1, Skv=4096, D=128,
+               block=16, causal=True, window=-1, std=1.0),
     # total work fixed: one 128K-token sequence, sequence-parallel ring over the N GPUs
     "c5": dict(workload="long-context flash_attention bf16 BHSD causal, zig-zag ring (config 5)",
                api="ring", dtype="bf16", layout="BHSD", B=1, H=32, S=131072, Skv=131072,
@@ -251,6 +257,220 @@ def config_json(c, n):
                    else "L2 flushed between timed iterations")}
 
 
+# ------------------------------------------------------------------------------ paged decode
+def paged_tables(c):
+    """Sequential block tables of the reference cache benchmark (create_block_table_from_lengths
+    over equal lengths): sequence b owns blocks b * n .. b * n + n - 1."""
+    n = (c["Skv"] + c["block"] - 1) // c["block"]
+    bt = np.arange(c["B"] * n, dtype=np.int32).reshape(c["B"], n)
+    return bt, np.full(c["B"], c["Skv"], dtype=np.int32), c["B"] * n
+
+
+def paged_flops_bytes(c, seqs=None):
+    """Algorithmic FLOPs (4 * D per admissible (query, key) pair per head) and minimum HBM bytes
+    (every K/V row of the contexts read once, q read and o written once) of a decode step."""
+    seqs = c["B"] if seqs is None else seqs
+    es = 4 if c["dtype"] == "fp32" else 2
+    pairs = seqs * c["Skv"] * c["H"]
+    return 4.0 * c["D"] * pairs, es * c["D"] * (2 * pairs + 2 * seqs * c["H"])
+
+
+def cpu_paged_sample(c, budget_s, max_seqs=None):
+    """The oracle's paged_attention (fp32 numpy) on whole sequences of config c until budget_s
+    is used.  Returns (TFLOPS, sequences, seconds, threads)."""
+    from oracle import attention_oracle as O
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max((i.get("num_threads", 1) for i in threadpool_info()), default=os.cpu_count())
+    except Exception:  # noqa: BLE001
+        threads = os.cpu_count()
+    n = (c["Skv"] + c["block"] - 1) // c["block"]
+    q, kp, vp = O.make_qkv((1, 1, c["H"], c["D"]), (n, c["block"], c["H"], c["D"]), seed=7)
+    if c["dtype"] != "fp32":
+        q, kp, vp = (O.round_bf16(a) for a in (q, kp, vp))
+    bt = np.arange(n, dtype=np.int32)[None]
+    ctx = np.array([c["Skv"]], dtype=np.int32)
+    seqs, t_total = 0, 0.0
+    cap = max_seqs or c["B"]
+    while seqs < cap and (seqs == 0 or t_total < budget_s):
+        t0 = time.perf_counter()
+        O.paged_attention(q, kp, vp, bt, ctx, block_size=c["block"], dtype=np.float32)
+        t_total += time.perf_counter() - t0
+        seqs += 1
+    flops, _ = paged_flops_bytes(c, seqs)
+    return flops / t_total / 1e12, seqs, t_total, threads
+
+
+def bench_paged(args, c, world, rank, local):
+    """Decode step of paged attention: q (B, 1, H, D) over the block pools through
+    mlx_primitives.cache.paged_attention.  value = algorithmic TFLOPS of the whole job; the
+    roofline is HBM (K/V bytes of the contexts / launch time, against MEASURED_PEAKS hbm_gbs)."""
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        per, seqs_total, threads = [], 0, None
+        for i in range(args.warmup + args.steps):
+            _, seqs, secs, threads = cpu_paged_sample(c, 0.0, max_seqs=1)
+            if i >= args.warmup:
+                per.append(secs)
+                seqs_total += seqs
+        flops, _ = paged_flops_bytes(c, seqs_total)
+        value = flops / sum(per) / 1e12
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOPS",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * sum(per) / len(per), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": paged_config_json(c, args.gpus),
+            "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": threads, "kind": "port",
+                             "sample": f"{seqs_total} sequences of {c['workload']}, one per step, "
+                                       "fp32 numpy (gather + dense masked softmax, as the reference)"},
+            "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "note": "MLX cannot run on this Linux/NVIDIA box; this arm times the oracle's "
+                    "restatement of the reference's paged_attention"}), flush=True)
+        return
+
+    import ctypes
+
+    import torch
+    import torch.distributed as dist
+
+    from mlx_primitives import _lib
+    from mlx_primitives.cache import paged_attention
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    dtype = torch.float32 if c["dtype"] == "fp32" else torch.bfloat16
+    B, H, D, bs = c["B"], c["H"], c["D"], c["block"]
+    bt_np, ctx_np, nblk = paged_tables(c)
+    g = torch.Generator(device=dev)
+    g.manual_seed(42 + rank)
+    q = torch.randn((B, 1, H, D), generator=g, device=dev).to(dtype)
+    kp = torch.randn((nblk, bs, H, D), generator=g, device=dev).to(dtype)
+    vp = torch.randn((nblk, bs, H, D), generator=g, device=dev).to(dtype)
+    bt = torch.from_numpy(bt_np).to(dev)
+    ctx = torch.from_numpy(ctx_np).to(dev)
+
+    def step(qq, btt, cc):
+        return paged_attention(qq, kp, vp, btt, cc, block_size=bs)
+
+    # the same launch straight through the C-ABI (arguments built once): the kernel timing
+    L = _lib.lib()
+    dt = _lib.DTYPE_CODES[dtype]
+    o = torch.empty_like(q)
+    ws_bytes = L.mlxp_paged_attn_workspace_size(dt, B, H, 1, D, H, nblk, bs, bt.shape[1], 0)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    cargs = (q.data_ptr(), kp.data_ptr(), vp.data_ptr(), bt.data_ptr(), ctx.data_ptr(), None,
+             o.data_ptr(), dt, B, H, 1, D, H, nblk, bs, bt.shape[1], _lib.strides4(q, "BSHD"),
+             (ctypes.c_int64 * 4)(*kp.stride()), bt.stride(0), _lib.strides4(o, "BSHD"),
+             ctypes.c_float(D ** -0.5), 1, 0, ws.data_ptr(), ws_bytes, stream.cuda_stream)
+    launches = 2 if ws_bytes else 1  # paged kernel (+ LSE merge when the contexts are split)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(fn, n):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(n)]
+        barrier()
+        torch.cuda.synchronize(dev)
+        for a, b in ev:
+            a.record(stream)
+            fn()
+            b.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        return sum(a.elapsed_time(b) for a, b in ev) / n
+
+    for _ in range(args.warmup):
+        step(q, bt, ctx)
+        _lib.check(L.mlxp_paged_attn(*cargs), "mlxp_paged_attn")
+    with ClockSampler(local) as clocks:
+        ms_local = timed(lambda: step(q, bt, ctx), args.steps)
+        ms_kernel = timed(lambda: L.mlxp_paged_attn(*cargs), args.steps)
+    torch.cuda.synchronize(dev)
+    assert torch.equal(o, step(q, bt, ctx)), "C-ABI launch and public API disagree"
+    ms = max_over_ranks(ms_local)
+    flops, min_bytes = paged_flops_bytes(c)
+    value = world * flops / (ms * 1e-3) / 1e12
+    _, _, hbm, peak_src = load_peaks()
+    achieved_gbs = min_bytes / (ms_kernel * 1e-3) / 1e9
+
+    # e2e: q, block tables and lengths from pinned host memory, output back to pinned memory;
+    # the pools are the cache's state and stay resident in HBM between decode steps
+    hq, hbt, hctx = q.cpu().pin_memory(), bt.cpu().pin_memory(), ctx.cpu().pin_memory()
+    oh = torch.empty(q.shape, dtype=dtype, pin_memory=True)
+
+    def e2e_step():
+        o_ = step(hq.to(dev, non_blocking=True), hbt.to(dev, non_blocking=True),
+                  hctx.to(dev, non_blocking=True))
+        oh.copy_(o_, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    e2e_ms = max_over_ranks(timed(e2e_step, max(args.e2e_steps, 1)))
+    e2e = {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS",
+           "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in (hq, hbt, hctx)),
+           "d2h_bytes_per_step": oh.numel() * oh.element_size(), "ms_per_step": e2e_ms,
+           "note": "per decode step: q, block tables and context lengths copied in, the output "
+                   "copied out; the K/V pools are the cache state, resident in HBM"}
+
+    line = None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded N(0, 1) q and pools generated on device (seed 42 + rank)",
+            "config": paged_config_json(c, world),
+            "kv_gbs": min_bytes / (ms * 1e-3) / 1e9,
+            "roofline": {
+                "bound": "hbm", "achieved": achieved_gbs, "peak": hbm, "unit": "GB/s",
+                "frac": achieved_gbs / hbm, "traffic": NCU_TRAFFIC_BYTES.get(args.config),
+                "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + write.sum)",
+                "kernel": "paged_attn_kernel + lse_merge_kernel (one C-ABI call)",
+                "kernel_ms": ms_kernel,
+                "peak_source": f"{peak_src}: hbm_gbs",
+                "algorithmic_bytes_per_launch": min_bytes,
+            },
+            "e2e": e2e,
+            "gpu_launches": args.steps * launches * 2,
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and args.cpu_budget > 0:
+            tf, seqs, secs, threads = cpu_paged_sample(c, args.cpu_budget)
+            line["cpu_baseline"] = {
+                "value": tf, "unit": "TFLOPS", "cores": threads, "kind": "port",
+                "sample": f"{seqs} of {B} sequences, oracle paged_attention fp32 numpy, "
+                          f"{secs:.1f} s"}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+def paged_config_json(c, n):
+    return {"workload": c["workload"], "global_batch": c["B"] * n, "batch_per_gpu": c["B"],
+            "heads": c["H"], "head_dim": c["D"], "context_len": c["Skv"],
+            "block_size": c["block"], "block_tables": "sequential (reference benchmark)",
+            "parallelism": f"dp{n} over sequences, no collective",
+            "l2": "inputs larger than L2"}
+
+
 # ------------------------------------------------------------------------------ GPU side
 def main():
     ap = argparse.ArgumentParser()
@@ -270,6 +490,9 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
 
+    if c["api"] == "paged":
+        bench_paged(args, c, world, rank, local)
+        return
     if args.impl == "reference":
         run_reference_arm(args, c, rank)
         return

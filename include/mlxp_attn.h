@@ -205,6 +205,41 @@ int mlxp_rope_qk(const void* q, const void* k, void* q_out, void* k_out, int dty
                  int64_t q_pos_offset, int64_t k_pos_offset, void* cuda_stream);
 
 /*
+ * Attention over a paged K/V pool: replaces paged_attention and paged_attention_with_bias
+ * (mlx_primitives/cache/paged_attention.py:44-105 and 323-384), whose decode and prefill
+ * bodies (paged_attention.py:108-208, 211-320) gather the pool blocks into dense K/V first.
+ * Here the kernel reads the blocks in place through the block table.
+ *   q, o:        [B][H][Sq][D] through q_strides / o_strides ((batch, head, seq, dim) order).
+ *   k_pool, v_pool: (num_blocks, block_size, kv_heads, D) through pool_strides ((block,
+ *                token, head, dim) order, shared by both pools); query head h reads pool head
+ *                h / (H / kv_heads) (kv_heads = H in the reference).
+ *   block_tables: int32 [B][max_blocks], row stride bt_stride; -1 marks a missing block.
+ *   context_lens: int32 [B].
+ *   alibi_slopes: fp32 [H] or NULL (get_alibi_slopes, paged_attention.py:17-41).
+ * Key position t = slot * block_size + offset is admissible when t < context_lens[b], the
+ * slot's id is in [0, num_blocks), and, if causal and Sq > 1, t <= query index.  ALiBi adds
+ * slope[h] * (t - q_pos), q_pos = context_lens[b] when Sq == 1 and the query index otherwise.
+ * A query row with no admissible key gets zeros (the reference's softmax gives NaN).
+ * head_dim 32, 64 or 128; fp32/bf16/fp16, computed in fp32.  q and the pools 4*elem-size
+ * aligned with strides that are multiples of 4 elements.  kv_splits: 0 = automatic, 1 = none,
+ * n = n shares of the block table per query row (combined by an LSE merge into o).
+ * workspace: >= mlxp_paged_attn_workspace_size bytes, 256-byte aligned (0 bytes when no split).
+ */
+int mlxp_paged_attn(const void* q, const void* k_pool, const void* v_pool,
+                    const int32_t* block_tables, const int32_t* context_lens,
+                    const float* alibi_slopes, void* o, int dtype, int64_t B, int64_t H,
+                    int64_t Sq, int64_t D, int64_t kv_heads, int64_t num_blocks,
+                    int64_t block_size, int64_t max_blocks, const int64_t q_strides[4],
+                    const int64_t pool_strides[4], int64_t bt_stride,
+                    const int64_t o_strides[4], float scale, int causal, int64_t kv_splits,
+                    void* workspace, size_t ws_bytes, void* cuda_stream);
+
+/* Bytes of workspace mlxp_paged_attn needs for these arguments (0 = none, or invalid shape). */
+size_t mlxp_paged_attn_workspace_size(int dtype, int64_t B, int64_t H, int64_t Sq, int64_t D,
+                                      int64_t kv_heads, int64_t num_blocks, int64_t block_size,
+                                      int64_t max_blocks, int64_t kv_splits);
+
+/*
  * Device-side status word of the current device: 0 when every bounded wait completed,
  * otherwise MLXP_ERR_TIMEOUT | (site << 8).  Synchronises the device.  reset != 0 clears it.
  */

@@ -21,6 +21,7 @@
 #include "attn_fwd_fp32.cuh"
 #include "attn_fwd_sm100.cuh"
 #include "rope.cuh"
+#include "paged_attn.cuh"
 
 namespace mlxp {
 
@@ -566,6 +567,69 @@ int rope_launch(int dtype, int64_t D, RopeParams& rp, const int64_t* const xs[2]
   return e == cudaSuccess ? MLXP_OK : cuda_fail(e, "rope launch");
 }
 
+
+// ---- paged attention (cache/paged_attention.py) ----
+
+struct PagedProblem {
+  int dtype;
+  int64_t B, H, Sq, D, Hkv, num_blocks, block_size, max_blocks;
+};
+
+int paged_validate(const PagedProblem& pp) {
+  if (pp.B < 0 || pp.H <= 0 || pp.Sq < 0 || pp.Hkv <= 0 || pp.num_blocks < 0 ||
+      pp.block_size <= 0 || pp.max_blocks < 0)
+    return fail(MLXP_ERR_INVALID,
+                "invalid paged shape B=%lld H=%lld Sq=%lld kv_heads=%lld num_blocks=%lld "
+                "block_size=%lld max_blocks=%lld",
+                (long long)pp.B, (long long)pp.H, (long long)pp.Sq, (long long)pp.Hkv,
+                (long long)pp.num_blocks, (long long)pp.block_size, (long long)pp.max_blocks);
+  if (pp.H % pp.Hkv)
+    return fail(MLXP_ERR_INVALID, "num_heads (%lld) must be divisible by the pool's heads (%lld)",
+                (long long)pp.H, (long long)pp.Hkv);
+  if (pp.dtype < 0 || pp.dtype > 2) return fail(MLXP_ERR_INVALID, "unknown dtype %d", pp.dtype);
+  if (pp.D != 32 && pp.D != 64 && pp.D != 128)
+    return fail(MLXP_ERR_UNSUPPORTED, "paged attention supports head_dim 32, 64 and 128, got %lld",
+                (long long)pp.D);
+  if (pp.B * pp.Sq > INT32_MAX || pp.max_blocks * pp.block_size > INT32_MAX ||
+      pp.num_blocks > INT32_MAX || pp.H > INT32_MAX)
+    return fail(MLXP_ERR_INVALID, "paged shape too large");
+  return MLXP_OK;
+}
+
+// Shares of the block-table slots per query row: about four CTAs per SM in all, at least 64
+// key positions per share, at most 65535 shares (grid y).
+int paged_splits(const PagedProblem& pp, int64_t kv_splits, int sms) {
+  const long long rows = pp.B * pp.Sq;
+  if (rows <= 0 || pp.max_blocks <= 1 || kv_splits == 1) return 1;
+  long long splits;
+  if (kv_splits > 1) {
+    splits = std::min<long long>(kv_splits, pp.max_blocks);
+  } else {
+    splits = (4LL * sms + rows - 1) / rows;
+    if (splits <= 1) return 1;
+    const long long min_bps = std::max<long long>(1, (64 + pp.block_size - 1) / pp.block_size);
+    const long long bps = std::max<long long>((pp.max_blocks + splits - 1) / splits, min_bps);
+    splits = (pp.max_blocks + bps - 1) / bps;
+  }
+  splits = std::min<long long>(splits, 65535);
+  const long long bps = (pp.max_blocks + splits - 1) / splits;
+  return (int)((pp.max_blocks + bps - 1) / bps);
+}
+
+size_t paged_workspace(const PagedProblem& pp, int splits) {
+  if (splits <= 1) return 0;
+  const size_t rows = (size_t)splits * pp.B * pp.H * pp.Sq;
+  return (rows * pp.D * 4 + 255) / 256 * 256 + rows * 4;
+}
+
+template <typename T>
+cudaError_t paged_launch_t(const PagedParams& p, int LPR, dim3 grid, cudaStream_t s) {
+  if (LPR == 32) paged_attn_kernel<T, 32><<<grid, 256, 0, s>>>(p);
+  else if (LPR == 16) paged_attn_kernel<T, 16><<<grid, 256, 0, s>>>(p);
+  else paged_attn_kernel<T, 8><<<grid, 256, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
 }  // namespace
 }  // namespace mlxp
 
@@ -758,6 +822,107 @@ int mlxp_rope_qk(const void* q, const void* k, void* q_out, void* k_out, int dty
   const int64_t* xs[2] = {q_strides, k_strides};
   const int64_t* ys[2] = {qo_strides, ko_strides};
   return rope_launch(dtype, D, rp, xs, ys, static_cast<cudaStream_t>(cuda_stream));
+}
+
+size_t mlxp_paged_attn_workspace_size(int dtype, int64_t B, int64_t H, int64_t Sq, int64_t D,
+                                      int64_t kv_heads, int64_t num_blocks, int64_t block_size,
+                                      int64_t max_blocks, int64_t kv_splits) {
+  PagedProblem pp{dtype, B, H, Sq, D, kv_heads, num_blocks, block_size, max_blocks};
+  if (paged_validate(pp) != MLXP_OK) return 0;
+  int sms = 148;
+  if (kv_splits == 0 && device_info(nullptr, &sms) != MLXP_OK) sms = 148;
+  return paged_workspace(pp, paged_splits(pp, kv_splits, sms));
+}
+
+int mlxp_paged_attn(const void* q, const void* k_pool, const void* v_pool,
+                    const int32_t* block_tables, const int32_t* context_lens,
+                    const float* alibi_slopes, void* o, int dtype, int64_t B, int64_t H,
+                    int64_t Sq, int64_t D, int64_t kv_heads, int64_t num_blocks,
+                    int64_t block_size, int64_t max_blocks, const int64_t q_strides[4],
+                    const int64_t pool_strides[4], int64_t bt_stride,
+                    const int64_t o_strides[4], float scale, int causal, int64_t kv_splits,
+                    void* workspace, size_t ws_bytes, void* cuda_stream) {
+  PagedProblem pp{dtype, B, H, Sq, D, kv_heads, num_blocks, block_size, max_blocks};
+  if (int rc = paged_validate(pp)) return rc;
+  if (!(scale > 0.f) || !std::isfinite(scale))
+    return fail(MLXP_ERR_INVALID, "scale must be positive and finite");
+  if (kv_splits < 0) return fail(MLXP_ERR_INVALID, "kv_splits must be >= 0");
+  if (B == 0 || Sq == 0) return MLXP_OK;
+  if (!q || !o || !context_lens || !q_strides || !o_strides || !pool_strides)
+    return fail(MLXP_ERR_INVALID, "q, o, context_lens and the stride arrays must be non-null");
+  if (max_blocks > 0 && (!k_pool || !v_pool || !block_tables))
+    return fail(MLXP_ERR_INVALID, "k_pool, v_pool and block_tables must be non-null");
+  if (max_blocks > 0 && B > 1 && bt_stride < max_blocks)
+    return fail(MLXP_ERR_INVALID, "block-table row stride (%lld) is below max_blocks (%lld)",
+                (long long)bt_stride, (long long)max_blocks);
+  if (q_strides[3] != 1 || o_strides[3] != 1 || pool_strides[3] != 1)
+    return fail(MLXP_ERR_INVALID, "head_dim stride must be 1");
+  // every lane reads 4 consecutive elements as one vector
+  const int es = dtype == MLXP_DTYPE_FP32 ? 4 : 2;
+  const uintptr_t qa = 4u * es;
+  const void* ptrs[3] = {q, k_pool, v_pool};
+  for (const void* ptr : ptrs)
+    if (ptr && reinterpret_cast<uintptr_t>(ptr) % qa)
+      return fail(MLXP_ERR_INVALID, "q, k_pool and v_pool must be %d-byte aligned", (int)qa);
+  for (int d = 0; d < 3; ++d)
+    if (q_strides[d] % 4 || pool_strides[d] % 4 || q_strides[d] < 0 || pool_strides[d] < 0)
+      return fail(MLXP_ERR_INVALID, "q and pool strides must be non-negative multiples of 4 elements");
+  int sms = 148;
+  if (int rc = device_info(nullptr, &sms)) return rc;
+  const int splits = paged_splits(pp, kv_splits, sms);
+  const size_t need = paged_workspace(pp, splits);
+  if (need > 0 && (workspace == nullptr || ws_bytes < need))
+    return fail(MLXP_ERR_WORKSPACE, "paged attention needs %zu bytes of workspace, got %zu", need,
+                ws_bytes);
+  if (need > 0 && reinterpret_cast<uintptr_t>(workspace) % 256)
+    return fail(MLXP_ERR_INVALID, "workspace must be 256-byte aligned");
+  PagedParams p{};
+  p.q = q;
+  p.k_pool = k_pool;
+  p.v_pool = v_pool;
+  p.block_tables = block_tables;
+  p.context_lens = context_lens;
+  p.alibi = alibi_slopes;
+  p.o = o;
+  p.q_sb = q_strides[0];
+  p.q_sh = q_strides[1];
+  p.q_ss = q_strides[2];
+  p.o_sb = o_strides[0];
+  p.o_sh = o_strides[1];
+  p.o_ss = o_strides[2];
+  p.p_sb = pool_strides[0];
+  p.p_st = pool_strides[1];
+  p.p_sh = pool_strides[2];
+  p.bt_stride = bt_stride;
+  p.B = (int)B;
+  p.H = (int)H;
+  p.Sq = (int)Sq;
+  p.D = (int)D;
+  p.kv_group = (int)(H / kv_heads);
+  p.num_blocks = (int)num_blocks;
+  p.block_size = (int)block_size;
+  p.max_blocks = (int)max_blocks;
+  p.blocks_per_split = (int)((max_blocks + splits - 1) / splits);
+  if (p.blocks_per_split < 1) p.blocks_per_split = 1;
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  if (splits > 1) {
+    const size_t rows = (size_t)splits * B * H * Sq;
+    p.o_part = static_cast<float*>(workspace);
+    p.lse_part = reinterpret_cast<float*>(static_cast<char*>(workspace) +
+                                          (rows * D * 4 + 255) / 256 * 256);
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(cuda_stream);
+  const dim3 grid((unsigned)(B * Sq), (unsigned)splits);
+  const int LPR = (int)(D / 4);
+  cudaError_t e;
+  if (dtype == MLXP_DTYPE_BF16) e = paged_launch_t<__nv_bfloat16>(p, LPR, grid, s);
+  else if (dtype == MLXP_DTYPE_FP16) e = paged_launch_t<__half>(p, LPR, grid, s);
+  else e = paged_launch_t<float>(p, LPR, grid, s);
+  if (e != cudaSuccess) return cuda_fail(e, "paged attention launch");
+  if (splits <= 1) return MLXP_OK;
+  Problem pr{dtype, B, H, Sq, 0, D, 0, -1, -1, 0, 0};
+  return merge_dispatch(p.o_part, p.lse_part, splits, o, nullptr, pr, o_strides, s);
 }
 
 int mlxp_device_status(int* status_out, int reset) {

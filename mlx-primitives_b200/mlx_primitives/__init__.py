@@ -9,6 +9,7 @@ from .attention import (ChunkedCrossAttention, FlashAttention, SlidingWindowAtte
                         chunked_cross_attention, create_sliding_window_mask,
                         estimate_memory_savings, flash_attention, get_optimal_flash_config,
                         sliding_window_attention)
+from .cache import paged_attention
 from .constants import Layout
 
 __version__ = "0.2.0+b200"
@@ -23,5 +24,6 @@ __all__ = [
     "ChunkedCrossAttention",
     "chunked_cross_attention",
     "estimate_memory_savings",
+    "paged_attention",
     "Layout",
 ]

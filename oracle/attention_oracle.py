@@ -353,6 +353,72 @@ def lse_merge(o_parts, lse_parts):
 
 
 # ----------------------------------------------------------------------------------------
+# Paged K/V attention (cache/paged_attention.py)
+# ----------------------------------------------------------------------------------------
+def get_alibi_slopes(num_heads: int) -> np.ndarray:
+    """paged_attention.py:17-41: slope_h = (2^(-8/H))^(h+1), fp32."""
+    ratio = 2 ** (-8 / num_heads)
+    return np.array([ratio ** (i + 1) for i in range(num_heads)], dtype=np.float32)
+
+
+def create_block_table_from_lengths(sequence_lengths, block_size: int, max_blocks=None):
+    """paged_attention.py:387-440: sequence b owns blocks cum[b] .. cum[b] + n_b - 1
+    (n_b = ceil(len_b / block_size), cum = exclusive prefix sum of n), -1 past n_b; int32."""
+    lens = np.asarray(sequence_lengths, dtype=np.int64)
+    n = (lens + block_size - 1) // block_size
+    mb = int(n.max()) if max_blocks is None else int(max_blocks)
+    cum = np.concatenate([[0], np.cumsum(n)[:-1]])
+    pos = np.arange(mb)[None, :]
+    return np.where(pos < n[:, None], cum[:, None] + pos, -1).astype(np.int32)
+
+
+def paged_attention(q, k_pool, v_pool, block_tables, context_lens, scale=None, block_size=16,
+                    causal=True, alibi_slopes=None, dtype=np.float64):
+    """paged_attention.py:44-320 semantics.  q (B, Sq, H, D); pools (num_blocks, block_size,
+    H, D); block_tables (B, max_blocks), -1 = missing block; context_lens (B,).
+
+    The reference gathers pool blocks max(id, 0) into (B, max_blocks * block_size, H, D)
+    (lines 137-147, 249-259) and masks key position t unless t < context_lens[b] and the
+    slot's id >= 0 (lines 181-199, 288-303); with Sq > 1 and causal it also masks t > i
+    (lines 306-313: top-left, query i at position i).  ALiBi adds slope[h] * (t - q_pos) to the
+    scaled scores, q_pos = context_lens[b] for Sq == 1 (lines 161-179) and i otherwise
+    (lines 271-286).  Softmax over the masked scores: a row with no admissible key is NaN, as
+    the reference's softmax of all -inf gives.
+    """
+    q = np.asarray(q, dtype=dtype)
+    k_pool = np.asarray(k_pool, dtype=dtype)
+    v_pool = np.asarray(v_pool, dtype=dtype)
+    bt = np.asarray(block_tables, dtype=np.int64)
+    ctx = np.asarray(context_lens, dtype=np.int64)
+    B, Sq, H, D = q.shape
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    mb = bt.shape[1]
+    T = mb * block_size
+    safe = np.maximum(bt, 0)
+    k = k_pool[safe].reshape(B, T, H, D)
+    v = v_pool[safe].reshape(B, T, H, D)
+    s = np.einsum("bqhd,bthd->bhqt", q, k) * scale                 # (B, H, Sq, T)
+    t = np.arange(T)
+    if alibi_slopes is not None:
+        slopes = np.asarray(alibi_slopes, dtype=dtype)
+        qpos = ctx[:, None] if Sq == 1 else np.broadcast_to(np.arange(Sq), (B, Sq))
+        diff = (t[None, None, :] - qpos[:, :, None]).astype(dtype)  # (B, Sq, T)
+        s = s + slopes[None, :, None, None] * diff[:, None]
+    valid = (t[None, :] < ctx[:, None]) & (bt[:, t // block_size] >= 0)  # (B, T)
+    valid = np.broadcast_to(valid[:, None, None, :], s.shape)
+    if causal and Sq > 1:
+        valid = valid & (t[None, :] <= np.arange(Sq)[:, None])[None, None]
+    s = np.where(valid, s, -np.inf)
+    with np.errstate(invalid="ignore"):
+        m = s.max(axis=-1, keepdims=True)
+        e = np.exp(s - m)
+        p = e / e.sum(axis=-1, keepdims=True)
+    o = np.einsum("bhqt,bthd->bqhd", p, v)
+    return o
+
+
+# ----------------------------------------------------------------------------------------
 # Zig-zag ring schedule (the sequence-parallel split of the 128K-token causal config)
 # ----------------------------------------------------------------------------------------
 def zigzag_chunks(world: int, rank: int):

@@ -20,6 +20,8 @@ Metal branches (as on an MLX build without them), and records what its own code 
   grouped_query.py:195-261  gqa_attention;  multi_query.py:161-225  mqa_attention
   kernels/rope.py:223-255, 451-496  precompute_rope_cache, rope (Python path)
   kernels/fused_rope_attention.py:766-800, 939-985  fused_rope_attention (use_metal=False)
+  cache/paged_attention.py:17-440  get_alibi_slopes, paged_attention (decode and prefill,
+                         with and without ALiBi), create_block_table_from_lengths
 
 Inputs come from numpy's legacy RandomState (frozen stream) through
 oracle.attention_oracle.make_qkv, so tests regenerate them bit-for-bit from the seed; only the
@@ -98,6 +100,8 @@ def _stand_in_mlx() -> types.ModuleType:
     mx.exp = np.exp
     mx.sum = lambda x, axis=None, keepdims=False: np.sum(x, axis=axis, keepdims=keepdims, dtype=x.dtype)
     mx.maximum = np.maximum
+    mx.take = lambda a, idx, axis=None: np.take(a, idx, axis=axis)
+    mx.cumsum = lambda x, axis=None: np.cumsum(x, axis=axis)
     mx.concatenate = lambda arrs, axis=0: np.concatenate(arrs, axis=axis)
     mx.abs = np.abs
     mx.transpose = lambda x, axes=None: np.transpose(x, axes)
@@ -137,7 +141,8 @@ def load_reference(ref_root: Path):
     sys.modules["mlx.nn"] = nn
     pkg_dir = ref_root / "mlx_primitives"
     for name, sub in [("mlx_primitives", ""), ("mlx_primitives.attention", "attention"),
-                      ("mlx_primitives.kernels", "kernels"), ("mlx_primitives.utils", "utils")]:
+                      ("mlx_primitives.kernels", "kernels"), ("mlx_primitives.utils", "utils"),
+                      ("mlx_primitives.cache", "cache")]:
         m = types.ModuleType(name)
         m.__path__ = [str(pkg_dir / sub) if sub else str(pkg_dir)]
         sys.modules[name] = m
@@ -153,6 +158,7 @@ def load_reference(ref_root: Path):
     mods["multi_query"] = importlib.import_module("mlx_primitives.attention.multi_query")
     mods["rope"] = importlib.import_module("mlx_primitives.kernels.rope")
     mods["fused_rope"] = importlib.import_module("mlx_primitives.kernels.fused_rope_attention")
+    mods["paged"] = importlib.import_module("mlx_primitives.cache.paged_attention")
     for n in ["rope", "fused_rope"]:
         setattr(mods[n], "_USE_METAL_KERNELS", False)
     setattr(mods["fused_rope"], "_HAS_SDPA", False)
@@ -258,6 +264,51 @@ def main() -> None:
     case("fused_rope_decode_causal_base500", 128, (2, 1, 4, 64), (2, 33, 4, 64),
          lambda q, k, v: fr.fused_rope_attention(q, k, v, rope_base=500.0, q_offset=32,
                                                  causal=True, use_metal=False))
+
+    # paged attention (cache/paged_attention.py): q from make_qkv's q, the pools from its k/v
+    # (shape_kv = (num_blocks, block_size, heads, dim)); tables, lengths and slopes are stored.
+    pa = mods["paged"]
+
+    def paged_case(name, seed, B, Sq, H, D, num_blocks, bs, tables, lens, causal=True,
+                   alibi=False, scale=None):
+        bt = np.asarray(tables, dtype=np.int32)
+        cl = np.asarray(lens, dtype=np.int32)
+        slopes = pa.get_alibi_slopes(H) if alibi else None
+        out[f"{name}__bt"] = bt
+        out[f"{name}__ctx"] = cl
+        out[f"{name}__opts"] = np.array([bs, int(causal), int(alibi),
+                                         -1.0 if scale is None else scale], dtype=np.float64)
+        case(name, seed, (B, Sq, H, D), (num_blocks, bs, H, D),
+             lambda q, k, v: pa.paged_attention(q, k, v, bt, cl, scale=scale, block_size=bs,
+                                                causal=causal, alibi_slopes=slopes))
+
+    # decode, the reference test's tables (tests/cache/test_paged_attention.py:164-196)
+    paged_case("paged_decode_batch_d64", 130, 4, 1, 8, 64, 20, 16,
+               [[0, -1, -1], [1, 2, -1], [3, 4, 5], [6, 7, -1]], [16, 32, 48, 25])
+    # decode with ALiBi, permuted blocks, a one-token context and an empty one (NaN row)
+    paged_case("paged_decode_alibi_d128", 131, 4, 1, 4, 128, 12, 16,
+               [[7, 2, 9, 0], [5, -1, -1, -1], [11, 3, 1, 4], [6, -1, -1, -1]],
+               [40, 1, 64, 0], alibi=True)
+    # decode, head_dim 32, block 8: a missing block inside the context, a length past the
+    # table's capacity, and an explicit scale
+    paged_case("paged_decode_hole_d32", 132, 3, 1, 2, 32, 16, 8,
+               [[0, 1, -1, 2, 3], [4, 5, 6, 7, 8], [9, 10, -1, -1, -1]], [37, 90, 11],
+               scale=0.3)
+    # prefill, causal (query i sees positions <= i), contexts longer and shorter than seq_q
+    paged_case("paged_prefill_causal_d64", 133, 2, 20, 8, 64, 10, 16,
+               [[0, 1, 2], [3, 4, -1]], [45, 13])
+    # prefill, ALiBi, bidirectional, block 32
+    paged_case("paged_prefill_alibi_noncausal_d64", 134, 1, 16, 4, 64, 4, 32,
+               [[2, 0]], [40], causal=False, alibi=True)
+    # prefill, ALiBi and causal, head_dim 128
+    paged_case("paged_prefill_alibi_causal_d128", 135, 2, 12, 2, 128, 6, 16,
+               [[5, 1], [0, -1]], [20, 5], alibi=True)
+    out["paged__alibi_8"] = np.asarray(pa.get_alibi_slopes(8), dtype=np.float32)
+    out["paged__alibi_12"] = np.asarray(pa.get_alibi_slopes(12), dtype=np.float32)
+    out["paged__table_16_33_5"] = np.asarray(
+        pa.create_block_table_from_lengths(np.array([16, 33, 5], dtype=np.int32), 16))
+    out["paged__table_7_0_64_b8_max10"] = np.asarray(
+        pa.create_block_table_from_lengths(np.array([7, 0, 64], dtype=np.int32), 8, max_blocks=10))
 
     # _online_softmax: merge and chunk helpers
     q, k, v = make_qkv((1, 16, 2, 64), (1, 48, 2, 64), seed=119)

@@ -252,9 +252,32 @@ GOLDEN_CALLS = {
     "fused_rope_offsets_noncausal_d128": ("frope", dict(q_offset=30, kv_offset=0, causal=False)),
     "fused_rope_decode_causal_base500": ("frope", dict(rope_base=500.0, q_offset=32, causal=True)),
 }
+# paged attention: block tables, lengths and options are stored with each case
+GOLDEN_CALLS.update({c: ("paged", c) for c in (
+    "paged_decode_batch_d64", "paged_decode_alibi_d128", "paged_decode_hole_d32",
+    "paged_prefill_causal_d64", "paged_prefill_alibi_noncausal_d64",
+    "paged_prefill_alibi_causal_d128")})
+
+
+def _paged_call(mod, case, q, k_pool, v_pool):
+    g = _golden()
+    bs, causal, alibi, scale = g[f"{case}__opts"]
+    kw = dict(scale=None if scale < 0 else float(scale), block_size=int(bs), causal=bool(causal))
+    bt, ctx = g[f"{case}__bt"], g[f"{case}__ctx"]
+    if mod is O:
+        slopes = O.get_alibi_slopes(q.shape[2]) if alibi else None
+        # rows with no admissible key: NaN in the reference, zeros by the library's definition
+        return np.nan_to_num(O.paged_attention(q, k_pool, v_pool, bt, ctx, alibi_slopes=slopes,
+                                               **kw), nan=0.0)
+    from mlx_primitives.cache import get_alibi_slopes, paged_attention
+    slopes = get_alibi_slopes(q.shape[2], device=q.device) if alibi else None
+    return paged_attention(q, k_pool, v_pool, torch.from_numpy(bt).to(q.device),
+                           torch.from_numpy(ctx).to(q.device), alibi_slopes=slopes, **kw)
 
 
 def _call(api, mod, q, k, v, kw):
+    if api == "paged":
+        return _paged_call(mod, kw, q, k, v)
     if api == "flash":
         return mod.flash_attention(q, k, v, **kw)
     if api == "swa":
@@ -296,7 +319,7 @@ def test_golden_fixtures_through_public_api(dtype):
         if dtype == torch.float32:
             # same inputs as the reference run: compare with its output directly
             tol = 2e-3 if "large_values" in case else 1e-4
-            assert maxabs(out, g[f"{case}__out"]) <= tol, case
+            assert maxabs(out, np.nan_to_num(g[f"{case}__out"], nan=0.0)) <= tol, case
         else:
             # bf16-rounded inputs: compare with the oracle on those inputs
             want = _call(api, O, nq, nk, nv, kw)

@@ -69,6 +69,20 @@ SEMANTIC = {
 }
 
 
+def _paged(case):
+    """Oracle call of a paged-attention case: tables, lengths and options are stored with it."""
+    def call(q, k, v):
+        bs, causal, alibi, scale = GOLDEN[f"{case}__opts"]
+        slopes = O.get_alibi_slopes(q.shape[2]) if alibi else None
+        return O.paged_attention(q, k, v, GOLDEN[f"{case}__bt"], GOLDEN[f"{case}__ctx"],
+                                 scale=None if scale < 0 else float(scale), block_size=int(bs),
+                                 causal=bool(causal), alibi_slopes=slopes)
+    return call
+
+
+SEMANTIC.update({c: (_paged(c), None) for c in CASES if c.startswith("paged_")})
+
+
 def golden_inputs(case):
     meta = GOLDEN[f"{case}__meta"]
     seed, std = int(meta[0]), float(meta[1])
@@ -128,6 +142,32 @@ def test_rope_cache_matches_reference():
     cos, sin = O.precompute_rope_cache(80, 64)
     np.testing.assert_allclose(cos, GOLDEN["rope__cos_80x64"], atol=1e-6)
     np.testing.assert_allclose(sin, GOLDEN["rope__sin_80x64"], atol=1e-6)
+
+
+def test_paged_helpers_match_reference():
+    """get_alibi_slopes and create_block_table_from_lengths (paged_attention.py:17-41,
+    387-440): the oracle's restatement and the package's torch versions."""
+    import torch
+    from mlx_primitives.cache import create_block_table_from_lengths, get_alibi_slopes
+
+    for h in (8, 12):
+        want = GOLDEN[f"paged__alibi_{h}"]
+        np.testing.assert_array_equal(O.get_alibi_slopes(h), want)
+        np.testing.assert_array_equal(get_alibi_slopes(h).numpy(), want)
+    for lens, bs, mb, key in (([16, 33, 5], 16, None, "paged__table_16_33_5"),
+                              ([7, 0, 64], 8, 10, "paged__table_7_0_64_b8_max10")):
+        want = GOLDEN[key]
+        np.testing.assert_array_equal(O.create_block_table_from_lengths(lens, bs, mb), want)
+        got = create_block_table_from_lengths(torch.tensor(lens, dtype=torch.int32), bs, mb)
+        assert got.dtype == torch.int32
+        np.testing.assert_array_equal(got.numpy(), want)
+
+
+def test_paged_empty_context_is_nan_in_reference():
+    """The reference's softmax over an all-masked row gives NaN (context length 0); the oracle
+    reproduces it, and the GPU tests expect zeros there instead."""
+    want = GOLDEN["paged_decode_alibi_d128__out"]
+    assert np.isnan(want[3]).all() and np.isfinite(want[:3]).all()
 
 
 def test_masks_match_reference():
