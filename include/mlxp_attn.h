@@ -205,6 +205,31 @@ int mlxp_rope_qk(const void* q, const void* k, void* q_out, void* k_out, int dty
                  int64_t q_pos_offset, int64_t k_pos_offset, void* cuda_stream);
 
 /*
+ * Backward pass of attention: dQ, dK, dV of O = softmax(scale * Q K^T + mask) V, the gradient
+ * the reference obtains by MLX autodiff through its forward (mlx_primitives/attention/
+ * flash.py:52-316; checked by tests/gradients/test_numerical_gradients.py:20-270).
+ * Inputs: q, k, v and the forward's o and lse (fp32 [B][H][Sq], natural log, as returned by
+ * mlxp_attn_fwd), and dout = dL/dO.  Outputs dq, dk, dv in the input dtype (dk/dv per K/V
+ * head: grouped heads sum their query heads' contributions).  Every tensor through its own
+ * strides ((batch, head, seq, dim) order, dim stride 1); masks and offsets as mlxp_attn_fwd.
+ * head_dim 32, 64 or 128; computed in fp32.  workspace: >= mlxp_attn_bwd_workspace_size bytes,
+ * 256-byte aligned.  Deterministic (every output element has one writer).
+ */
+int mlxp_attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                  const float* lse, void* dq, void* dk, void* dv, int dtype, int64_t B,
+                  int64_t H, int64_t H_kv, int64_t Sq, int64_t Skv, int64_t D,
+                  const int64_t q_strides[4], const int64_t k_strides[4],
+                  const int64_t v_strides[4], const int64_t o_strides[4],
+                  const int64_t do_strides[4], const int64_t dq_strides[4],
+                  const int64_t dk_strides[4], const int64_t dv_strides[4], float scale,
+                  int causal, int64_t window_left, int64_t window_right, int64_t q_pos_offset,
+                  int64_t kv_pos_offset, void* workspace, size_t ws_bytes, void* cuda_stream);
+
+/* Bytes of workspace mlxp_attn_bwd needs (the per-row dO . O terms). */
+size_t mlxp_attn_bwd_workspace_size(int dtype, int64_t B, int64_t H, int64_t Sq, int64_t Skv,
+                                    int64_t D);
+
+/*
  * Attention over a paged K/V pool: replaces paged_attention and paged_attention_with_bias
  * (mlx_primitives/cache/paged_attention.py:44-105 and 323-384), whose decode and prefill
  * bodies (paged_attention.py:108-208, 211-320) gather the pool blocks into dense K/V first.

@@ -22,6 +22,7 @@
 #include "attn_fwd_sm100.cuh"
 #include "rope.cuh"
 #include "paged_attn.cuh"
+#include "attn_bwd.cuh"
 
 namespace mlxp {
 
@@ -630,6 +631,39 @@ cudaError_t paged_launch_t(const PagedParams& p, int LPR, dim3 grid, cudaStream_
   return cudaGetLastError();
 }
 
+
+// ---- backward (dQ, dK, dV) ----
+
+size_t bwd_workspace(const Problem& pr) {
+  return ((size_t)pr.B * pr.H * pr.Sq * 4 + 255) / 256 * 256;
+}
+
+template <typename T, int D>
+int bwd_launch_t(const BwdParams& bp, cudaStream_t s) {
+  constexpr int smem_kv = bwd_dkdv_smem<D>();
+  constexpr int smem_q = bwd_dq_smem<D>();
+  // attribute-cache bits 13..30: two per (element type, head_dim) pair
+  constexpr int ti = sizeof(T) == 4 ? 0 : (std::is_same<T, __nv_bfloat16>::value ? 1 : 2);
+  constexpr int slot = 13 + 2 * (ti * 3 + (D == 32 ? 0 : D == 64 ? 1 : 2));
+  if (int rc = ensure_smem_attr(bwd_dkdv_kernel<T, D>, smem_kv, 1u << slot)) return rc;
+  if (int rc = ensure_smem_attr(bwd_dq_kernel<T, D>, smem_q, 1u << (slot + 1))) return rc;
+  const long long rows = (long long)bp.B * bp.H * bp.Sq;
+  bwd_delta_kernel<T><<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(bp, D);
+  const long long n_kt = (bp.Skv + 63) / 64, n_qt = (bp.Sq + 63) / 64;
+  const long long g_kv = n_kt * bp.B * (bp.H / bp.kv_group), g_q = n_qt * bp.B * bp.H;
+  if (g_kv > 0) bwd_dkdv_kernel<T, D><<<(unsigned)g_kv, 256, smem_kv, s>>>(bp);
+  if (g_q > 0) bwd_dq_kernel<T, D><<<(unsigned)g_q, 256, smem_q, s>>>(bp);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MLXP_OK : cuda_fail(e, "attention backward launch");
+}
+
+template <typename T>
+int bwd_dispatch_d(const BwdParams& bp, int D, cudaStream_t s) {
+  if (D == 32) return bwd_launch_t<T, 32>(bp, s);
+  if (D == 64) return bwd_launch_t<T, 64>(bp, s);
+  return bwd_launch_t<T, 128>(bp, s);
+}
+
 }  // namespace
 }  // namespace mlxp
 
@@ -923,6 +957,84 @@ int mlxp_paged_attn(const void* q, const void* k_pool, const void* v_pool,
   if (splits <= 1) return MLXP_OK;
   Problem pr{dtype, B, H, Sq, 0, D, 0, -1, -1, 0, 0};
   return merge_dispatch(p.o_part, p.lse_part, splits, o, nullptr, pr, o_strides, s);
+}
+
+size_t mlxp_attn_bwd_workspace_size(int dtype, int64_t B, int64_t H, int64_t Sq, int64_t Skv,
+                                    int64_t D) {
+  Problem pr{dtype, B, H, Sq, Skv, D, 0, -1, -1, 0, 0};
+  if (B < 0 || H <= 0 || Sq < 0 || Skv < 0) return 0;
+  return bwd_workspace(pr);
+}
+
+int mlxp_attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                  const float* lse, void* dq, void* dk, void* dv, int dtype, int64_t B,
+                  int64_t H, int64_t H_kv, int64_t Sq, int64_t Skv, int64_t D,
+                  const int64_t q_strides[4], const int64_t k_strides[4],
+                  const int64_t v_strides[4], const int64_t o_strides[4],
+                  const int64_t do_strides[4], const int64_t dq_strides[4],
+                  const int64_t dk_strides[4], const int64_t dv_strides[4], float scale,
+                  int causal, int64_t window_left, int64_t window_right, int64_t q_pos_offset,
+                  int64_t kv_pos_offset, void* workspace, size_t ws_bytes, void* cuda_stream) {
+  if (B < 0 || H <= 0 || H_kv <= 0 || Sq < 0 || Skv < 0)
+    return fail(MLXP_ERR_INVALID, "invalid backward shape B=%lld H=%lld H_kv=%lld Sq=%lld Skv=%lld",
+                (long long)B, (long long)H, (long long)H_kv, (long long)Sq, (long long)Skv);
+  if (H % H_kv) return fail(MLXP_ERR_INVALID, "num_heads must be divisible by num_kv_heads");
+  if (dtype < 0 || dtype > 2) return fail(MLXP_ERR_INVALID, "unknown dtype %d", dtype);
+  if (D != 32 && D != 64 && D != 128)
+    return fail(MLXP_ERR_UNSUPPORTED, "attention backward supports head_dim 32, 64 and 128, got %lld",
+                (long long)D);
+  if (!(scale > 0.f) || !std::isfinite(scale))
+    return fail(MLXP_ERR_INVALID, "scale must be positive and finite");
+  if (window_left < -1 || window_right < -1)
+    return fail(MLXP_ERR_INVALID, "window must be >= 0 or -1");
+  if (B * H * std::max(Sq, Skv) > INT32_MAX || Sq > INT32_MAX / 2 || Skv > INT32_MAX / 2)
+    return fail(MLXP_ERR_INVALID, "shape too large");
+  if (B == 0 || Sq == 0) return MLXP_OK;
+  const int64_t* st[8] = {q_strides, k_strides, v_strides, o_strides, do_strides, dq_strides,
+                          dk_strides, dv_strides};
+  for (const int64_t* a : st) {
+    if (!a) return fail(MLXP_ERR_INVALID, "stride arrays must be non-null");
+    if (a[3] != 1) return fail(MLXP_ERR_INVALID, "head_dim stride must be 1");
+  }
+  if (!q || !o || !dout || !lse || !dq || (Skv > 0 && (!k || !v || !dk || !dv)))
+    return fail(MLXP_ERR_INVALID, "tensor pointers must be non-null");
+  Problem pr{dtype, B, H, Sq, Skv, D, causal ? 1 : 0, window_left, window_right, q_pos_offset,
+             kv_pos_offset, H_kv};
+  const size_t need = bwd_workspace(pr);
+  if (workspace == nullptr || ws_bytes < need)
+    return fail(MLXP_ERR_WORKSPACE, "attention backward needs %zu bytes of workspace, got %zu",
+                need, ws_bytes);
+  if (reinterpret_cast<uintptr_t>(workspace) % 256)
+    return fail(MLXP_ERR_INVALID, "workspace must be 256-byte aligned");
+  BwdParams bp{};
+  bp.B = (int)B;
+  bp.H = (int)H;
+  bp.Sq = (int)Sq;
+  bp.Skv = (int)Skv;
+  bp.kv_group = (int)(H / H_kv);
+  bp.q = q;
+  bp.k = k;
+  bp.v = v;
+  bp.o = o;
+  bp.dout = dout;
+  bp.lse = lse;
+  bp.delta = static_cast<float*>(workspace);
+  bp.dq = dq;
+  bp.dk = dk;
+  bp.dv = dv;
+  long long* dst[8][3] = {{&bp.q_sb, &bp.q_sh, &bp.q_ss},    {&bp.k_sb, &bp.k_sh, &bp.k_ss},
+                          {&bp.v_sb, &bp.v_sh, &bp.v_ss},    {&bp.o_sb, &bp.o_sh, &bp.o_ss},
+                          {&bp.do_sb, &bp.do_sh, &bp.do_ss}, {&bp.dq_sb, &bp.dq_sh, &bp.dq_ss},
+                          {&bp.dk_sb, &bp.dk_sh, &bp.dk_ss}, {&bp.dv_sb, &bp.dv_sh, &bp.dv_ss}};
+  for (int t = 0; t < 8; ++t)
+    for (int d = 0; d < 3; ++d) *dst[t][d] = st[t][d];
+  bp.scale = scale;
+  bp.scale_log2 = scale * 1.4426950408889634f;
+  bp.mask = mask_of(pr);
+  cudaStream_t s = static_cast<cudaStream_t>(cuda_stream);
+  if (dtype == MLXP_DTYPE_BF16) return bwd_dispatch_d<__nv_bfloat16>(bp, (int)D, s);
+  if (dtype == MLXP_DTYPE_FP16) return bwd_dispatch_d<__half>(bp, (int)D, s);
+  return bwd_dispatch_d<float>(bp, (int)D, s);
 }
 
 int mlxp_device_status(int* status_out, int reset) {

@@ -68,6 +68,11 @@ _SIGNATURES = {
     "mlxp_rope_qk": (ctypes.c_int, [_p, _p, _p, _p, ctypes.c_int, _i64, _i64, _i64, _i64, _i64,
                                     _i64, _i64x4, _i64x4, _i64x4, _i64x4, _p, _p, _i64, _i64,
                                     _i64, _p]),
+    "mlxp_attn_bwd": (ctypes.c_int, [
+        _p, _p, _p, _p, _p, _p, _p, _p, _p, ctypes.c_int, _i64, _i64, _i64, _i64, _i64, _i64,
+        _i64x4, _i64x4, _i64x4, _i64x4, _i64x4, _i64x4, _i64x4, _i64x4, ctypes.c_float,
+        ctypes.c_int, _i64, _i64, _i64, _i64, _p, ctypes.c_size_t, _p]),
+    "mlxp_attn_bwd_workspace_size": (ctypes.c_size_t, [ctypes.c_int, _i64, _i64, _i64, _i64, _i64]),
     "mlxp_paged_attn": (ctypes.c_int, [
         _p, _p, _p, _p, _p, _p, _p, ctypes.c_int, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
         _i64, _i64x4, _i64x4, _i64, _i64x4, ctypes.c_float, ctypes.c_int, _i64, _p,

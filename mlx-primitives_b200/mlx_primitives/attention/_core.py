@@ -48,7 +48,85 @@ def attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, layo
     kpos <= qpos, window_left keeps qpos - kpos <= window_left, window_right keeps
     kpos - qpos <= window_right (-1 = unbounded).  Returns O with q's layout and dtype and,
     if return_lse, the fp32 log-sum-exp [B, H, Sq].
+
+    Differentiable: when autograd records and q, k or v requires grad, the backward runs the
+    library's backward kernels (mlxp_attn_bwd) from the saved O and log-sum-exp.
     """
+    kw = dict(layout=layout, scale=scale, causal=causal, window_left=window_left,
+              window_right=window_right, q_offset=q_offset, kv_offset=kv_offset,
+              kv_splits=kv_splits)
+    if torch.is_grad_enabled() and any(t.requires_grad for t in (q, k, v)):
+        if q.device.type != "cuda":
+            raise NotImplementedError("attention gradients need CUDA tensors (host tensors are "
+                                      "only staged for the forward)")
+        out, lse = _AttentionFn.apply(q, k, v, kw)
+        return (out, lse) if return_lse else out
+    return _forward_impl(q, k, v, return_lse=return_lse, **kw)
+
+
+class _AttentionFn(torch.autograd.Function):
+    """Forward through the attention kernels, backward through mlxp_attn_bwd."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, kw):
+        out, lse = _forward_impl(q, k, v, return_lse=True, **kw)
+        ctx.kw = kw
+        ctx.save_for_backward(q, k, v, out, lse)
+        ctx.mark_non_differentiable(lse)
+        return out, lse
+
+    @staticmethod
+    def backward(ctx, dout, _dlse):
+        q, k, v, out, lse = ctx.saved_tensors
+        dq, dk, dv = attention_backward(q, k, v, out, lse, dout, **ctx.kw)
+        return dq, dk, dv, None
+
+
+_BWD_HEAD_DIMS = (32, 64, 128)
+
+
+def attention_backward(q, k, v, out, lse, dout, *, layout: str, scale: float, causal: bool,
+                       window_left: int = -1, window_right: int = -1, q_offset: int = 0,
+                       kv_offset: int = 0, kv_splits: int = 1):
+    """dQ, dK, dV of attention_forward (same arguments) from its output and log-sum-exp."""
+    B, H, Sq, D = _dims(q, layout)
+    _, Hkv, Skv, _ = _dims(k, layout)
+    Dp = next((c for c in _BWD_HEAD_DIMS if D <= c), None)
+    if Dp is None:
+        raise ValueError(f"head_dim={D} exceeds the kernel limit of {MAX_HEAD_DIM}")
+    if dout is None:
+        dout = torch.zeros_like(out)
+    dout = dout.to(q.dtype)
+    ts = [q, k, v, out, dout]
+    if Dp != D:
+        ts = [torch.nn.functional.pad(t, (0, Dp - D)) for t in ts]
+    q_, k_, v_, o_, do_ = (t if t.stride(-1) == 1 else t.contiguous() for t in ts)
+    do_ = do_.contiguous()
+    dq = torch.empty(q_.shape, dtype=q.dtype, device=q.device)
+    dk = torch.empty(k_.shape, dtype=k.dtype, device=q.device)
+    dv = torch.empty(v_.shape, dtype=v.dtype, device=q.device)
+    L = _lib.lib()
+    dt = _lib.DTYPE_CODES[q.dtype]
+    with torch.cuda.device(q.device):
+        ws_bytes = L.mlxp_attn_bwd_workspace_size(dt, B, H, Sq, Skv, Dp)
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
+        st = [_lib.strides4(t, layout) for t in (q_, k_, v_, o_, do_, dq, dk, dv)]
+        rc = L.mlxp_attn_bwd(q_.data_ptr(), k_.data_ptr(), v_.data_ptr(), o_.data_ptr(),
+                             do_.data_ptr(), lse.contiguous().data_ptr(), dq.data_ptr(),
+                             dk.data_ptr(), dv.data_ptr(), dt, B, H, Hkv, Sq, Skv, Dp, *st,
+                             ctypes.c_float(scale), int(causal), window_left, window_right,
+                             q_offset, kv_offset, ws.data_ptr(), ws_bytes,
+                             _lib.stream_handle(q.device))
+    _lib.check(rc, "mlxp_attn_bwd")
+    if Dp != D:
+        dq, dk, dv = dq[..., :D], dk[..., :D], dv[..., :D]
+    return dq, dk, dv
+
+
+def _forward_impl(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, layout: str,
+                  scale: float, causal: bool, window_left: int = -1, window_right: int = -1,
+                  q_offset: int = 0, kv_offset: int = 0, kv_splits: int = 1,
+                  return_lse: bool = False):
     if q.dtype not in _lib.DTYPE_CODES:
         raise ValueError(f"unsupported dtype {q.dtype}; expected float32, bfloat16 or float16")
     if q.device.type == "cpu":

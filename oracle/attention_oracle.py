@@ -353,6 +353,44 @@ def lse_merge(o_parts, lse_parts):
 
 
 # ----------------------------------------------------------------------------------------
+# Backward: the gradient the reference takes by MLX autodiff through its forward
+# ----------------------------------------------------------------------------------------
+def attention_bwd_bhsd(q, k, v, dout, scale: float, causal: bool = False, window_left: int = -1,
+                       window_right: int = -1, q_offset: int = 0, kv_offset: int = 0):
+    """dQ, dK, dV (fp64, BHSD) of O = softmax(scale * Q K^T + mask) V for the loss
+    sum(dout * O), by the chain rule written out: P = softmax(S), dV = P^T dO, dP = dO V^T,
+    dS = P * (dP - rowsum(dO * O)), dQ = scale dS K, dK = scale dS^T Q.  K/V may have fewer
+    heads than Q (grouped heads: query head h reads K/V head h // (H / H_kv)); their gradients
+    sum over the query heads that read them.  Rows with no admissible key contribute nothing.
+    This is what autodiff of the reference's forward (flash.py:52-316 under mx.grad) computes;
+    tests/test_oracle_backward.py checks it against torch autograd of the dense definition."""
+    q, k, v, dout = (np.asarray(t, dtype=np.float64) for t in (q, k, v, dout))
+    B, H, Sq, D = q.shape
+    Hkv, Skv = k.shape[1], k.shape[2]
+    g = H // Hkv
+    ok = admissible(Sq, Skv, causal, window_left, window_right, q_offset, kv_offset)
+    dq = np.zeros_like(q)
+    dk = np.zeros_like(k)
+    dv = np.zeros_like(v)
+    for b in range(B):
+        for h in range(H):
+            kh, vh = k[b, h // g], v[b, h // g]
+            s = np.where(ok, (q[b, h] @ kh.T) * scale, -np.inf)
+            m = s.max(axis=1, keepdims=True)
+            m = np.where(np.isfinite(m), m, 0.0)
+            e = np.exp(s - m)
+            den = e.sum(axis=1, keepdims=True)
+            p = e / np.where(den > 0, den, 1.0)
+            o = p @ vh
+            dv[b, h // g] += p.T @ dout[b, h]
+            dp = dout[b, h] @ vh.T
+            ds = p * (dp - (dout[b, h] * o).sum(axis=1, keepdims=True))
+            dq[b, h] = scale * ds @ kh
+            dk[b, h // g] += scale * ds.T @ q[b, h]
+    return dq, dk, dv
+
+
+# ----------------------------------------------------------------------------------------
 # Paged K/V attention (cache/paged_attention.py)
 # ----------------------------------------------------------------------------------------
 def get_alibi_slopes(num_heads: int) -> np.ndarray:
