@@ -8,7 +8,8 @@ head_dim / 2 and the row's position p = offset + s,
     y[..., h:] = x[..., :h] * sin[p] + x[..., h:] * cos[p].
 The rotation runs in libmlxp_attn.so (mlxp_rope / mlxp_rope_qk: one memory-bound kernel, Q and
 K in one launch), in fp32, rounded once to the input dtype.  There is no CPU fallback: host
-tensors are staged through the current CUDA device.
+tensors are staged through the current CUDA device.  Differentiable in x (q, k): the rotation
+is orthogonal, so its gradient is the same kernel with the sine table negated.
 """
 
 from __future__ import annotations
@@ -64,6 +65,39 @@ def _check(x: torch.Tensor, name: str = "Input"):
         raise ValueError(f"unsupported dtype {x.dtype}")
 
 
+def _rope_raw(xd: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, offset: int) -> torch.Tensor:
+    """mlxp_rope on a device tensor with fp32 device caches."""
+    if xd.stride(-1) != 1:
+        xd = xd.contiguous()
+    y = torch.empty_like(xd)
+    B, S, H, D = xd.shape
+    dev = xd.device
+    with torch.cuda.device(dev):
+        rc = _lib.lib().mlxp_rope(xd.data_ptr(), y.data_ptr(), _lib.DTYPE_CODES[xd.dtype], B, H, S,
+                                  D, _lib.strides4(xd, "BSHD"), _lib.strides4(y, "BSHD"),
+                                  cos.data_ptr(), sin.data_ptr(), cos.shape[0], int(offset),
+                                  _lib.stream_handle(dev))
+    _lib.check(rc, "mlxp_rope")
+    return y
+
+
+class _RopeFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, cos, sin, offset):
+        ctx.save_for_backward(cos, sin)
+        ctx.offset = offset
+        return _rope_raw(x, cos, sin, offset)
+
+    @staticmethod
+    def backward(ctx, gy):
+        cos, sin = ctx.saved_tensors
+        return _rope_raw(gy.contiguous(), cos, -sin, ctx.offset), None, None, None
+
+
+def _needs_grad(*ts) -> bool:
+    return torch.is_grad_enabled() and any(t.requires_grad for t in ts)
+
+
 def fast_rope(x: torch.Tensor, cos_cache: torch.Tensor, sin_cache: torch.Tensor,
               offset: int = 0) -> torch.Tensor:
     """RoPE of x (batch, seq_len, num_heads, head_dim) at positions offset .. offset+seq_len-1."""
@@ -71,19 +105,14 @@ def fast_rope(x: torch.Tensor, cos_cache: torch.Tensor, sin_cache: torch.Tensor,
     dev = _device_of(x)
     host = x.device.type == "cpu"
     xd = x.to(dev) if host else x
-    if xd.stride(-1) != 1:
-        xd = xd.contiguous()
     cos, sin = _f32_cache(cos_cache, dev), _f32_cache(sin_cache, dev)
     if cos.shape != sin.shape or cos.ndim != 2 or cos.shape[1] != x.shape[-1] // 2:
         raise ValueError("cos/sin caches must both be (max_seq, head_dim // 2)")
-    y = torch.empty_like(xd)
-    B, S, H, D = xd.shape
-    with torch.cuda.device(dev):
-        rc = _lib.lib().mlxp_rope(xd.data_ptr(), y.data_ptr(), _lib.DTYPE_CODES[x.dtype], B, H, S, D,
-                                  _lib.strides4(xd, "BSHD"), _lib.strides4(y, "BSHD"),
-                                  cos.data_ptr(), sin.data_ptr(), cos.shape[0], int(offset),
-                                  _lib.stream_handle(dev))
-    _lib.check(rc, "mlxp_rope")
+    if _needs_grad(x):
+        if host:
+            raise NotImplementedError("RoPE gradients need CUDA tensors")
+        return _RopeFn.apply(xd, cos.detach(), sin.detach(), int(offset))
+    y = _rope_raw(xd, cos, sin, offset)
     return y.cpu() if host else y
 
 
@@ -108,22 +137,49 @@ def fast_rope_qk(q: torch.Tensor, k: torch.Tensor, cos_cache: torch.Tensor,
     dev = _device_of(q, k)
     host = q.device.type == "cpu"
     qd, kd = (t.to(dev) if t.device.type == "cpu" else t for t in (q, k))
-    qd, kd = (t if t.stride(-1) == 1 else t.contiguous() for t in (qd, kd))
     cos, sin = _f32_cache(cos_cache, dev), _f32_cache(sin_cache, dev)
     if cos.shape != sin.shape or cos.ndim != 2 or cos.shape[1] != q.shape[-1] // 2:
         raise ValueError("cos/sin caches must both be (max_seq, head_dim // 2)")
+    k_off = int(offset if k_offset is None else k_offset)
+    if _needs_grad(q, k):
+        if host:
+            raise NotImplementedError("RoPE gradients need CUDA tensors")
+        return _RopeQKFn.apply(qd, kd, cos.detach(), sin.detach(), int(offset), k_off)
+    qo, ko = _rope_qk_raw(qd, kd, cos, sin, int(offset), k_off)
+    return (qo.cpu(), ko.cpu()) if host else (qo, ko)
+
+
+def _rope_qk_raw(qd, kd, cos, sin, offset: int, k_offset: int):
+    """mlxp_rope_qk on device tensors with fp32 device caches."""
+    qd, kd = (t if t.stride(-1) == 1 else t.contiguous() for t in (qd, kd))
     qo, ko = torch.empty_like(qd), torch.empty_like(kd)
     B, Sq, Hq, D = qd.shape
     _, Sk, Hk, _ = kd.shape
+    dev = qd.device
     with torch.cuda.device(dev):
         rc = _lib.lib().mlxp_rope_qk(
-            qd.data_ptr(), kd.data_ptr(), qo.data_ptr(), ko.data_ptr(), _lib.DTYPE_CODES[q.dtype],
+            qd.data_ptr(), kd.data_ptr(), qo.data_ptr(), ko.data_ptr(), _lib.DTYPE_CODES[qd.dtype],
             B, Hq, Hk, Sq, Sk, D, _lib.strides4(qd, "BSHD"), _lib.strides4(kd, "BSHD"),
             _lib.strides4(qo, "BSHD"), _lib.strides4(ko, "BSHD"), cos.data_ptr(), sin.data_ptr(),
-            cos.shape[0], int(offset), int(offset if k_offset is None else k_offset),
-            _lib.stream_handle(dev))
+            cos.shape[0], offset, k_offset, _lib.stream_handle(dev))
     _lib.check(rc, "mlxp_rope_qk")
-    return (qo.cpu(), ko.cpu()) if host else (qo, ko)
+    return qo, ko
+
+
+class _RopeQKFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, cos, sin, offset, k_offset):
+        ctx.save_for_backward(cos, sin)
+        ctx.offsets = (offset, k_offset)
+        return _rope_qk_raw(q, k, cos, sin, offset, k_offset)
+
+    @staticmethod
+    def backward(ctx, gq, gk):
+        cos, sin = ctx.saved_tensors
+        gq = torch.zeros_like(gq) if gq is None else gq.contiguous()
+        gk = torch.zeros_like(gk) if gk is None else gk.contiguous()
+        dq, dk = _rope_qk_raw(gq, gk, cos, -sin, *ctx.offsets)
+        return dq, dk, None, None, None, None
 
 
 def rope_qk(q: torch.Tensor, k: torch.Tensor, cos_cache: torch.Tensor, sin_cache: torch.Tensor,

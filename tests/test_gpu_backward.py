@@ -146,3 +146,42 @@ def test_no_grad_path_unchanged():
         o1 = mp.flash_attention(q, k, v, causal=True)
     o2 = mp.flash_attention(q.detach(), k.detach(), v.detach(), causal=True)
     assert o1.grad_fn is None and torch.equal(o1, o2)
+
+
+def _rope_t(x, cos, sin, off):
+    h = x.shape[-1] // 2
+    c = cos[off:off + x.shape[1]][None, :, None, :]
+    s = sin[off:off + x.shape[1]][None, :, None, :]
+    x1, x2 = x[..., :h], x[..., h:]
+    return torch.cat([x1 * c - x2 * s, x1 * s + x2 * c], dim=-1)
+
+
+def test_fused_rope_attention_gradients():
+    """RoPE (orthogonal: its gradient is the inverse rotation) then attention, against fp64
+    torch autograd of the same composition."""
+    from mlx_primitives.kernels import fused_rope_attention, precompute_rope_cache
+    (q, k, v, do), (nq, nk, nv, ndo) = _make((1, 90, 2, 64), (1, 120, 2, 64), torch.float32, 19)
+    out = fused_rope_attention(q, k, v, q_offset=30, kv_offset=0, causal=True)
+    out.backward(do)
+    cos, sin = (t.double().cpu() for t in precompute_rope_cache(150, 64))
+    tq, tk, tv = (torch.tensor(a, dtype=torch.float64, requires_grad=True) for a in (nq, nk, nv))
+    qr, kr = _rope_t(tq, cos, sin, 30), _rope_t(tk, cos, sin, 0)
+    s = torch.einsum("bqhd,bkhd->bhqk", qr, kr) * 0.125
+    ok = torch.from_numpy(O.admissible(90, 120, True, q_offset=30))
+    p = torch.softmax(s.masked_fill(~ok, float("-inf")), dim=-1)
+    ref = torch.einsum("bhqk,bkhd->bqhd", p, tv)
+    (ref * torch.tensor(ndo, dtype=torch.float64)).sum().backward()
+    _check((q.grad, k.grad, v.grad), (tq.grad.numpy(), tk.grad.numpy(), tv.grad.numpy()),
+           torch.float32)
+
+
+def test_rope_gradient_is_inverse_rotation():
+    from mlx_primitives.kernels import precompute_rope_cache, rope
+    (x, _, _, g), (nx, _, _, ng) = _make((2, 40, 3, 64), (2, 40, 3, 64), torch.float32, 23)
+    cos, sin = precompute_rope_cache(64, 64)
+    rope(x, cos, sin, 7).backward(g)
+    tx = torch.tensor(nx, dtype=torch.float64, requires_grad=True)
+    _rope_t(tx, cos.double().cpu(), sin.double().cpu(), 7).backward(
+        torch.tensor(ng, dtype=torch.float64))
+    err = float((x.grad.double().cpu() - tx.grad).abs().max())
+    assert err <= 1e-5
