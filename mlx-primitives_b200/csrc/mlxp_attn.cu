@@ -597,38 +597,67 @@ int paged_validate(const PagedProblem& pp) {
   return MLXP_OK;
 }
 
-// Shares of the block-table slots per query row: about four CTAs per SM in all, at least 64
-// key positions per share, at most 65535 shares (grid y).
+// Shares of the block-table slots per (query row, head).  A CTA per (row, head, share), about
+// `per_sm` resident per SM: pick the share count that minimises (waves of CTAs) x (blocks per
+// share + a per-CTA overhead of ~4 blocks), fewer shares on ties.  At most 65535 (grid y).
 int paged_splits(const PagedProblem& pp, int64_t kv_splits, int sms) {
-  const long long rows = pp.B * pp.Sq;
-  if (rows <= 0 || pp.max_blocks <= 1 || kv_splits == 1) return 1;
-  long long splits;
+  const long long ctas = pp.B * pp.Sq * pp.H;
+  if (ctas <= 0 || pp.max_blocks <= 1 || kv_splits == 1) return 1;
+  long long splits = 1;
   if (kv_splits > 1) {
     splits = std::min<long long>(kv_splits, pp.max_blocks);
   } else {
-    splits = (4LL * sms + rows - 1) / rows;
-    if (splits <= 1) return 1;
-    const long long min_bps = std::max<long long>(1, (64 + pp.block_size - 1) / pp.block_size);
-    const long long bps = std::max<long long>((pp.max_blocks + splits - 1) / splits, min_bps);
-    splits = (pp.max_blocks + bps - 1) / bps;
+    const int per_sm = pp.dtype == MLXP_DTYPE_FP32 ? 1 : 3;
+    const long long slots = (long long)sms * per_sm;
+    long long best = -1;
+    for (long long s = 1; s <= std::min<long long>(pp.max_blocks, 256); ++s) {
+      const long long bps = (pp.max_blocks + s - 1) / s;
+      const long long se = (pp.max_blocks + bps - 1) / bps;
+      const long long waves = (ctas * se + slots - 1) / slots;
+      const long long cost = waves * (bps + 4);
+      if (best < 0 || cost < best) {
+        best = cost;
+        splits = se;
+      }
+    }
   }
   splits = std::min<long long>(splits, 65535);
   const long long bps = (pp.max_blocks + splits - 1) / splits;
   return (int)((pp.max_blocks + bps - 1) / bps);
 }
 
+// Workspace of several shares: fp32 partials, their log2-sum-exps and the (row, head) counters.
 size_t paged_workspace(const PagedProblem& pp, int splits) {
   if (splits <= 1) return 0;
   const size_t rows = (size_t)splits * pp.B * pp.H * pp.Sq;
-  return (rows * pp.D * 4 + 255) / 256 * 256 + rows * 4;
+  const size_t o_bytes = (rows * pp.D * 4 + 255) / 256 * 256;
+  const size_t l_bytes = (rows * 4 + 255) / 256 * 256;
+  return o_bytes + l_bytes + (size_t)pp.B * pp.H * pp.Sq * 4;
+}
+
+template <typename T, int LPR>
+int paged_launch_d(const PagedParams& p, dim3 grid, cudaStream_t s) {
+  constexpr int smem = paged_smem_bytes<T>(LPR * 4);
+  static std::atomic<unsigned long long> attr_done{0};  // one bit per device
+  int dev;
+  if (int rc = current_device(dev)) return rc;
+  cudaError_t e;
+  if (!(attr_done.load() >> dev & 1ull)) {
+    e = cudaFuncSetAttribute(paged_attn_kernel<T, LPR>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(paged attention)");
+    attr_done.fetch_or(1ull << dev);
+  }
+  paged_attn_kernel<T, LPR><<<grid, 32 * kPagedWarps, smem, s>>>(p);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? MLXP_OK : cuda_fail(e, "paged attention launch");
 }
 
 template <typename T>
-cudaError_t paged_launch_t(const PagedParams& p, int LPR, dim3 grid, cudaStream_t s) {
-  if (LPR == 32) paged_attn_kernel<T, 32><<<grid, 256, 0, s>>>(p);
-  else if (LPR == 16) paged_attn_kernel<T, 16><<<grid, 256, 0, s>>>(p);
-  else paged_attn_kernel<T, 8><<<grid, 256, 0, s>>>(p);
-  return cudaGetLastError();
+int paged_launch_t(const PagedParams& p, int LPR, dim3 grid, cudaStream_t s) {
+  if (LPR == 32) return paged_launch_d<T, 32>(p, grid, s);
+  if (LPR == 16) return paged_launch_d<T, 16>(p, grid, s);
+  return paged_launch_d<T, 8>(p, grid, s);
 }
 
 
@@ -940,23 +969,25 @@ int mlxp_paged_attn(const void* q, const void* k_pool, const void* v_pool,
   if (p.blocks_per_split < 1) p.blocks_per_split = 1;
   p.causal = causal ? 1 : 0;
   p.scale_log2 = scale * 1.4426950408889634f;
+  p.splits = splits;
+  cudaStream_t s = static_cast<cudaStream_t>(cuda_stream);
   if (splits > 1) {
     const size_t rows = (size_t)splits * B * H * Sq;
-    p.o_part = static_cast<float*>(workspace);
-    p.lse_part = reinterpret_cast<float*>(static_cast<char*>(workspace) +
-                                          (rows * D * 4 + 255) / 256 * 256);
+    char* w = static_cast<char*>(workspace);
+    const size_t o_bytes = (rows * D * 4 + 255) / 256 * 256;
+    const size_t l_bytes = (rows * 4 + 255) / 256 * 256;
+    p.o_part = reinterpret_cast<float*>(w);
+    p.lse_part = reinterpret_cast<float*>(w + o_bytes);
+    p.counters = reinterpret_cast<unsigned*>(w + o_bytes + l_bytes);
+    cudaError_t e = cudaMemsetAsync(p.counters, 0, (size_t)B * H * Sq * 4, s);
+    if (e != cudaSuccess) return cuda_fail(e, "paged attention counter reset");
   }
-  cudaStream_t s = static_cast<cudaStream_t>(cuda_stream);
-  const dim3 grid((unsigned)(B * Sq), (unsigned)splits);
+  if ((long long)B * Sq * H > INT32_MAX) return fail(MLXP_ERR_INVALID, "paged shape too large");
+  const dim3 grid((unsigned)(B * Sq * H), (unsigned)splits);
   const int LPR = (int)(D / 4);
-  cudaError_t e;
-  if (dtype == MLXP_DTYPE_BF16) e = paged_launch_t<__nv_bfloat16>(p, LPR, grid, s);
-  else if (dtype == MLXP_DTYPE_FP16) e = paged_launch_t<__half>(p, LPR, grid, s);
-  else e = paged_launch_t<float>(p, LPR, grid, s);
-  if (e != cudaSuccess) return cuda_fail(e, "paged attention launch");
-  if (splits <= 1) return MLXP_OK;
-  Problem pr{dtype, B, H, Sq, 0, D, 0, -1, -1, 0, 0};
-  return merge_dispatch(p.o_part, p.lse_part, splits, o, nullptr, pr, o_strides, s);
+  if (dtype == MLXP_DTYPE_BF16) return paged_launch_t<__nv_bfloat16>(p, LPR, grid, s);
+  if (dtype == MLXP_DTYPE_FP16) return paged_launch_t<__half>(p, LPR, grid, s);
+  return paged_launch_t<float>(p, LPR, grid, s);
 }
 
 size_t mlxp_attn_bwd_workspace_size(int dtype, int64_t B, int64_t H, int64_t Sq, int64_t Skv,
