@@ -369,7 +369,7 @@ def bench_paged(args, c, world, rank, local):
              o.data_ptr(), dt, B, H, 1, D, H, nblk, bs, bt.shape[1], _lib.strides4(q, "BSHD"),
              (ctypes.c_int64 * 4)(*kp.stride()), bt.stride(0), _lib.strides4(o, "BSHD"),
              ctypes.c_float(D ** -0.5), 1, 0, ws.data_ptr(), ws_bytes, stream.cuda_stream)
-    launches = 2 if ws_bytes else 1  # paged kernel (+ LSE merge when the contexts are split)
+    launches = 1  # one paged-attention kernel per call (shares merged inside it)
 
     def barrier():
         if world > 1:
@@ -441,7 +441,7 @@ def bench_paged(args, c, world, rank, local):
                 "bound": "hbm", "achieved": achieved_gbs, "peak": hbm, "unit": "GB/s",
                 "frac": achieved_gbs / hbm, "traffic": NCU_TRAFFIC_BYTES.get(args.config),
                 "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + write.sum)",
-                "kernel": "paged_attn_kernel + lse_merge_kernel (one C-ABI call)",
+                "kernel": "paged_attn_tma_kernel (one C-ABI call: counter reset + kernel)",
                 "kernel_ms": ms_kernel,
                 "peak_source": f"{peak_src}: hbm_gbs",
                 "algorithmic_bytes_per_launch": min_bytes,

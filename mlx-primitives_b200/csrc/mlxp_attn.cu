@@ -597,46 +597,100 @@ int paged_validate(const PagedProblem& pp) {
   return MLXP_OK;
 }
 
-// Shares of the block-table slots per (query row, head).  A CTA per (row, head, share), about
-// `per_sm` resident per SM: pick the share count that minimises (waves of CTAs) x (blocks per
-// share + a per-CTA overhead of ~4 blocks), fewer shares on ties.  At most 65535 (grid y).
-int paged_splits(const PagedProblem& pp, int64_t kv_splits, int sms) {
-  const long long ctas = pp.B * pp.Sq * pp.H;
-  if (ctas <= 0 || pp.max_blocks <= 1 || kv_splits == 1) return 1;
-  long long splits = 1;
-  if (kv_splits > 1) {
-    splits = std::min<long long>(kv_splits, pp.max_blocks);
-  } else {
-    const int per_sm = pp.dtype == MLXP_DTYPE_FP32 ? 1 : 3;
-    const long long slots = (long long)sms * per_sm;
-    long long best = -1;
-    for (long long s = 1; s <= std::min<long long>(pp.max_blocks, 256); ++s) {
-      const long long bps = (pp.max_blocks + s - 1) / s;
-      const long long se = (pp.max_blocks + bps - 1) / bps;
-      const long long waves = (ctas * se + slots - 1) / slots;
-      const long long cost = waves * (bps + 4);
-      if (best < 0 || cost < best) {
-        best = cost;
-        splits = se;
-      }
-    }
-  }
-  splits = std::min<long long>(splits, 65535);
-  const long long bps = (pp.max_blocks + splits - 1) / splits;
-  return (int)((pp.max_blocks + bps - 1) / bps);
+// Grid of the stream-K decomposition (paged_attn.cuh).  kv_splits: 1 = one CTA per (row, head)
+// pair (no partials), n > 1 = n CTAs per pair, 0 = automatic: the resident CTA count (3 per SM
+// for 16-bit types, 1 for fp32, set by shared memory), or fewer so that every CTA gets at least
+// 4 blocks.
+// The TMA kernel (paged_attn_tma_kernel) serves bf16/fp16 pools whose block size is a multiple
+// of its 16-row chunk; everything else runs the cp.async kernel.
+bool paged_tma_shape(const PagedProblem& pp) {
+  return pp.dtype != MLXP_DTYPE_FP32 && pp.block_size % kTmaRows == 0 && pp.num_blocks >= 1;
 }
 
-// Workspace of several shares: fp32 partials, their log2-sum-exps and the (row, head) counters.
-size_t paged_workspace(const PagedProblem& pp, int splits) {
-  if (splits <= 1) return 0;
-  const size_t rows = (size_t)splits * pp.B * pp.H * pp.Sq;
-  const size_t o_bytes = (rows * pp.D * 4 + 255) / 256 * 256;
-  const size_t l_bytes = (rows * 4 + 255) / 256 * 256;
-  return o_bytes + l_bytes + (size_t)pp.B * pp.H * pp.Sq * 4;
+long long paged_grid(const PagedProblem& pp, int64_t kv_splits, int sms) {
+  const long long pairs = pp.B * pp.Sq * pp.H;
+  const long long total = pairs * pp.max_blocks;
+  if (total <= 0) return 0;
+  const int per_sm = paged_tma_shape(pp) ? 1 : (pp.dtype == MLXP_DTYPE_FP32 ? 1 : 3);
+  long long g;
+  if (kv_splits == 1) g = pairs;
+  else if (kv_splits > 1) g = pairs * std::min<long long>(kv_splits, pp.max_blocks);
+  else g = std::min<long long>((long long)sms * per_sm, std::max<long long>(1, total / 4));
+  return std::max<long long>(1, std::min<long long>(g, total));
+}
+
+// Tensor map of a pool as {D, kv_heads, block_size, num_blocks} with a {D, 1, 16, 1} box.
+// Returns false when the pool's address or strides do not suit TMA.
+bool make_pool_tmap(const void* ptr, int dtype, const PagedProblem& pp, const int64_t ps[4],
+                    CUtensorMap* map) {
+  if (get_encode_fn() != MLXP_OK) return false;
+  const int es = 2;
+  if (reinterpret_cast<uintptr_t>(ptr) % 16) return false;
+  int64_t sh = ps[2], st = ps[1], sb = ps[0];
+  if (pp.Hkv == 1) sh = (pp.D * es + 15) / 16 * 16 / es;  // unused dimension: any legal stride
+  if (pp.num_blocks == 1 && sb <= 0) sb = st * pp.block_size;
+  for (int64_t x : {sh, st, sb})
+    if (x <= 0 || (x * es) % 16) return false;
+  cuuint64_t gdim[4] = {(cuuint64_t)pp.D, (cuuint64_t)pp.Hkv, (cuuint64_t)pp.block_size,
+                        (cuuint64_t)pp.num_blocks};
+  cuuint64_t gstride[3] = {(cuuint64_t)(sh * es), (cuuint64_t)(st * es), (cuuint64_t)(sb * es)};
+  cuuint32_t box[4] = {(cuuint32_t)pp.D, 1, (cuuint32_t)kTmaRows, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType dt =
+      dtype == MLXP_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = g_encode(map, dt, 4, const_cast<void*>(ptr), gdim, gstride, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
 }
 
 template <typename T, int LPR>
-int paged_launch_d(const PagedParams& p, dim3 grid, cudaStream_t s) {
+int paged_tma_launch_d(const CUtensorMap& mk, const CUtensorMap& mv, const PagedParams& p,
+                       unsigned grid, cudaStream_t s) {
+  constexpr int smem = paged_tma_smem<T, LPR * 4>();
+  static std::atomic<unsigned long long> attr_done{0};  // one bit per device
+  int dev;
+  if (int rc = current_device(dev)) return rc;
+  cudaError_t e;
+  if (!(attr_done.load() >> dev & 1ull)) {
+    e = cudaFuncSetAttribute(paged_attn_tma_kernel<T, LPR>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(paged attention, TMA)");
+    attr_done.fetch_or(1ull << dev);
+  }
+  paged_attn_tma_kernel<T, LPR><<<grid, 32 * kTmaWarps, smem, s>>>(mk, mv, p);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? MLXP_OK : cuda_fail(e, "paged attention launch (TMA)");
+}
+
+template <typename T>
+int paged_tma_launch_t(const CUtensorMap& mk, const CUtensorMap& mv, const PagedParams& p,
+                       int LPR, unsigned grid, cudaStream_t s) {
+  if (LPR == 32) return paged_tma_launch_d<T, 32>(mk, mv, p, grid, s);
+  if (LPR == 16) return paged_tma_launch_d<T, 16>(mk, mv, p, grid, s);
+  return paged_tma_launch_d<T, 8>(mk, mv, p, grid, s);
+}
+
+// Partial slots per pair: a pair of max_blocks slots meets at most this many CTA ranges.
+long long paged_max_parts(const PagedProblem& pp, long long grid) {
+  const long long total = pp.B * pp.Sq * pp.H * pp.max_blocks;
+  const long long per = total / grid;  // >= 1: grid <= total
+  return (pp.max_blocks + per - 1) / per + 1;
+}
+
+// Workspace: fp32 partials and log2-sum-exps per (pair, slot), then the pair counters.  None
+// when every CTA owns whole pairs.
+size_t paged_workspace(const PagedProblem& pp, long long grid) {
+  const long long pairs = pp.B * pp.Sq * pp.H;
+  if (grid <= 0 || grid == pairs) return 0;
+  const size_t rows = (size_t)pairs * paged_max_parts(pp, grid);
+  const size_t o_bytes = (rows * pp.D * 4 + 255) / 256 * 256;
+  const size_t l_bytes = (rows * 4 + 255) / 256 * 256;
+  return o_bytes + l_bytes + (size_t)pairs * 4;
+}
+
+template <typename T, int LPR>
+int paged_launch_d(const PagedParams& p, unsigned grid, cudaStream_t s) {
   constexpr int smem = paged_smem_bytes<T>(LPR * 4);
   static std::atomic<unsigned long long> attr_done{0};  // one bit per device
   int dev;
@@ -654,7 +708,7 @@ int paged_launch_d(const PagedParams& p, dim3 grid, cudaStream_t s) {
 }
 
 template <typename T>
-int paged_launch_t(const PagedParams& p, int LPR, dim3 grid, cudaStream_t s) {
+int paged_launch_t(const PagedParams& p, int LPR, unsigned grid, cudaStream_t s) {
   if (LPR == 32) return paged_launch_d<T, 32>(p, grid, s);
   if (LPR == 16) return paged_launch_d<T, 16>(p, grid, s);
   return paged_launch_d<T, 8>(p, grid, s);
@@ -894,7 +948,7 @@ size_t mlxp_paged_attn_workspace_size(int dtype, int64_t B, int64_t H, int64_t S
   if (paged_validate(pp) != MLXP_OK) return 0;
   int sms = 148;
   if (kv_splits == 0 && device_info(nullptr, &sms) != MLXP_OK) sms = 148;
-  return paged_workspace(pp, paged_splits(pp, kv_splits, sms));
+  return paged_workspace(pp, paged_grid(pp, kv_splits, sms));
 }
 
 int mlxp_paged_attn(const void* q, const void* k_pool, const void* v_pool,
@@ -932,8 +986,8 @@ int mlxp_paged_attn(const void* q, const void* k_pool, const void* v_pool,
       return fail(MLXP_ERR_INVALID, "q and pool strides must be non-negative multiples of 4 elements");
   int sms = 148;
   if (int rc = device_info(nullptr, &sms)) return rc;
-  const int splits = paged_splits(pp, kv_splits, sms);
-  const size_t need = paged_workspace(pp, splits);
+  const long long grid = paged_grid(pp, kv_splits, sms);
+  const size_t need = paged_workspace(pp, grid);
   if (need > 0 && (workspace == nullptr || ws_bytes < need))
     return fail(MLXP_ERR_WORKSPACE, "paged attention needs %zu bytes of workspace, got %zu", need,
                 ws_bytes);
@@ -965,29 +1019,46 @@ int mlxp_paged_attn(const void* q, const void* k_pool, const void* v_pool,
   p.num_blocks = (int)num_blocks;
   p.block_size = (int)block_size;
   p.max_blocks = (int)max_blocks;
-  p.blocks_per_split = (int)((max_blocks + splits - 1) / splits);
-  if (p.blocks_per_split < 1) p.blocks_per_split = 1;
   p.causal = causal ? 1 : 0;
   p.scale_log2 = scale * 1.4426950408889634f;
-  p.splits = splits;
   cudaStream_t s = static_cast<cudaStream_t>(cuda_stream);
-  if (splits > 1) {
-    const size_t rows = (size_t)splits * B * H * Sq;
+  if (grid == 0) {  // no block-table slots: every row has no admissible key
+    Problem pr{dtype, B, H, Sq, 0, D, 0, -1, -1, 0, 0};
+    return fill_empty(pr, o, nullptr, o_strides, s);
+  }
+  if (grid > INT32_MAX) return fail(MLXP_ERR_INVALID, "paged shape too large");
+  p.grid = (int)grid;
+  p.total = B * Sq * H * max_blocks;
+  if (need > 0) {
+    const long long pairs = B * Sq * H;
+    p.max_parts = (int)paged_max_parts(pp, grid);
+    const size_t rows = (size_t)pairs * p.max_parts;
     char* w = static_cast<char*>(workspace);
     const size_t o_bytes = (rows * D * 4 + 255) / 256 * 256;
     const size_t l_bytes = (rows * 4 + 255) / 256 * 256;
     p.o_part = reinterpret_cast<float*>(w);
     p.lse_part = reinterpret_cast<float*>(w + o_bytes);
     p.counters = reinterpret_cast<unsigned*>(w + o_bytes + l_bytes);
-    cudaError_t e = cudaMemsetAsync(p.counters, 0, (size_t)B * H * Sq * 4, s);
+    cudaError_t e = cudaMemsetAsync(p.counters, 0, (size_t)pairs * 4, s);
     if (e != cudaSuccess) return cuda_fail(e, "paged attention counter reset");
   }
-  if ((long long)B * Sq * H > INT32_MAX) return fail(MLXP_ERR_INVALID, "paged shape too large");
-  const dim3 grid((unsigned)(B * Sq * H), (unsigned)splits);
   const int LPR = (int)(D / 4);
-  if (dtype == MLXP_DTYPE_BF16) return paged_launch_t<__nv_bfloat16>(p, LPR, grid, s);
-  if (dtype == MLXP_DTYPE_FP16) return paged_launch_t<__half>(p, LPR, grid, s);
-  return paged_launch_t<float>(p, LPR, grid, s);
+  if (paged_tma_shape(pp)) {
+    CUtensorMap mk, mv;
+    if (make_pool_tmap(k_pool, dtype, pp, pool_strides, &mk) &&
+        make_pool_tmap(v_pool, dtype, pp, pool_strides, &mv)) {
+      int* status = nullptr;
+      if (int rc = device_info(&status, nullptr)) return rc;
+      p.status = status;
+      p.timeout_ns = g_timeout_ns.load();
+      if (dtype == MLXP_DTYPE_BF16)
+        return paged_tma_launch_t<__nv_bfloat16>(mk, mv, p, LPR, (unsigned)grid, s);
+      return paged_tma_launch_t<__half>(mk, mv, p, LPR, (unsigned)grid, s);
+    }
+  }
+  if (dtype == MLXP_DTYPE_BF16) return paged_launch_t<__nv_bfloat16>(p, LPR, (unsigned)grid, s);
+  if (dtype == MLXP_DTYPE_FP16) return paged_launch_t<__half>(p, LPR, (unsigned)grid, s);
+  return paged_launch_t<float>(p, LPR, (unsigned)grid, s);
 }
 
 size_t mlxp_attn_bwd_workspace_size(int dtype, int64_t B, int64_t H, int64_t Sq, int64_t Skv,

@@ -71,6 +71,17 @@ def test_decode_matches_oracle(dtype, D, bs):
     assert _maxabs(out, _oracle(*n, bt, ctx, block_size=bs)) <= TOL[dtype]
 
 
+@pytest.mark.parametrize("bs", [8, 24, 48, 64, 128])
+@pytest.mark.parametrize("D", [64, 128])
+def test_decode_block_sizes(bs, D):
+    """Block sizes a multiple of 16 take the TMA kernel (16-row boxes), others the cp.async
+    kernel; both against the oracle."""
+    lens = [5, 130, 777, 2000]
+    t, n, bt, ctx = _case(4, 1, 4, D, 4, bs, lens, torch.bfloat16, seed=bs + D, holes=1)
+    out = _run(t, bt, ctx, block_size=bs)
+    assert _maxabs(out, _oracle(*n, bt, ctx, block_size=bs)) <= 2e-2
+
+
 @pytest.mark.parametrize("kv_splits", [1, 2, 7, 0])
 def test_decode_forced_splits(kv_splits):
     lens = [4000, 123, 2500]
