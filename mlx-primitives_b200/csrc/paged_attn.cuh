@@ -525,27 +525,38 @@ __global__ void __launch_bounds__(32 * kTmaWarps, 1)
         for (int e = 0; e < 4; ++e) a = fmaf(q[e], kx[e], a);
         sc[u] = a;
       }
+      // Reduce-scatter over the LPR lanes of a key group: each halving step keeps half of the
+      // values (the upper half in lanes with that offset bit set) and adds the partner's copy,
+      // so STEPS/2 + STEPS/4 + ... + 1 shuffles replace STEPS * log2(LPR).  Afterwards lane
+      // holds the full score of step u = (lane >> 1) % STEPS (lanes 2u and 2u + 1 alike).
 #pragma unroll
-      for (int off = LPR / 2; off > 0; off >>= 1) {
+      for (int n = STEPS, off = LPR / 2; n > 1; n >>= 1, off >>= 1) {
+        const bool up = (lane & off) != 0;
 #pragma unroll
-        for (int u = 0; u < STEPS; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], off);
+        for (int j = 0; j < n / 2; ++j) {
+          const float send = up ? sc[j] : sc[j + n / 2];
+          const float keep = up ? sc[j + n / 2] : sc[j];
+          sc[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
       }
-      float m_blk = -INFINITY;
-#pragma unroll
-      for (int u = 0; u < STEPS; ++u) {
-        const int t = cc.t0 + u * KPW + g;
-        sc[u] = (t < cc.nt) ? fmaf(slope2, (float)(cc.pos0 + t - q_pos), sc[u]) : -INFINITY;
-        m_blk = fmaxf(m_blk, sc[u]);
+      float sv = sc[0] + __shfl_xor_sync(0xffffffffu, sc[0], 1);
+      {
+        const int t = cc.t0 + ((lane >> 1) & (STEPS - 1)) * KPW + g;
+        sv = (t < cc.nt) ? fmaf(slope2, (float)(cc.pos0 + t - q_pos), sv) : -INFINITY;
       }
+      float m_blk = sv;  // over the warp: every key of the chunk
+#pragma unroll
+      for (int off = 16; off > 1; off >>= 1) m_blk = fmaxf(m_blk, __shfl_xor_sync(0xffffffffu, m_blk, off));
       const float m_new = fmaxf(m, m_blk);
       const float m_use = m_new == -INFINITY ? 0.f : m_new;
       const float alpha = ex2_approx(m - m_use);
       l *= alpha;
 #pragma unroll
       for (int e = 0; e < 4; ++e) o[e] *= alpha;
+      const float pv = ex2_approx(sv - m_use);  // 0 for masked keys (their rows are finite)
 #pragma unroll
       for (int u = 0; u < STEPS; ++u) {
-        const float pw = ex2_approx(sc[u] - m_use);  // 0 for masked keys (their rows are finite)
+        const float pw = __shfl_sync(0xffffffffu, pv, g * LPR + 2 * u);  // key u * KPW + g
         float vx[4];
         quad_to_f<T>(reinterpret_cast<const T*>(st + HALF + u * STEP), vx);
         l += pw;
