@@ -64,6 +64,11 @@ CONFIGS = {
     "r2": dict(workload="fused_rope_attention bf16 BSHD causal (config-2 shape)", api="frope",
                dtype="bf16", layout="BSHD", B=4, H=32, S=4096, Skv=4096, D=128, causal=True,
                window=-1, std=1.0),
+    # backward pass (dQ, dK, dV) of config 2 through torch autograd's entry point
+    # (attention_backward); algorithmic FLOPs = 2.5 x the forward's (five matmuls per pair)
+    "b2": dict(workload="attention backward bf16 BHSD causal (config-2 shape)", api="bwd",
+               dtype="bf16", layout="BHSD", B=4, H=32, S=4096, Skv=4096, D=128, causal=True,
+               window=-1, std=1.0),
     # paged-KV decode (cache.paged_attention): the reference cache benchmark's largest shape
     # (benchmarks/suites/cache.py:64-80, 204-234: batch 8, 4096 cached tokens, 32 heads,
     # head_dim 128, block 16, sequential block tables); HBM-bound, not a BASELINE config
@@ -463,6 +468,77 @@ def bench_paged(args, c, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def bench_backward(args, c, world, rank, local):
+    """Backward of attention on config c: the forward's O and log-sum-exp are computed once,
+    each step runs attention_backward (the autograd backward of every attention entry point)
+    on a fresh dO.  value = algorithmic TFLOPS (2.5 x the forward's FLOPs)."""
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the reference's gradients "
+                              "come from MLX autodiff, which cannot run on this Linux/NVIDIA box"}),
+                  flush=True)
+        return
+    import torch
+    import torch.distributed as dist
+
+    from mlx_primitives.attention._core import _forward_impl, attention_backward
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    B, H, S, D = c["B"], c["H"], c["S"], c["D"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(42 + rank)
+    q, k, v, do = (torch.randn((B, H, S, D), generator=g, device=dev).bfloat16() for _ in range(4))
+    kw = dict(layout=c["layout"], scale=D ** -0.5, causal=c["causal"])
+    out, lse = _forward_impl(q, k, v, return_lse=True, **kw)
+
+    def step():
+        return attention_backward(q, k, v, out, lse, do, **kw)
+
+    for _ in range(args.warmup):
+        step()
+    stream = torch.cuda.current_stream(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clocks:
+        for a, b in ev:
+            a.record(stream)
+            step()
+            b.record(stream)
+        torch.cuda.synchronize(dev)
+    ms_local = sum(a.elapsed_time(b) for a, b in ev) / args.steps
+    ms = ms_local
+    if world > 1:
+        t = torch.tensor([ms_local], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    flops = 2.5 * config_flops(c)
+    peak, _, _, peak_src = load_peaks()
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC + " (backward)", "value": world * flops / (ms * 1e-3) / 1e12,
+            "unit": "TFLOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic: seeded N(0, 1) q, k, v, dO on device",
+            "config": config_json(c, world),
+            "roofline": {"bound": "tensor", "achieved": flops / (ms_local * 1e-3) / 1e12,
+                         "peak": peak, "unit": "TFLOP/s",
+                         "frac": flops / (ms_local * 1e-3) / 1e12 / peak, "traffic": None,
+                         "kernel": "bwd_delta + bwd_dkdv + bwd_dq (CUDA cores, fp32 math)",
+                         "peak_source": f"{peak_src}: bf16_tflops (the tensor-core target)",
+                         "algorithmic_flops_per_launch": flops},
+            "gpu_launches": 3 * args.steps, "clocks": clocks.summary()}), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def paged_config_json(c, n):
     return {"workload": c["workload"], "global_batch": c["B"] * n, "batch_per_gpu": c["B"],
             "heads": c["H"], "head_dim": c["D"], "context_len": c["Skv"],
@@ -492,6 +568,9 @@ def main():
 
     if c["api"] == "paged":
         bench_paged(args, c, world, rank, local)
+        return
+    if c["api"] == "bwd":
+        bench_backward(args, c, world, rank, local)
         return
     if args.impl == "reference":
         run_reference_arm(args, c, rank)
