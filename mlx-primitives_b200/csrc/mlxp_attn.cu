@@ -23,6 +23,7 @@
 #include "rope.cuh"
 #include "paged_attn.cuh"
 #include "attn_bwd.cuh"
+#include "attn_bwd_sm100.cuh"
 
 namespace mlxp {
 
@@ -52,6 +53,8 @@ int cuda_fail(cudaError_t e, const char* what) {
 }
 
 std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
+// Test hook (mlxp_set_backward_path): 1 = always the CUDA-core backward.
+std::atomic<int> g_bwd_force_cuda_cores{0};
 
 constexpr int kMaxDevices = 64;
 std::mutex g_dev_mu;
@@ -717,8 +720,114 @@ int paged_launch_t(const PagedParams& p, int LPR, unsigned grid, cudaStream_t s)
 
 // ---- backward (dQ, dK, dV) ----
 
+// The tensor-core backward serves bf16/fp16 with head_dim 128; it needs the padded L2 and
+// Delta rows and the fp32 dQ accumulator.  Everything else runs the CUDA-core backward (Delta).
+bool bwd_tc_shape(const Problem& pr) {
+  return (pr.dtype == MLXP_DTYPE_BF16 || pr.dtype == MLXP_DTYPE_FP16) && pr.D == 128 &&
+         pr.Sq > 0 && pr.Skv > 0;
+}
+size_t bwd_tc_rows_bytes(const Problem& pr) {
+  const size_t sq_pad = (size_t)(pr.Sq + 63) / 64 * 64;
+  return ((size_t)pr.B * pr.H * sq_pad * 4 + 255) / 256 * 256;
+}
 size_t bwd_workspace(const Problem& pr) {
-  return ((size_t)pr.B * pr.H * pr.Sq * 4 + 255) / 256 * 256;
+  const size_t base = ((size_t)pr.B * pr.H * pr.Sq * 4 + 255) / 256 * 256;
+  if (!bwd_tc_shape(pr)) return base;
+  const size_t acc = ((size_t)pr.B * pr.H * pr.Sq * pr.D * 4 + 255) / 256 * 256;
+  return std::max(base, 2 * bwd_tc_rows_bytes(pr) + acc);
+}
+
+// Tensor-core backward; returns MLXP_ERR_UNSUPPORTED (nothing launched) when an operand does
+// not suit TMA, so that the caller can take the CUDA-core path.
+int bwd_tc_launch(const BwdParams& bp, const Problem& pr, const int64_t* const st[8],
+                  void* workspace, cudaStream_t s) {
+  const int es = 2;
+  const CUtensorMapDataType dt = pr.dtype == MLXP_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  // dK / dV rows are written with 16-byte stores
+  for (const void* ptr : {bp.dk, bp.dv})
+    if (reinterpret_cast<uintptr_t>(ptr) % 16) return MLXP_ERR_UNSUPPORTED;
+  for (int t : {6, 7})
+    for (int d = 0; d < 3; ++d)
+      if (st[t][d] % 8) return MLXP_ERR_UNSUPPORTED;
+  const int64_t Hkv = pr.kv_heads();
+  CUtensorMap mq, mk, mv, mdo, mdq;
+  BwdTcParams tp{};
+  const std::string saved = t_last_error;
+  if (make_tmap(bp.q, dt, es, pr.B, pr.H, pr.Sq, 128, st[0], 64, 64, "q", &mq, &tp.cq) ||
+      make_tmap(bp.k, dt, es, pr.B, Hkv, pr.Skv, 128, st[1], 128, 64, "k", &mk, &tp.ck) ||
+      make_tmap(bp.v, dt, es, pr.B, Hkv, pr.Skv, 128, st[2], 128, 64, "v", &mv, &tp.cv) ||
+      make_tmap(bp.dout, dt, es, pr.B, pr.H, pr.Sq, 128, st[4], 64, 64, "dout", &mdo, &tp.cdo)) {
+    t_last_error = saved;
+    return MLXP_ERR_UNSUPPORTED;
+  }
+  char* w = static_cast<char*>(workspace);
+  const size_t rows = bwd_tc_rows_bytes(pr);
+  float* lse2 = reinterpret_cast<float*>(w);
+  float* delta = reinterpret_cast<float*>(w + rows);
+  float* acc = reinterpret_cast<float*>(w + 2 * rows);
+  const int64_t acc_st[4] = {pr.H * pr.Sq * 128, pr.Sq * 128, 128, 1};
+  if (int rc = make_tmap(acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, pr.B, pr.H, pr.Sq, 128, acc_st,
+                         64, 32, "dq accumulator", &mdq, &tp.cdq))
+    return rc;
+  int* status = nullptr;
+  int sms = 148;
+  if (int rc = device_info(&status, &sms)) return rc;
+  const int Sq_pad = (int)((pr.Sq + 63) / 64 * 64);
+  tp.B = (int)pr.B;
+  tp.H = (int)pr.H;
+  tp.Sq = (int)pr.Sq;
+  tp.Skv = (int)pr.Skv;
+  tp.kv_group = bp.kv_group;
+  tp.n_kt = (int)((pr.Skv + 127) / 128);
+  tp.Sq_pad = Sq_pad;
+  tp.lse2 = lse2;
+  tp.delta = delta;
+  tp.dk = bp.dk;
+  tp.dv = bp.dv;
+  tp.dk_sb = bp.dk_sb;
+  tp.dk_sh = bp.dk_sh;
+  tp.dk_ss = bp.dk_ss;
+  tp.dv_sb = bp.dv_sb;
+  tp.dv_sh = bp.dv_sh;
+  tp.dv_ss = bp.dv_ss;
+  tp.scale = bp.scale;
+  tp.scale_log2 = bp.scale_log2;
+  tp.mask = bp.mask;
+  tp.status = status;
+  tp.timeout_ns = g_timeout_ns.load();
+  cudaError_t e = cudaMemsetAsync(acc, 0, (size_t)pr.B * pr.H * pr.Sq * 128 * 4, s);
+  if (e != cudaSuccess) return cuda_fail(e, "dq accumulator reset");
+  const long long prow = pr.B * pr.H * Sq_pad;
+  const bool bf16 = pr.dtype == MLXP_DTYPE_BF16;
+  if (bf16)
+    bwd_tc_prep_kernel<__nv_bfloat16><<<(unsigned)((prow + 7) / 8), 256, 0, s>>>(bp, 128, Sq_pad, lse2, delta);
+  else
+    bwd_tc_prep_kernel<__half><<<(unsigned)((prow + 7) / 8), 256, 0, s>>>(bp, 128, Sq_pad, lse2, delta);
+  const unsigned grid = (unsigned)(tp.n_kt * pr.B * Hkv);
+  static std::atomic<unsigned long long> attr_done[2] = {{0}, {0}};
+  int dev;
+  if (int rc = current_device(dev)) return rc;
+  if (!(attr_done[bf16].load() >> dev & 1ull)) {
+    e = bf16 ? cudaFuncSetAttribute(attn_bwd_sm100_kernel<true>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, BwdTcCfg::SMEM_ALLOC)
+             : cudaFuncSetAttribute(attn_bwd_sm100_kernel<false>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, BwdTcCfg::SMEM_ALLOC);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(backward)");
+    attr_done[bf16].fetch_or(1ull << dev);
+  }
+  if (bf16)
+    attn_bwd_sm100_kernel<true><<<grid, BwdTcCfg::THREADS, BwdTcCfg::SMEM_ALLOC, s>>>(mq, mk, mv, mdo, mdq, tp);
+  else
+    attn_bwd_sm100_kernel<false><<<grid, BwdTcCfg::THREADS, BwdTcCfg::SMEM_ALLOC, s>>>(mq, mk, mv, mdo, mdq, tp);
+  const long long n = pr.B * pr.H * pr.Sq * 128;
+  const unsigned pg = (unsigned)std::min<long long>((n + 255) / 256, (long long)sms * 16);
+  if (bf16)
+    bwd_tc_post_kernel<__nv_bfloat16><<<pg, 256, 0, s>>>(bp, 128, acc);
+  else
+    bwd_tc_post_kernel<__half><<<pg, 256, 0, s>>>(bp, 128, acc);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? MLXP_OK : cuda_fail(e, "attention backward launch (tensor cores)");
 }
 
 template <typename T, int D>
@@ -1134,6 +1243,10 @@ int mlxp_attn_bwd(const void* q, const void* k, const void* v, const void* o, co
   bp.scale_log2 = scale * 1.4426950408889634f;
   bp.mask = mask_of(pr);
   cudaStream_t s = static_cast<cudaStream_t>(cuda_stream);
+  if (bwd_tc_shape(pr) && !g_bwd_force_cuda_cores.load()) {
+    const int rc = bwd_tc_launch(bp, pr, st, workspace, s);
+    if (rc != MLXP_ERR_UNSUPPORTED) return rc;
+  }
   if (dtype == MLXP_DTYPE_BF16) return bwd_dispatch_d<__nv_bfloat16>(bp, (int)D, s);
   if (dtype == MLXP_DTYPE_FP16) return bwd_dispatch_d<__half>(bp, (int)D, s);
   return bwd_dispatch_d<float>(bp, (int)D, s);
@@ -1153,6 +1266,11 @@ int mlxp_device_status(int* status_out, int reset) {
     e = cudaMemcpy(status, &zero, sizeof(int), cudaMemcpyHostToDevice);
     if (e != cudaSuccess) return cuda_fail(e, "reset device status");
   }
+  return MLXP_OK;
+}
+
+int mlxp_set_backward_path(int cuda_cores_only) {
+  g_bwd_force_cuda_cores.store(cuda_cores_only ? 1 : 0);
   return MLXP_OK;
 }
 

@@ -124,6 +124,25 @@ __device__ __forceinline__ void tma_store_4d(const void* map, uint32_t src, int 
       "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
 }
+// 4-D tiled reduce-add (f32) of one shared-memory box into global memory (bulk-group
+// completion).  Same coordinate rules as tma_store_4d.
+__device__ __forceinline__ void tma_reduce_add_4d(const void* map, uint32_t src, int c0, int c1,
+                                                  int c2, int c3) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.tile.bulk_group"
+      " [%0, {%2, %3, %4, %5}], [%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+// Contiguous global -> shared copy of `bytes` (multiple of 16, both addresses 16-byte
+// aligned), completing on mbarrier `bar`.  No multicast.
+__device__ __forceinline__ void bulk_copy_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                              uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
@@ -235,6 +254,11 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, bool is_bf16
   return (1u << 4) | ((is_bf16 ? 1u : 0u) << 7) | ((is_bf16 ? 1u : 0u) << 10) |
          ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) |
          ((uint32_t)(M >> 4) << 24);
+}
+// The same with the A operand's major-ness as well (bit 15: 1 = MN-major A in shared memory).
+__host__ __device__ constexpr uint32_t make_idesc_f16_ab(int M, int N, bool is_bf16,
+                                                         bool a_mn_major, bool b_mn_major) {
+  return make_idesc_f16(M, N, is_bf16, b_mn_major) | ((a_mn_major ? 1u : 0u) << 15);
 }
 
 // Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version field = 1.

@@ -128,15 +128,62 @@ def test_loss_through_sum_and_broadcast_kv():
     _check((q.grad, k.grad, v.grad), want, torch.float32)
 
 
-def test_backward_is_deterministic():
+def _cuda_core_backward(on: bool):
+    from mlx_primitives import _lib
+    assert _lib.lib().mlxp_set_backward_path(1 if on else 0) == 0
+
+
+def test_cuda_core_backward_is_deterministic():
+    """The CUDA-core backward has one writer per output element: bit-identical reruns.  (The
+    tensor-core path accumulates dQ by TMA reduce-add, whose order of additions varies.)"""
     import mlx_primitives as mp
-    grads = []
-    for _ in range(2):
-        (q, k, v, do), _ = _make((1, 300, 2, 128), (1, 300, 2, 128), torch.bfloat16, 13)
-        mp.flash_attention(q, k, v, causal=True).backward(do)
-        grads.append([t.grad.clone() for t in (q, k, v)])
-    for a, b in zip(*grads):
-        assert torch.equal(a, b)
+    _cuda_core_backward(True)
+    try:
+        grads = []
+        for _ in range(2):
+            (q, k, v, do), _ = _make((1, 300, 2, 128), (1, 300, 2, 128), torch.bfloat16, 13)
+            mp.flash_attention(q, k, v, causal=True).backward(do)
+            grads.append([t.grad.clone() for t in (q, k, v)])
+        for a, b in zip(*grads):
+            assert torch.equal(a, b)
+    finally:
+        _cuda_core_backward(False)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("case", ["causal", "noncausal", "gqa", "window", "cross", "ragged"])
+def test_tensor_core_backward_matches_oracle(dtype, case):
+    """head_dim 128 in bf16/fp16 takes the tensor-core kernel; every mask form, grouped heads,
+    lengths that are not multiples of the 64-query / 128-key tiles."""
+    from mlx_primitives.attention._core import _forward_impl, attention_backward
+    B, H, Hkv, Sq, Skv, kw = 2, 4, 4, 320, 320, dict(causal=True)
+    if case == "noncausal":
+        kw = dict(causal=False)
+    elif case == "gqa":
+        Hkv = 1
+    elif case == "window":
+        kw = dict(causal=True, window_left=70)
+    elif case == "cross":
+        Sq, Skv, kw = 100, 333, dict(causal=True, q_offset=233)
+    elif case == "ragged":
+        Sq, Skv = 77, 201
+    (q, k, v, do), (nq, nk, nv, ndo) = _make((B, H, Sq, 128), (B, Hkv, Skv, 128), dtype, 29)
+    args = dict(layout="BHSD", scale=128 ** -0.5, **kw)
+    with torch.no_grad():
+        out, lse = _forward_impl(q, k, v, return_lse=True, **args)
+        grads = attention_backward(q, k, v, out, lse, do, **args)
+    want = O.attention_bwd_bhsd(nq, nk, nv, ndo, 128 ** -0.5, causal=kw["causal"],
+                                window_left=kw.get("window_left", -1),
+                                q_offset=kw.get("q_offset", 0))
+    _check(grads, want, dtype, case)
+    # and the CUDA-core path on the same inputs agrees with it
+    _cuda_core_backward(True)
+    try:
+        with torch.no_grad():
+            ref = attention_backward(q, k, v, out, lse, do, **args)
+    finally:
+        _cuda_core_backward(False)
+    _check(grads, [r.float().cpu().numpy().astype(np.float64) for r in ref], dtype, case + " vs cuda cores")
 
 
 def test_no_grad_path_unchanged():
