@@ -12,15 +12,20 @@
 //   dK  += dS^T Q_i         (TS: dS^T from TMEM [160, 192), Q MN-major)         TMEM [320, 448)
 //   dQ_i^T = K^T dS_i^T     (SS: K as an MN-major A, dS^T from shared memory)   TMEM [448, 512)
 // and dQ_i^T leaves through a shared-memory box and TMA reduce-add (fp32) into a zeroed
-// accumulator that bwd_tc_post_kernel scales and converts.  The MMA order is
-//   S_0 dP_0 | P_0 ready | S_1 dP_1 dV_0 dK_0 dQ_0 | P_1 ready | S_2 dP_2 dV_1 dK_1 dQ_1 | ...
-// so the softmax warps compute step i+1 while the tensor core runs dV_i, dK_i and dQ_i; they
-// wait for dK_i (which reads the previous P^T / dS^T columns) only before storing.
+// accumulator that bwd_tc_post_kernel scales and converts.  The softmax warps signal twice per
+// step: once they have loaded S^T_i and dP^T_i into registers (the tensor core then computes
+// S^T_{i+1}, dP^T_{i+1} into the same columns while they work), and once P^T_i, dS^T_i are
+// stored (then dV_i, dK_i, dQ_i run while they start step i+1).  MMA order:
+//   S_0 dP_0 | consumed 0 | S_1 dP_1 | ready 0 | dV_0 dK_0 dQ_0 | consumed 1 | S_2 dP_2 | ...
+// Before storing P^T_{i+1} / dS^T_{i+1} the softmax warps wait for dK_i, the last reader of
+// those columns.  (Measured with one softmax warpgroup and S/dP not overlapped: 5500 cycles
+// per step, 3000 of them the softmax compute; see the history of this file.)
 //
-//   warps 0-3  softmax: thread = key row (TMEM lane), 64 queries per step
-//   warps 4-7  dQ writer (thread = head-dim row of dQ^T), then the dK / dV epilogue
-//   warp 8     TMA producer (K, V once; Q_i, dO_i, L2_i, Delta_i per step, two stages)
-//   warp 9     MMA issuer (one thread)
+//   warps 0-7  softmax: thread = key row (TMEM lane); warps w and w + 4 share the lanes and
+//              take queries 0-31 and 32-63 of the step
+//   warps 8-11 dQ writer (thread = head-dim row of dQ^T), then the dK / dV epilogue
+//   warp 12    TMA producer (K, V once; Q_i, dO_i, L2_i, Delta_i per step, two stages)
+//   warp 13    MMA issuer (one thread)
 // Every mbarrier wait is bounded; on a timeout the CTA stops, drains (bounded) and frees TMEM.
 #pragma once
 
@@ -50,22 +55,23 @@ struct BwdTcCfg {
   static constexpr int Q_TILE = BM * D * 2;   // 16 KB
   static constexpr int BOX_Q = BM * 128;      // one 64-column box of Q / dO
   static constexpr int DS_TILE = BN * 128;    // dS^T: 128 key rows x 64 queries (bf16)
-  static constexpr int DQ_BOX = BM * 128;     // dQ staging: 4 boxes of 64 rows x 32 fp32
+  static constexpr int NQS = 3;               // Q / dO stages
+  static constexpr int DQ_BOX = 32 * 128;     // dQ staging: 4 boxes of 32 rows x 32 fp32
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + K_TILE;
-  static constexpr int OFF_QS = OFF_V + K_TILE;             // 2 stages x (Q, dO)
-  static constexpr int OFF_LD = OFF_QS + 2 * 2 * Q_TILE;    // 2 stages x (L2, Delta) 512 B
-  static constexpr int OFF_DS = OFF_LD + 1024;              // 2 x dS^T
-  static constexpr int OFF_DQ = OFF_DS + 2 * DS_TILE;       // dQ staging (32 KB)
+  static constexpr int OFF_QS = OFF_V + K_TILE;             // NQS stages x (Q, dO)
+  static constexpr int OFF_LD = OFF_QS + NQS * 2 * Q_TILE;  // NQS stages x (L2, Delta) 512 B
+  static constexpr int OFF_DS = OFF_LD + 2048;              // 2 x dS^T
+  static constexpr int OFF_DQ = OFF_DS + 2 * DS_TILE;       // dQ staging (16 KB, half a step)
   static constexpr int OFF_BAR = OFF_DQ + 4 * DQ_BOX;
   enum {
-    B_KVF = 0, B_QF = 1, B_QE = 3, B_SF = 5, B_PF = 6, B_PDF = 7, B_DSF = 8, B_DQF = 10,
-    B_DQE = 11, B_ACC = 12, NBAR = 13
+    B_KVF = 0, B_QF = 1, B_QE = 4, B_SF = 7, B_PF = 8, B_PDF = 9, B_DSF = 10, B_DQF = 12,
+    B_DQE = 13, B_ACC = 14, B_SC = 15, NBAR = 16
   };
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16;
   static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;
-  static constexpr int THREADS = 320;
+  static constexpr int THREADS = 448;
   static constexpr uint32_t TM_S = 0, TM_DP = 64, TM_P = 128, TM_DS = 160, TM_DV = 192,
                             TM_DK = 320, TM_DQ = 448, TM_COLS = 512;
   static_assert(OFF_DS % 1024 == 0 && OFF_DQ % 1024 == 0 && OFF_QS % 1024 == 0, "atoms");
@@ -74,9 +80,10 @@ struct BwdTcCfg {
 
 enum : int { kSiteBwdProducer = 10, kSiteBwdMma = 11, kSiteBwdSoftmax = 12, kSiteBwdWriter = 13 };
 
-// L2 and Delta in the padded layout the TMA kernel copies from, one warp per padded row.
+// L2 and Delta in the padded layout the TMA kernel copies from, one warp per padded row
+// (head_dim 128: each lane reads 4 consecutive elements of O and dO).
 template <typename T>
-__global__ void __launch_bounds__(256) bwd_tc_prep_kernel(const BwdParams p, int D, int Sq_pad,
+__global__ void __launch_bounds__(256) bwd_tc_prep_kernel(const BwdParams p, int Sq_pad,
                                                           float* lse2, float* delta) {
   const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -90,10 +97,19 @@ __global__ void __launch_bounds__(256) bwd_tc_prep_kernel(const BwdParams p, int
     }
     return;
   }
-  const T* o = static_cast<const T*>(p.o) + b * p.o_sb + h * p.o_sh + i * p.o_ss;
-  const T* g = static_cast<const T*>(p.dout) + b * p.do_sb + h * p.do_sh + i * p.do_ss;
+  const T* o = static_cast<const T*>(p.o) + b * p.o_sb + h * p.o_sh + i * p.o_ss + 4 * lane;
+  const T* g = static_cast<const T*>(p.dout) + b * p.do_sb + h * p.do_sh + i * p.do_ss + 4 * lane;
   float a = 0.f;
-  for (int d = lane; d < D; d += 32) a = fmaf(bwd_ld(o + d), bwd_ld(g + d), a);
+  if (((reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(g)) & 7) == 0) {
+    const uint2 uo = *reinterpret_cast<const uint2*>(o), ug = *reinterpret_cast<const uint2*>(g);
+    const T* eo = reinterpret_cast<const T*>(&uo);
+    const T* eg = reinterpret_cast<const T*>(&ug);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) a = fmaf(bwd_ld(eo + e), bwd_ld(eg + e), a);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) a = fmaf(bwd_ld(o + e), bwd_ld(g + e), a);
+  }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
   if (lane == 0) {
@@ -103,23 +119,37 @@ __global__ void __launch_bounds__(256) bwd_tc_prep_kernel(const BwdParams p, int
   }
 }
 
-// dq = scale * accumulator (fp32 [B][H][Sq][D] contiguous), in the output type and strides.
-template <typename T>
-__global__ void __launch_bounds__(256) bwd_tc_post_kernel(const BwdParams p, int D,
-                                                          const float* acc) {
-  const long long n = (long long)p.B * p.H * p.Sq * D;
-  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < n;
-       e += (long long)gridDim.x * blockDim.x) {
-    const long long d = e % D, r = e / D;
+// dq = scale * accumulator (fp32 [B][H][Sq][128] contiguous), in the output type and strides;
+// 8 consecutive elements per thread (one 16-byte store when VEC: dq rows 16-byte aligned).
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(256) bwd_tc_post_kernel(const BwdParams p, const float* acc) {
+  const long long n8 = (long long)p.B * p.H * p.Sq * 16;
+  for (long long e8 = (long long)blockIdx.x * blockDim.x + threadIdx.x; e8 < n8;
+       e8 += (long long)gridDim.x * blockDim.x) {
+    const int d0 = (int)(e8 & 15) * 8;
+    const long long r = e8 >> 4;
     const long long i = r % p.Sq, bh = r / p.Sq;
     const long long h = bh % p.H, b = bh / p.H;
-    bwd_st<T>(static_cast<T*>(p.dq) + b * p.dq_sb + h * p.dq_sh + i * p.dq_ss + d,
-              acc[e] * p.scale);
+    const float4 x0 = *reinterpret_cast<const float4*>(acc + e8 * 8);
+    const float4 x1 = *reinterpret_cast<const float4*>(acc + e8 * 8 + 4);
+    const float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+    T* dst = static_cast<T*>(p.dq) + b * p.dq_sb + h * p.dq_sh + i * p.dq_ss + d0;
+    if constexpr (VEC) {
+      uint4 u;
+      u.x = pack2<std::is_same<T, __nv_bfloat16>::value>(v[0] * p.scale, v[1] * p.scale);
+      u.y = pack2<std::is_same<T, __nv_bfloat16>::value>(v[2] * p.scale, v[3] * p.scale);
+      u.z = pack2<std::is_same<T, __nv_bfloat16>::value>(v[4] * p.scale, v[5] * p.scale);
+      u.w = pack2<std::is_same<T, __nv_bfloat16>::value>(v[6] * p.scale, v[7] * p.scale);
+      *reinterpret_cast<uint4*>(dst) = u;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) bwd_st<T>(dst + e, v[e] * p.scale);
+    }
   }
 }
 
 template <bool kBF16>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(448, 1)
     attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                           const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v,
@@ -136,10 +166,13 @@ __global__ void __launch_bounds__(320, 1)
   auto BAR = [&](int i) -> uint32_t { return sbase + C::OFF_BAR + 8 * i; };
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  // work: key tile (heaviest first for causal masks: small j sees the most query tiles)
+  // work: (batch, K/V head) major, key tile minor — the CTAs running at the same time share
+  // the Q, dO and dQ-accumulator rows of a few heads in L2 (key-tile-major order re-read Q and
+  // dO from DRAM for every key tile: 7.8 GB of reads for config 2); within a head the small j
+  // (most query tiles under a causal mask) come first
   const int Hkv = p.H / p.kv_group;
-  const int j = blockIdx.x / (p.B * Hkv);
-  const int bhk = blockIdx.x - j * (p.B * Hkv);
+  const int bhk = blockIdx.x / p.n_kt;
+  const int j = blockIdx.x - bhk * p.n_kt;
   const int hk = bhk % Hkv, b = bhk / Hkv;
   const int c0 = j * C::BN;
   long long qlo, qhi;
@@ -150,13 +183,14 @@ __global__ void __launch_bounds__(320, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(BAR(C::B_KVF), 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < C::NQS; ++s) {
       mbar_init(BAR(C::B_QF + s), 1);
       mbar_init(BAR(C::B_QE + s), 1);
-      mbar_init(BAR(C::B_DSF + s), 1);
     }
+    for (int s = 0; s < 2; ++s) mbar_init(BAR(C::B_DSF + s), 1);
     mbar_init(BAR(C::B_SF), 1);
-    mbar_init(BAR(C::B_PF), 128);
+    mbar_init(BAR(C::B_PF), 256);
+    mbar_init(BAR(C::B_SC), 256);
     mbar_init(BAR(C::B_PDF), 1);
     mbar_init(BAR(C::B_DQF), 1);
     mbar_init(BAR(C::B_DQE), 128);
@@ -164,7 +198,7 @@ __global__ void __launch_bounds__(320, 1)
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 9) {
+  if (warp == 13) {
     tmem_alloc(smem_u32(tmem_slot), C::TM_COLS);
     tmem_relinquish();
   }
@@ -179,7 +213,7 @@ __global__ void __launch_bounds__(320, 1)
     q0 = (qt_lo + (i - g * per_head)) * C::BM;
   };
 
-  if (warp == 8) {
+  if (warp == 12) {
     // =================================== TMA producer ===================================
     if (lane == 0 && n_steps > 0) {
       tma_prefetch_desc(&tm_q);
@@ -199,9 +233,9 @@ __global__ void __launch_bounds__(320, 1)
       bool ok = true;
       int issued = 0;
       for (int i = 0; i < n_steps; ++i) {
-        const int s = i & 1;
-        if (i >= 2) {
-          ok = mbar_wait(BAR(C::B_QE + s), ((i >> 1) - 1) & 1, wctx, kSiteBwdProducer);
+        const int s = i % C::NQS;
+        if (i >= C::NQS) {
+          ok = mbar_wait(BAR(C::B_QE + s), ((i / C::NQS) - 1) & 1, wctx, kSiteBwdProducer);
           if (!ok) break;
         }
         int h, q0;
@@ -226,10 +260,10 @@ __global__ void __launch_bounds__(320, 1)
       // Let every load already issued land before the CTA releases its shared memory (a
       // normal run consumed all of them already: these waits then return at once).
       mbar_wait_drain(BAR(C::B_KVF), 0, p.status, p.timeout_ns);
-      for (int i = (issued > 2 ? issued - 2 : 0); i < issued; ++i)
-        mbar_wait_drain(BAR(C::B_QF + (i & 1)), (i >> 1) & 1, p.status, p.timeout_ns);
+      for (int i = (issued > C::NQS ? issued - C::NQS : 0); i < issued; ++i)
+        mbar_wait_drain(BAR(C::B_QF + i % C::NQS), (i / C::NQS) & 1, p.status, p.timeout_ns);
     }
-  } else if (warp == 9) {
+  } else if (warp == 13) {
     // ==================================== MMA issuer ====================================
     if (lane == 0) {
       constexpr uint32_t id_s = make_idesc_f16_ab(128, C::BM, kBF16, false, false);
@@ -240,7 +274,7 @@ __global__ void __launch_bounds__(320, 1)
       const uint32_t k_mn = ((sbase + C::OFF_K) >> 4) | ((uint32_t)(C::BOX_K >> 4) << 16);
       bool ok = n_steps > 0 ? mbar_wait(BAR(C::B_KVF), 0, wctx, kSiteBwdMma) : true;
       auto issue_sdp = [&](int i) {
-        const int s = i & 1;
+        const int s = i % C::NQS;
         const uint32_t q_lo = ((sbase + C::OFF_QS + s * 2 * C::Q_TILE) >> 4) | (1u << 16);
         const uint32_t o_lo = q_lo + (uint32_t)(C::Q_TILE >> 4);
 #pragma unroll
@@ -269,16 +303,18 @@ __global__ void __launch_bounds__(320, 1)
         }
       }
       for (int i = 0; i < n_steps && ok; ++i) {
-        const int s = i & 1;
-        ok = mbar_wait(BAR(C::B_PF), i & 1, wctx, kSiteBwdMma);
-        if (!ok) break;
-        tc_fence_after();
-        if (i + 1 < n_steps) {
-          ok = mbar_wait(BAR(C::B_QF + ((i + 1) & 1)), ((i + 1) >> 1) & 1, wctx, kSiteBwdMma);
+        const int s = i % C::NQS, sb = i & 1;  // Q / dO stage, dS buffer
+        if (i + 1 < n_steps) {  // S^T_{i+1}, dP^T_{i+1} once the softmax warps hold S^T_i, dP^T_i
+          ok = mbar_wait(BAR(C::B_SC), i & 1, wctx, kSiteBwdMma) &&
+               mbar_wait(BAR(C::B_QF + (i + 1) % C::NQS), ((i + 1) / C::NQS) & 1, wctx,
+                         kSiteBwdMma);
           if (!ok) break;
           tc_fence_after();
           issue_sdp(i + 1);
         }
+        ok = mbar_wait(BAR(C::B_PF), i & 1, wctx, kSiteBwdMma);
+        if (!ok) break;
+        tc_fence_after();
         // dV += P^T dO_i, dK += dS^T Q_i (MN-major B: 64-column chunks 8 KB apart)
         const uint32_t qm = ((sbase + C::OFF_QS + s * 2 * C::Q_TILE) >> 4) |
                             ((uint32_t)(C::BOX_Q >> 4) << 16);
@@ -299,67 +335,70 @@ __global__ void __launch_bounds__(320, 1)
           if (!ok) break;
           tc_fence_after();
         }
-        const uint32_t ds = ((sbase + C::OFF_DS + s * C::DS_TILE) >> 4) |
+        const uint32_t ds = ((sbase + C::OFF_DS + sb * C::DS_TILE) >> 4) |
                             ((uint32_t)(C::DS_TILE >> 4) << 16);
 #pragma unroll
         for (int kk = 0; kk < C::BN / 16; ++kk)
           mma_ss(tmem + C::TM_DQ, sdesc(k_mn + (uint32_t)(kk * 16 * 128 >> 4)),
                  sdesc(ds + (uint32_t)(kk * 16 * 128 >> 4)), id_dq, kk > 0 ? 1u : 0u);
         tc_commit(BAR(C::B_DQF));
-        tc_commit(BAR(C::B_DSF + s));
+        tc_commit(BAR(C::B_DSF + sb));
         tc_commit(BAR(C::B_QE + s));
       }
       tc_commit(BAR(C::B_ACC));  // every MMA issued above is complete when this arrives
       mbar_wait_drain(BAR(C::B_ACC), 0, p.status, p.timeout_ns);
     }
-  } else if (warp < 4) {
+  } else if (warp < 8) {
     // ===================================== softmax ======================================
-    const int k = warp * 32 + lane;  // key row of the tile = TMEM lane
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const int k = (warp & 3) * 32 + lane;  // key row of the tile = TMEM lane
+    const int hc = warp >> 2;              // query half: local queries 32 * hc .. 32 * hc + 31
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const long long kpos = (long long)c0 + k + p.mask.kv_off;
     const bool key_ok = c0 + k < p.Skv;
     bool ok = true;
     for (int i = 0; i < n_steps && ok; ++i) {
-      const int s = i & 1;
+      const int s = i % C::NQS, sb = i & 1;  // Q / dO stage, dS buffer
       int h, q0;
       step_qh(i, h, q0);
-      // admissible local queries [qa, qb) of this key
+      // admissible queries [qa, qb) of this key, local to this warp's 32 columns
       long long qa = 0, qb = C::BM;
       const long long base = q0 + p.mask.q_off;  // position of local query 0
       if (p.mask.causal && kpos - base > qa) qa = kpos - base;
       if (p.mask.wr >= 0 && kpos - p.mask.wr - base > qa) qa = kpos - p.mask.wr - base;
       if (p.mask.wl >= 0 && kpos + p.mask.wl - base + 1 < qb) qb = kpos + p.mask.wl - base + 1;
       if (!key_ok || qb < qa) qb = qa;
-      const uint32_t lo = (uint32_t)qa, width = (uint32_t)(qb - qa);
+      const uint32_t lo = (uint32_t)(qa - 32 * hc), width = (uint32_t)(qb - qa);
       ok = mbar_wait(BAR(C::B_SF), i & 1, wctx, kSiteBwdSoftmax) &&
-           mbar_wait(BAR(C::B_QF + s), (i >> 1) & 1, wctx, kSiteBwdSoftmax);
+           mbar_wait(BAR(C::B_QF + s), (i / C::NQS) & 1, wctx, kSiteBwdSoftmax);
       if (!ok) break;
       tc_fence_after();
-      const float* l2 = reinterpret_cast<const float*>(smem + C::OFF_LD + s * 512);
-      const float* dl = l2 + 64;
-      uint32_t pp[32], dd[32];
+      uint32_t sr[32], dr[32];
+      tmem_ld_x32(lane_base + C::TM_S + 32 * hc, sr);
+      tmem_ld_x32(lane_base + C::TM_DP + 32 * hc, dr);
+      tmem_wait_ld();
+      reg_fence(sr);
+      reg_fence(dr);
+      tc_fence_before();
+      mbar_arrive(BAR(C::B_SC));  // S^T_i, dP^T_i are in registers: their columns may be reused
+      const float4* l2 = reinterpret_cast<const float4*>(smem + C::OFF_LD + s * 512) + 8 * hc;
+      const float4* dl = l2 + 16;
+      uint32_t pp[16], dd[16];
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t sr[32], dr[32];
-        tmem_ld_x32(lane_base + C::TM_S + 32 * half, sr);
-        tmem_ld_x32(lane_base + C::TM_DP + 32 * half, dr);
-        tmem_wait_ld();
-        reg_fence(sr);
-        reg_fence(dr);
+      for (int c = 0; c < 32; c += 4) {
+        const float4 L4 = l2[c / 4], D4 = dl[c / 4];
+        const float Ls[4] = {L4.x, L4.y, L4.z, L4.w}, Ds[4] = {D4.x, D4.y, D4.z, D4.w};
+        float pv[4], dv[4];
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          float pv[2], dv[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int q = 32 * half + c + e;
-            const float x = fmaf(__uint_as_float(sr[c + e]), p.scale_log2, -l2[q]);
-            const float pr = ((uint32_t)q - lo < width) ? ex2_approx(x) : 0.f;
-            pv[e] = pr;
-            dv[e] = pr * (__uint_as_float(dr[c + e]) - dl[q]);
-          }
-          pp[16 * half + c / 2] = pack2<kBF16>(pv[0], pv[1]);
-          dd[16 * half + c / 2] = pack2<kBF16>(dv[0], dv[1]);
+        for (int e = 0; e < 4; ++e) {
+          const float x = fmaf(__uint_as_float(sr[c + e]), p.scale_log2, -Ls[e]);
+          const float pr = ((uint32_t)(c + e) - lo < width) ? ex2_approx(x) : 0.f;
+          pv[e] = pr;
+          dv[e] = pr * (__uint_as_float(dr[c + e]) - Ds[e]);
         }
+        pp[c / 2] = pack2<kBF16>(pv[0], pv[1]);
+        pp[c / 2 + 1] = pack2<kBF16>(pv[2], pv[3]);
+        dd[c / 2] = pack2<kBF16>(dv[0], dv[1]);
+        dd[c / 2 + 1] = pack2<kBF16>(dv[2], dv[3]);
       }
       // the previous step's P^T / dS^T columns are free once dK_{i-1} completed
       if (i >= 1) {
@@ -367,18 +406,19 @@ __global__ void __launch_bounds__(320, 1)
         if (!ok) break;
         tc_fence_after();
       }
-      tmem_st_x32(lane_base + C::TM_P, pp);
-      tmem_st_x32(lane_base + C::TM_DS, dd);
-      // dS^T row k into this step's shared-memory buffer (MN-major B, 128-byte swizzle)
+      tmem_st_x16(lane_base + C::TM_P + 16 * hc, pp);
+      tmem_st_x16(lane_base + C::TM_DS + 16 * hc, dd);
+      // dS^T row k, this half, into the step's shared-memory buffer (MN-major B, 128-byte
+      // swizzle: 16-byte chunk c of row k at chunk c ^ (k % 8))
       if (i >= 2) {
-        ok = mbar_wait(BAR(C::B_DSF + s), ((i >> 1) - 1) & 1, wctx, kSiteBwdSoftmax);
+        ok = mbar_wait(BAR(C::B_DSF + sb), ((i >> 1) - 1) & 1, wctx, kSiteBwdSoftmax);
         if (!ok) break;
       }
-      const uint32_t row = sbase + C::OFF_DS + s * C::DS_TILE + k * 128;
+      const uint32_t row = sbase + C::OFF_DS + sb * C::DS_TILE + k * 128;
 #pragma unroll
-      for (int c = 0; c < 8; ++c)
-        st_shared_v4(row + ((c ^ (k & 7)) << 4), dd[4 * c], dd[4 * c + 1], dd[4 * c + 2],
-                     dd[4 * c + 3]);
+      for (int c = 0; c < 4; ++c)
+        st_shared_v4(row + (((4 * hc + c) ^ (k & 7)) << 4), dd[4 * c], dd[4 * c + 1],
+                     dd[4 * c + 2], dd[4 * c + 3]);
       tmem_wait_st();
       fence_proxy_async_smem();
       tc_fence_before();
@@ -386,9 +426,9 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else {
     // ============================ dQ writer, then dK / dV ==============================
-    const int d = (warp - 4) * 32 + lane;  // dQ^T lane = head-dim row; dK/dV lane = key row
-    const uint32_t lane_base = tmem + ((uint32_t)((warp - 4) * 32) << 16);
-    const bool leader = warp == 4 && lane == 0;
+    const int d = (warp - 8) * 32 + lane;  // dQ^T lane = head-dim row; dK/dV lane = key row
+    const uint32_t lane_base = tmem + ((uint32_t)((warp - 8) * 32) << 16);
+    const bool leader = warp == 8 && lane == 0;
     bool ok = true;
     for (int i = 0; i < n_steps && ok; ++i) {
       int h, q0;
@@ -405,27 +445,28 @@ __global__ void __launch_bounds__(320, 1)
       reg_fence(v1);
       tc_fence_before();
       mbar_arrive(BAR(C::B_DQE));
-      // staging: box d/32 holds 64 query rows x 32 fp32 (128 B), 128-byte swizzle
-      if (leader) bulk_wait_group_read0();  // the previous reduce has read the staging
-      named_bar_sync(1, 128);
+      // staging: queries 0-31, then 32-63; box d/32 holds 32 query rows x 32 fp32 (128 B),
+      // 128-byte swizzle
       const uint32_t box = sbase + C::OFF_DQ + (d >> 5) * C::DQ_BOX;
       const int chunk = (d & 31) >> 2, within = (d & 3) * 4;
+      int c1, c2, c3;
 #pragma unroll
-      for (int q = 0; q < 32; ++q) {
-        asm volatile("st.shared.b32 [%0], %1;" ::"r"(box + q * 128 + ((chunk ^ (q & 7)) << 4) + within),
-                     "r"(v0[q]) : "memory");
-        asm volatile("st.shared.b32 [%0], %1;" ::"r"(box + (q + 32) * 128 + ((chunk ^ (q & 7)) << 4) + within),
-                     "r"(v1[q]) : "memory");
-      }
-      fence_proxy_async_smem();
-      named_bar_sync(1, 128);
-      if (leader) {
-        int c1, c2, c3;
-        tma_coords(p.cdq, q0, h, b, c1, c2, c3);
+      for (int half = 0; half < 2; ++half) {
+        if (leader) bulk_wait_group_read0();  // the previous reduce has read the staging
+        named_bar_sync(1, 128);
 #pragma unroll
-        for (int bx = 0; bx < 4; ++bx)
-          tma_reduce_add_4d(&tm_dq, sbase + C::OFF_DQ + bx * C::DQ_BOX, bx * 32, c1, c2, c3);
-        bulk_commit_group();
+        for (int q = 0; q < 32; ++q)
+          asm volatile("st.shared.b32 [%0], %1;" ::"r"(box + q * 128 + ((chunk ^ (q & 7)) << 4) + within),
+                       "r"(half ? v1[q] : v0[q]) : "memory");
+        fence_proxy_async_smem();
+        named_bar_sync(1, 128);
+        if (leader) {
+          tma_coords(p.cdq, q0 + 32 * half, h, b, c1, c2, c3);
+#pragma unroll
+          for (int bx = 0; bx < 4; ++bx)
+            tma_reduce_add_4d(&tm_dq, sbase + C::OFF_DQ + bx * C::DQ_BOX, bx * 32, c1, c2, c3);
+          bulk_commit_group();
+        }
       }
     }
     if (leader) bulk_wait_group0();
@@ -468,7 +509,7 @@ __global__ void __launch_bounds__(320, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == 13) {
     tc_fence_after();
     tmem_dealloc(tmem, C::TM_COLS);
   }

@@ -768,7 +768,7 @@ int bwd_tc_launch(const BwdParams& bp, const Problem& pr, const int64_t* const s
   float* acc = reinterpret_cast<float*>(w + 2 * rows);
   const int64_t acc_st[4] = {pr.H * pr.Sq * 128, pr.Sq * 128, 128, 1};
   if (int rc = make_tmap(acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, pr.B, pr.H, pr.Sq, 128, acc_st,
-                         64, 32, "dq accumulator", &mdq, &tp.cdq))
+                         32, 32, "dq accumulator", &mdq, &tp.cdq))
     return rc;
   int* status = nullptr;
   int sms = 148;
@@ -801,9 +801,9 @@ int bwd_tc_launch(const BwdParams& bp, const Problem& pr, const int64_t* const s
   const long long prow = pr.B * pr.H * Sq_pad;
   const bool bf16 = pr.dtype == MLXP_DTYPE_BF16;
   if (bf16)
-    bwd_tc_prep_kernel<__nv_bfloat16><<<(unsigned)((prow + 7) / 8), 256, 0, s>>>(bp, 128, Sq_pad, lse2, delta);
+    bwd_tc_prep_kernel<__nv_bfloat16><<<(unsigned)((prow + 7) / 8), 256, 0, s>>>(bp, Sq_pad, lse2, delta);
   else
-    bwd_tc_prep_kernel<__half><<<(unsigned)((prow + 7) / 8), 256, 0, s>>>(bp, 128, Sq_pad, lse2, delta);
+    bwd_tc_prep_kernel<__half><<<(unsigned)((prow + 7) / 8), 256, 0, s>>>(bp, Sq_pad, lse2, delta);
   const unsigned grid = (unsigned)(tp.n_kt * pr.B * Hkv);
   static std::atomic<unsigned long long> attr_done[2] = {{0}, {0}};
   int dev;
@@ -820,12 +820,17 @@ int bwd_tc_launch(const BwdParams& bp, const Problem& pr, const int64_t* const s
     attn_bwd_sm100_kernel<true><<<grid, BwdTcCfg::THREADS, BwdTcCfg::SMEM_ALLOC, s>>>(mq, mk, mv, mdo, mdq, tp);
   else
     attn_bwd_sm100_kernel<false><<<grid, BwdTcCfg::THREADS, BwdTcCfg::SMEM_ALLOC, s>>>(mq, mk, mv, mdo, mdq, tp);
-  const long long n = pr.B * pr.H * pr.Sq * 128;
-  const unsigned pg = (unsigned)std::min<long long>((n + 255) / 256, (long long)sms * 16);
-  if (bf16)
-    bwd_tc_post_kernel<__nv_bfloat16><<<pg, 256, 0, s>>>(bp, 128, acc);
-  else
-    bwd_tc_post_kernel<__half><<<pg, 256, 0, s>>>(bp, 128, acc);
+  const long long n8 = pr.B * pr.H * pr.Sq * 16;
+  const unsigned pg = (unsigned)std::min<long long>((n8 + 255) / 256, (long long)sms * 32);
+  const bool vec = reinterpret_cast<uintptr_t>(bp.dq) % 16 == 0 && bp.dq_sb % 8 == 0 &&
+                   bp.dq_sh % 8 == 0 && bp.dq_ss % 8 == 0;
+  if (bf16) {
+    if (vec) bwd_tc_post_kernel<__nv_bfloat16, true><<<pg, 256, 0, s>>>(bp, acc);
+    else bwd_tc_post_kernel<__nv_bfloat16, false><<<pg, 256, 0, s>>>(bp, acc);
+  } else {
+    if (vec) bwd_tc_post_kernel<__half, true><<<pg, 256, 0, s>>>(bp, acc);
+    else bwd_tc_post_kernel<__half, false><<<pg, 256, 0, s>>>(bp, acc);
+  }
   e = cudaGetLastError();
   return e == cudaSuccess ? MLXP_OK : cuda_fail(e, "attention backward launch (tensor cores)");
 }
