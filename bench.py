@@ -69,6 +69,10 @@ CONFIGS = {
     "b2": dict(workload="attention backward bf16 BHSD causal (config-2 shape)", api="bwd",
                dtype="bf16", layout="BHSD", B=4, H=32, S=4096, Skv=4096, D=128, causal=True,
                window=-1, std=1.0),
+    # backward of the config-4 shape's head_dim (64), causal self-attention, BSHD
+    "b4": dict(workload="attention backward bf16 BHSD causal, head_dim 64", api="bwd",
+               dtype="bf16", layout="BHSD", B=8, H=16, S=4096, Skv=4096, D=64, causal=True,
+               window=-1, std=1.0),
     # paged-KV decode (cache.paged_attention): the reference cache benchmark's largest shape
     # (benchmarks/suites/cache.py:64-80, 204-234: batch 8, 4096 cached tokens, 32 heads,
     # head_dim 128, block 16, sequential block tables); HBM-bound, not a BASELINE config
@@ -530,7 +534,7 @@ def bench_backward(args, c, world, rank, local):
             "roofline": {"bound": "tensor", "achieved": flops / (ms_local * 1e-3) / 1e12,
                          "peak": peak, "unit": "TFLOP/s",
                          "frac": flops / (ms_local * 1e-3) / 1e12 / peak, "traffic": None,
-                         "kernel": "bwd_delta + bwd_dkdv + bwd_dq (CUDA cores, fp32 math)",
+                         "kernel": "attn_bwd_sm100_kernel (+ prep, dQ convert)",
                          "peak_source": f"{peak_src}: bf16_tflops (the tensor-core target)",
                          "algorithmic_flops_per_launch": flops},
             "gpu_launches": 3 * args.steps, "clocks": clocks.summary()}), flush=True)

@@ -213,7 +213,7 @@ int mlxp_rope_qk(const void* q, const void* k, void* q_out, void* k_out, int dty
  * head: grouped heads sum their query heads' contributions).  Every tensor through its own
  * strides ((batch, head, seq, dim) order, dim stride 1); masks and offsets as mlxp_attn_fwd.
  * head_dim 32, 64 or 128; computed in fp32.  workspace: >= mlxp_attn_bwd_workspace_size bytes,
- * 256-byte aligned.  bf16/fp16 with head_dim 128 run on the tensor cores (P and dS rounded to
+ * 256-byte aligned.  bf16/fp16 with head_dim 64 or 128 run on the tensor cores (P and dS rounded to
  * the input type for the matmuls, as flash-attention backward passes do; dQ accumulated in
  * fp32 by TMA reduce-add, so its last bits depend on the order of the additions); the rest on
  * CUDA cores in fp32, deterministic.
@@ -230,7 +230,7 @@ int mlxp_attn_bwd(const void* q, const void* k, const void* v, const void* o, co
 
 /*
  * Which backward runs: 0 (default) = the tensor-core kernel where it applies (bf16/fp16,
- * head_dim 128, TMA-compatible operands), the CUDA-core kernels otherwise; 1 = always the
+ * head_dim 64 or 128, TMA-compatible operands), the CUDA-core kernels otherwise; 1 = always the
  * CUDA-core kernels (for cross-checking the two).  Process-wide.
  */
 int mlxp_set_backward_path(int cuda_cores_only);

@@ -1,5 +1,5 @@
 // attn_bwd_sm100.cuh — attention backward (dQ, dK, dV) on the 5th-generation tensor cores,
-// head_dim 128, bf16/fp16 inputs, fp32 accumulation in TMEM.
+// head_dim 64 or 128, bf16/fp16 inputs, fp32 accumulation in TMEM.
 //
 // One CTA per (key tile of 128 keys, batch, K/V head); it keeps K_j and V_j in shared memory
 // and dK_j, dV_j in TMEM while it walks the 64-row query tiles (of every query head of a
@@ -48,22 +48,27 @@ struct BwdTcParams {
   unsigned long long timeout_ns;
 };
 
+// head_dim 64: dQ^T = K^T dS^T keeps M = 128 (the tensor core's row count for one CTA) with an
+// A operand whose second 64-row chunk (head-dim rows 64-127) is a zero tile in shared memory;
+// those accumulator lanes hold zeros and are never read.
+template <int D_>
 struct BwdTcCfg {
-  static constexpr int D = 128, BN = 128, BM = 64, KB = 2;
-  static constexpr int K_TILE = BN * D * 2;   // 32 KB
+  static constexpr int D = D_, BN = 128, BM = 64, KB = D / 64;
+  static constexpr int K_TILE = BN * D * 2;   // K or V tile
   static constexpr int BOX_K = BN * 128;      // one 64-column box of K / V
-  static constexpr int Q_TILE = BM * D * 2;   // 16 KB
+  static constexpr int Q_TILE = BM * D * 2;   // Q or dO tile
   static constexpr int BOX_Q = BM * 128;      // one 64-column box of Q / dO
   static constexpr int DS_TILE = BN * 128;    // dS^T: 128 key rows x 64 queries (bf16)
   static constexpr int NQS = 3;               // Q / dO stages
-  static constexpr int DQ_BOX = 32 * 128;     // dQ staging: 4 boxes of 32 rows x 32 fp32
+  static constexpr int DQ_BOX = 32 * 128;     // dQ staging: D/32 boxes of 32 rows x 32 fp32
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + K_TILE;
-  static constexpr int OFF_QS = OFF_V + K_TILE;             // NQS stages x (Q, dO)
+  static constexpr int OFF_ZERO = OFF_V + K_TILE;           // head_dim 64: 16 KB of zeros
+  static constexpr int OFF_QS = OFF_ZERO + (D == 64 ? BOX_K : 0);  // NQS stages x (Q, dO)
   static constexpr int OFF_LD = OFF_QS + NQS * 2 * Q_TILE;  // NQS stages x (L2, Delta) 512 B
   static constexpr int OFF_DS = OFF_LD + 2048;              // 2 x dS^T
   static constexpr int OFF_DQ = OFF_DS + 2 * DS_TILE;       // dQ staging (16 KB, half a step)
-  static constexpr int OFF_BAR = OFF_DQ + 4 * DQ_BOX;
+  static constexpr int OFF_BAR = OFF_DQ + (D / 32) * DQ_BOX;
   enum {
     B_KVF = 0, B_QF = 1, B_QE = 4, B_SF = 7, B_PF = 8, B_PDF = 9, B_DSF = 10, B_DQF = 12,
     B_DQE = 13, B_ACC = 14, B_SC = 15, NBAR = 16
@@ -73,7 +78,8 @@ struct BwdTcCfg {
   static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;
   static constexpr int THREADS = 448;
   static constexpr uint32_t TM_S = 0, TM_DP = 64, TM_P = 128, TM_DS = 160, TM_DV = 192,
-                            TM_DK = 320, TM_DQ = 448, TM_COLS = 512;
+                            TM_DK = 192 + D, TM_DQ = 192 + 2 * D, TM_COLS = 512;
+  static_assert(D == 64 || D == 128, "head_dim 64 or 128");
   static_assert(OFF_DS % 1024 == 0 && OFF_DQ % 1024 == 0 && OFF_QS % 1024 == 0, "atoms");
   static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
 };
@@ -81,10 +87,11 @@ struct BwdTcCfg {
 enum : int { kSiteBwdProducer = 10, kSiteBwdMma = 11, kSiteBwdSoftmax = 12, kSiteBwdWriter = 13 };
 
 // L2 and Delta in the padded layout the TMA kernel copies from, one warp per padded row
-// (head_dim 128: each lane reads 4 consecutive elements of O and dO).
-template <typename T>
+// (each lane reads D/32 consecutive elements of O and dO).
+template <typename T, int D>
 __global__ void __launch_bounds__(256) bwd_tc_prep_kernel(const BwdParams p, int Sq_pad,
                                                           float* lse2, float* delta) {
+  constexpr int E = D / 32;
   const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= (long long)p.B * p.H * Sq_pad) return;
@@ -97,18 +104,19 @@ __global__ void __launch_bounds__(256) bwd_tc_prep_kernel(const BwdParams p, int
     }
     return;
   }
-  const T* o = static_cast<const T*>(p.o) + b * p.o_sb + h * p.o_sh + i * p.o_ss + 4 * lane;
-  const T* g = static_cast<const T*>(p.dout) + b * p.do_sb + h * p.do_sh + i * p.do_ss + 4 * lane;
+  const T* o = static_cast<const T*>(p.o) + b * p.o_sb + h * p.o_sh + i * p.o_ss + E * lane;
+  const T* g = static_cast<const T*>(p.dout) + b * p.do_sb + h * p.do_sh + i * p.do_ss + E * lane;
+  using V = typename std::conditional<E == 4, uint2, uint32_t>::type;
   float a = 0.f;
-  if (((reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(g)) & 7) == 0) {
-    const uint2 uo = *reinterpret_cast<const uint2*>(o), ug = *reinterpret_cast<const uint2*>(g);
+  if (((reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(g)) & (2 * E - 1)) == 0) {
+    const V uo = *reinterpret_cast<const V*>(o), ug = *reinterpret_cast<const V*>(g);
     const T* eo = reinterpret_cast<const T*>(&uo);
     const T* eg = reinterpret_cast<const T*>(&ug);
 #pragma unroll
-    for (int e = 0; e < 4; ++e) a = fmaf(bwd_ld(eo + e), bwd_ld(eg + e), a);
+    for (int e = 0; e < E; ++e) a = fmaf(bwd_ld(eo + e), bwd_ld(eg + e), a);
   } else {
 #pragma unroll
-    for (int e = 0; e < 4; ++e) a = fmaf(bwd_ld(o + e), bwd_ld(g + e), a);
+    for (int e = 0; e < E; ++e) a = fmaf(bwd_ld(o + e), bwd_ld(g + e), a);
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
@@ -119,15 +127,15 @@ __global__ void __launch_bounds__(256) bwd_tc_prep_kernel(const BwdParams p, int
   }
 }
 
-// dq = scale * accumulator (fp32 [B][H][Sq][128] contiguous), in the output type and strides;
+// dq = scale * accumulator (fp32 [B][H][Sq][D] contiguous), in the output type and strides;
 // 8 consecutive elements per thread (one 16-byte store when VEC: dq rows 16-byte aligned).
-template <typename T, bool VEC>
+template <typename T, int D, bool VEC>
 __global__ void __launch_bounds__(256) bwd_tc_post_kernel(const BwdParams p, const float* acc) {
-  const long long n8 = (long long)p.B * p.H * p.Sq * 16;
+  const long long n8 = (long long)p.B * p.H * p.Sq * (D / 8);
   for (long long e8 = (long long)blockIdx.x * blockDim.x + threadIdx.x; e8 < n8;
        e8 += (long long)gridDim.x * blockDim.x) {
-    const int d0 = (int)(e8 & 15) * 8;
-    const long long r = e8 >> 4;
+    const int d0 = (int)(e8 % (D / 8)) * 8;
+    const long long r = e8 / (D / 8);
     const long long i = r % p.Sq, bh = r / p.Sq;
     const long long h = bh % p.H, b = bh / p.H;
     const float4 x0 = *reinterpret_cast<const float4*>(acc + e8 * 8);
@@ -148,14 +156,14 @@ __global__ void __launch_bounds__(256) bwd_tc_post_kernel(const BwdParams p, con
   }
 }
 
-template <bool kBF16>
+template <bool kBF16, int D>
 __global__ void __launch_bounds__(448, 1)
     attn_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                           const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v,
                           const __grid_constant__ CUtensorMap tm_do,
                           const __grid_constant__ CUtensorMap tm_dq, const BwdTcParams p) {
-  using C = BwdTcCfg;
+  using C = BwdTcCfg<D>;
   using T = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -271,7 +279,10 @@ __global__ void __launch_bounds__(448, 1)
       constexpr uint32_t id_dq = make_idesc_f16_ab(128, C::BM, kBF16, true, true);
       const uint32_t k_lo = ((sbase + C::OFF_K) >> 4) | (1u << 16);
       const uint32_t v_lo = ((sbase + C::OFF_V) >> 4) | (1u << 16);
-      const uint32_t k_mn = ((sbase + C::OFF_K) >> 4) | ((uint32_t)(C::BOX_K >> 4) << 16);
+      // dQ^T's A = K^T (MN-major, two 64-row chunks of head dim: K's second box, or the zero
+      // tile for head_dim 64)
+      constexpr uint32_t a_lbo = (D == 128 ? C::BOX_K : C::OFF_ZERO - C::OFF_K);
+      const uint32_t k_mn = ((sbase + C::OFF_K) >> 4) | ((a_lbo >> 4) << 16);
       bool ok = n_steps > 0 ? mbar_wait(BAR(C::B_KVF), 0, wctx, kSiteBwdMma) : true;
       auto issue_sdp = [&](int i) {
         const int s = i % C::NQS;
@@ -350,6 +361,10 @@ __global__ void __launch_bounds__(448, 1)
     }
   } else if (warp < 8) {
     // ===================================== softmax ======================================
+    if constexpr (D == 64) {  // the zero half of dQ^T's A operand (fenced before the first PF)
+      for (int e = threadIdx.x; e < C::BOX_K / 16; e += 256)
+        st_shared_v4(sbase + C::OFF_ZERO + 16 * e, 0u, 0u, 0u, 0u);
+    }
     const int k = (warp & 3) * 32 + lane;  // key row of the tile = TMEM lane
     const int hc = warp >> 2;              // query half: local queries 32 * hc .. 32 * hc + 31
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
@@ -437,12 +452,15 @@ __global__ void __launch_bounds__(448, 1)
       ok = named_bar_and(1, 128, ok);  // the 128 writers agree before their named barriers
       if (!ok) break;
       tc_fence_after();
+      const bool rows = warp - 8 < D / 32;  // warp-uniform: this warp's head-dim rows exist
       uint32_t v0[32], v1[32];
-      tmem_ld_x32(lane_base + C::TM_DQ, v0);
-      tmem_ld_x32(lane_base + C::TM_DQ + 32, v1);
-      tmem_wait_ld();
-      reg_fence(v0);
-      reg_fence(v1);
+      if (rows) {
+        tmem_ld_x32(lane_base + C::TM_DQ, v0);
+        tmem_ld_x32(lane_base + C::TM_DQ + 32, v1);
+        tmem_wait_ld();
+        reg_fence(v0);
+        reg_fence(v1);
+      }
       tc_fence_before();
       mbar_arrive(BAR(C::B_DQE));
       // staging: queries 0-31, then 32-63; box d/32 holds 32 query rows x 32 fp32 (128 B),
@@ -454,16 +472,18 @@ __global__ void __launch_bounds__(448, 1)
       for (int half = 0; half < 2; ++half) {
         if (leader) bulk_wait_group_read0();  // the previous reduce has read the staging
         named_bar_sync(1, 128);
+        if (rows) {
 #pragma unroll
-        for (int q = 0; q < 32; ++q)
-          asm volatile("st.shared.b32 [%0], %1;" ::"r"(box + q * 128 + ((chunk ^ (q & 7)) << 4) + within),
-                       "r"(half ? v1[q] : v0[q]) : "memory");
+          for (int q = 0; q < 32; ++q)
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(box + q * 128 + ((chunk ^ (q & 7)) << 4) + within),
+                         "r"(half ? v1[q] : v0[q]) : "memory");
+        }
         fence_proxy_async_smem();
         named_bar_sync(1, 128);
         if (leader) {
           tma_coords(p.cdq, q0 + 32 * half, h, b, c1, c2, c3);
 #pragma unroll
-          for (int bx = 0; bx < 4; ++bx)
+          for (int bx = 0; bx < D / 32; ++bx)
             tma_reduce_add_4d(&tm_dq, sbase + C::OFF_DQ + bx * C::DQ_BOX, bx * 32, c1, c2, c3);
           bulk_commit_group();
         }
@@ -482,7 +502,7 @@ __global__ void __launch_bounds__(448, 1)
         T* dst = which ? dkr : dvr;
         const float mul = which ? p.scale : 1.f;
 #pragma unroll 1
-        for (int cb = 0; cb < 4; ++cb) {
+        for (int cb = 0; cb < D / 32; ++cb) {
           uint32_t r[32];
           if (n_steps > 0) {
             tmem_ld_x32(lane_base + (which ? C::TM_DK : C::TM_DV) + 32 * cb, r);

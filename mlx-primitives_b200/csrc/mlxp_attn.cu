@@ -720,11 +720,11 @@ int paged_launch_t(const PagedParams& p, int LPR, unsigned grid, cudaStream_t s)
 
 // ---- backward (dQ, dK, dV) ----
 
-// The tensor-core backward serves bf16/fp16 with head_dim 128; it needs the padded L2 and
+// The tensor-core backward serves bf16/fp16 with head_dim 64 or 128; it needs the padded L2 and
 // Delta rows and the fp32 dQ accumulator.  Everything else runs the CUDA-core backward (Delta).
 bool bwd_tc_shape(const Problem& pr) {
-  return (pr.dtype == MLXP_DTYPE_BF16 || pr.dtype == MLXP_DTYPE_FP16) && pr.D == 128 &&
-         pr.Sq > 0 && pr.Skv > 0;
+  return (pr.dtype == MLXP_DTYPE_BF16 || pr.dtype == MLXP_DTYPE_FP16) &&
+         (pr.D == 64 || pr.D == 128) && pr.Sq > 0 && pr.Skv > 0;
 }
 size_t bwd_tc_rows_bytes(const Problem& pr) {
   const size_t sq_pad = (size_t)(pr.Sq + 63) / 64 * 64;
@@ -737,11 +737,46 @@ size_t bwd_workspace(const Problem& pr) {
   return std::max(base, 2 * bwd_tc_rows_bytes(pr) + acc);
 }
 
+template <bool kBF16, int D>
+int bwd_tc_kernel_launch(const CUtensorMap* m, const BwdTcParams& tp, unsigned grid,
+                         cudaStream_t s) {
+  using C = BwdTcCfg<D>;
+  static std::atomic<unsigned long long> attr_done{0};  // one bit per device
+  int dev;
+  if (int rc = current_device(dev)) return rc;
+  if (!(attr_done.load() >> dev & 1ull)) {
+    cudaError_t e = cudaFuncSetAttribute(attn_bwd_sm100_kernel<kBF16, D>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_ALLOC);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(backward)");
+    attr_done.fetch_or(1ull << dev);
+  }
+  attn_bwd_sm100_kernel<kBF16, D><<<grid, C::THREADS, C::SMEM_ALLOC, s>>>(m[0], m[1], m[2], m[3],
+                                                                         m[4], tp);
+  return MLXP_OK;
+}
+
+template <typename T, int D>
+void bwd_tc_aux_launch(const BwdParams& bp, int Sq_pad, float* lse2, float* delta,
+                       const float* acc, bool post, int sms, cudaStream_t s) {
+  if (!post) {
+    const long long prow = (long long)bp.B * bp.H * Sq_pad;
+    bwd_tc_prep_kernel<T, D><<<(unsigned)((prow + 7) / 8), 256, 0, s>>>(bp, Sq_pad, lse2, delta);
+    return;
+  }
+  const long long n8 = (long long)bp.B * bp.H * bp.Sq * (D / 8);
+  const unsigned pg = (unsigned)std::min<long long>((n8 + 255) / 256, (long long)sms * 32);
+  const bool vec = reinterpret_cast<uintptr_t>(bp.dq) % 16 == 0 && bp.dq_sb % 8 == 0 &&
+                   bp.dq_sh % 8 == 0 && bp.dq_ss % 8 == 0;
+  if (vec) bwd_tc_post_kernel<T, D, true><<<pg, 256, 0, s>>>(bp, acc);
+  else bwd_tc_post_kernel<T, D, false><<<pg, 256, 0, s>>>(bp, acc);
+}
+
 // Tensor-core backward; returns MLXP_ERR_UNSUPPORTED (nothing launched) when an operand does
 // not suit TMA, so that the caller can take the CUDA-core path.
 int bwd_tc_launch(const BwdParams& bp, const Problem& pr, const int64_t* const st[8],
                   void* workspace, cudaStream_t s) {
   const int es = 2;
+  const int64_t D = pr.D;
   const CUtensorMapDataType dt = pr.dtype == MLXP_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                             : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   // dK / dV rows are written with 16-byte stores
@@ -751,13 +786,13 @@ int bwd_tc_launch(const BwdParams& bp, const Problem& pr, const int64_t* const s
     for (int d = 0; d < 3; ++d)
       if (st[t][d] % 8) return MLXP_ERR_UNSUPPORTED;
   const int64_t Hkv = pr.kv_heads();
-  CUtensorMap mq, mk, mv, mdo, mdq;
+  CUtensorMap maps[5];  // q, k, v, dout, dq accumulator
   BwdTcParams tp{};
   const std::string saved = t_last_error;
-  if (make_tmap(bp.q, dt, es, pr.B, pr.H, pr.Sq, 128, st[0], 64, 64, "q", &mq, &tp.cq) ||
-      make_tmap(bp.k, dt, es, pr.B, Hkv, pr.Skv, 128, st[1], 128, 64, "k", &mk, &tp.ck) ||
-      make_tmap(bp.v, dt, es, pr.B, Hkv, pr.Skv, 128, st[2], 128, 64, "v", &mv, &tp.cv) ||
-      make_tmap(bp.dout, dt, es, pr.B, pr.H, pr.Sq, 128, st[4], 64, 64, "dout", &mdo, &tp.cdo)) {
+  if (make_tmap(bp.q, dt, es, pr.B, pr.H, pr.Sq, D, st[0], 64, 64, "q", &maps[0], &tp.cq) ||
+      make_tmap(bp.k, dt, es, pr.B, Hkv, pr.Skv, D, st[1], 128, 64, "k", &maps[1], &tp.ck) ||
+      make_tmap(bp.v, dt, es, pr.B, Hkv, pr.Skv, D, st[2], 128, 64, "v", &maps[2], &tp.cv) ||
+      make_tmap(bp.dout, dt, es, pr.B, pr.H, pr.Sq, D, st[4], 64, 64, "dout", &maps[3], &tp.cdo)) {
     t_last_error = saved;
     return MLXP_ERR_UNSUPPORTED;
   }
@@ -766,9 +801,9 @@ int bwd_tc_launch(const BwdParams& bp, const Problem& pr, const int64_t* const s
   float* lse2 = reinterpret_cast<float*>(w);
   float* delta = reinterpret_cast<float*>(w + rows);
   float* acc = reinterpret_cast<float*>(w + 2 * rows);
-  const int64_t acc_st[4] = {pr.H * pr.Sq * 128, pr.Sq * 128, 128, 1};
-  if (int rc = make_tmap(acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, pr.B, pr.H, pr.Sq, 128, acc_st,
-                         32, 32, "dq accumulator", &mdq, &tp.cdq))
+  const int64_t acc_st[4] = {pr.H * pr.Sq * D, pr.Sq * D, D, 1};
+  if (int rc = make_tmap(acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, pr.B, pr.H, pr.Sq, D, acc_st,
+                         32, 32, "dq accumulator", &maps[4], &tp.cdq))
     return rc;
   int* status = nullptr;
   int sms = 148;
@@ -796,40 +831,27 @@ int bwd_tc_launch(const BwdParams& bp, const Problem& pr, const int64_t* const s
   tp.mask = bp.mask;
   tp.status = status;
   tp.timeout_ns = g_timeout_ns.load();
-  cudaError_t e = cudaMemsetAsync(acc, 0, (size_t)pr.B * pr.H * pr.Sq * 128 * 4, s);
+  cudaError_t e = cudaMemsetAsync(acc, 0, (size_t)pr.B * pr.H * pr.Sq * D * 4, s);
   if (e != cudaSuccess) return cuda_fail(e, "dq accumulator reset");
-  const long long prow = pr.B * pr.H * Sq_pad;
   const bool bf16 = pr.dtype == MLXP_DTYPE_BF16;
-  if (bf16)
-    bwd_tc_prep_kernel<__nv_bfloat16><<<(unsigned)((prow + 7) / 8), 256, 0, s>>>(bp, Sq_pad, lse2, delta);
-  else
-    bwd_tc_prep_kernel<__half><<<(unsigned)((prow + 7) / 8), 256, 0, s>>>(bp, Sq_pad, lse2, delta);
   const unsigned grid = (unsigned)(tp.n_kt * pr.B * Hkv);
-  static std::atomic<unsigned long long> attr_done[2] = {{0}, {0}};
-  int dev;
-  if (int rc = current_device(dev)) return rc;
-  if (!(attr_done[bf16].load() >> dev & 1ull)) {
-    e = bf16 ? cudaFuncSetAttribute(attn_bwd_sm100_kernel<true>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, BwdTcCfg::SMEM_ALLOC)
-             : cudaFuncSetAttribute(attn_bwd_sm100_kernel<false>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, BwdTcCfg::SMEM_ALLOC);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(backward)");
-    attr_done[bf16].fetch_or(1ull << dev);
-  }
-  if (bf16)
-    attn_bwd_sm100_kernel<true><<<grid, BwdTcCfg::THREADS, BwdTcCfg::SMEM_ALLOC, s>>>(mq, mk, mv, mdo, mdq, tp);
-  else
-    attn_bwd_sm100_kernel<false><<<grid, BwdTcCfg::THREADS, BwdTcCfg::SMEM_ALLOC, s>>>(mq, mk, mv, mdo, mdq, tp);
-  const long long n8 = pr.B * pr.H * pr.Sq * 16;
-  const unsigned pg = (unsigned)std::min<long long>((n8 + 255) / 256, (long long)sms * 32);
-  const bool vec = reinterpret_cast<uintptr_t>(bp.dq) % 16 == 0 && bp.dq_sb % 8 == 0 &&
-                   bp.dq_sh % 8 == 0 && bp.dq_ss % 8 == 0;
-  if (bf16) {
-    if (vec) bwd_tc_post_kernel<__nv_bfloat16, true><<<pg, 256, 0, s>>>(bp, acc);
-    else bwd_tc_post_kernel<__nv_bfloat16, false><<<pg, 256, 0, s>>>(bp, acc);
+  int rc;
+  if (D == 128) {
+    if (bf16) bwd_tc_aux_launch<__nv_bfloat16, 128>(bp, Sq_pad, lse2, delta, acc, false, sms, s);
+    else bwd_tc_aux_launch<__half, 128>(bp, Sq_pad, lse2, delta, acc, false, sms, s);
+    rc = bf16 ? bwd_tc_kernel_launch<true, 128>(maps, tp, grid, s)
+              : bwd_tc_kernel_launch<false, 128>(maps, tp, grid, s);
+    if (rc) return rc;
+    if (bf16) bwd_tc_aux_launch<__nv_bfloat16, 128>(bp, Sq_pad, lse2, delta, acc, true, sms, s);
+    else bwd_tc_aux_launch<__half, 128>(bp, Sq_pad, lse2, delta, acc, true, sms, s);
   } else {
-    if (vec) bwd_tc_post_kernel<__half, true><<<pg, 256, 0, s>>>(bp, acc);
-    else bwd_tc_post_kernel<__half, false><<<pg, 256, 0, s>>>(bp, acc);
+    if (bf16) bwd_tc_aux_launch<__nv_bfloat16, 64>(bp, Sq_pad, lse2, delta, acc, false, sms, s);
+    else bwd_tc_aux_launch<__half, 64>(bp, Sq_pad, lse2, delta, acc, false, sms, s);
+    rc = bf16 ? bwd_tc_kernel_launch<true, 64>(maps, tp, grid, s)
+              : bwd_tc_kernel_launch<false, 64>(maps, tp, grid, s);
+    if (rc) return rc;
+    if (bf16) bwd_tc_aux_launch<__nv_bfloat16, 64>(bp, Sq_pad, lse2, delta, acc, true, sms, s);
+    else bwd_tc_aux_launch<__half, 64>(bp, Sq_pad, lse2, delta, acc, true, sms, s);
   }
   e = cudaGetLastError();
   return e == cudaSuccess ? MLXP_OK : cuda_fail(e, "attention backward launch (tensor cores)");

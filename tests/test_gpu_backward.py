@@ -150,11 +150,12 @@ def test_cuda_core_backward_is_deterministic():
         _cuda_core_backward(False)
 
 
+@pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("case", ["causal", "noncausal", "gqa", "window", "cross", "ragged"])
-def test_tensor_core_backward_matches_oracle(dtype, case):
-    """head_dim 128 in bf16/fp16 takes the tensor-core kernel; every mask form, grouped heads,
-    lengths that are not multiples of the 64-query / 128-key tiles."""
+def test_tensor_core_backward_matches_oracle(dtype, case, D):
+    """head_dim 64 and 128 in bf16/fp16 take the tensor-core kernel; every mask form, grouped
+    heads, lengths that are not multiples of the 64-query / 128-key tiles."""
     from mlx_primitives.attention._core import _forward_impl, attention_backward
     B, H, Hkv, Sq, Skv, kw = 2, 4, 4, 320, 320, dict(causal=True)
     if case == "noncausal":
@@ -167,12 +168,12 @@ def test_tensor_core_backward_matches_oracle(dtype, case):
         Sq, Skv, kw = 100, 333, dict(causal=True, q_offset=233)
     elif case == "ragged":
         Sq, Skv = 77, 201
-    (q, k, v, do), (nq, nk, nv, ndo) = _make((B, H, Sq, 128), (B, Hkv, Skv, 128), dtype, 29)
-    args = dict(layout="BHSD", scale=128 ** -0.5, **kw)
+    (q, k, v, do), (nq, nk, nv, ndo) = _make((B, H, Sq, D), (B, Hkv, Skv, D), dtype, 29 + D)
+    args = dict(layout="BHSD", scale=D ** -0.5, **kw)
     with torch.no_grad():
         out, lse = _forward_impl(q, k, v, return_lse=True, **args)
         grads = attention_backward(q, k, v, out, lse, do, **args)
-    want = O.attention_bwd_bhsd(nq, nk, nv, ndo, 128 ** -0.5, causal=kw["causal"],
+    want = O.attention_bwd_bhsd(nq, nk, nv, ndo, D ** -0.5, causal=kw["causal"],
                                 window_left=kw.get("window_left", -1),
                                 q_offset=kw.get("q_offset", 0))
     _check(grads, want, dtype, case)
