@@ -352,9 +352,9 @@ __global__ void __launch_bounds__(448, 1)
         for (int kk = 0; kk < C::BN / 16; ++kk)
           mma_ss(tmem + C::TM_DQ, sdesc(k_mn + (uint32_t)(kk * 16 * 128 >> 4)),
                  sdesc(ds + (uint32_t)(kk * 16 * 128 >> 4)), id_dq, kk > 0 ? 1u : 0u);
+        // one commit: its completion also frees dS buffer sb and Q/dO stage s, which the dQ
+        // writer passes on (commits in the MMA stream are not free)
         tc_commit(BAR(C::B_DQF));
-        tc_commit(BAR(C::B_DSF + sb));
-        tc_commit(BAR(C::B_QE + s));
       }
       tc_commit(BAR(C::B_ACC));  // every MMA issued above is complete when this arrives
       mbar_wait_drain(BAR(C::B_ACC), 0, p.status, p.timeout_ns);
@@ -451,6 +451,10 @@ __global__ void __launch_bounds__(448, 1)
       ok = mbar_wait(BAR(C::B_DQF), i & 1, wctx, kSiteBwdWriter);
       ok = named_bar_and(1, 128, ok);  // the 128 writers agree before their named barriers
       if (!ok) break;
+      if (leader) {  // every MMA of step i is complete: its dS buffer and Q/dO stage are free
+        mbar_arrive(BAR(C::B_DSF + (i & 1)));
+        mbar_arrive(BAR(C::B_QE + i % C::NQS));
+      }
       tc_fence_after();
       const bool rows = warp - 8 < D / 32;  // warp-uniform: this warp's head-dim rows exist
       uint32_t v0[32], v1[32];
