@@ -86,6 +86,7 @@ CONFIGS = {
 }
 
 L2_BYTES = 126 * 1024 * 1024
+FP32_LANES_PER_SM = 128  # FP32 FMA lanes per SM (4 sub-partitions x 32)
 
 
 def admissible_pairs(Sq, Skv, causal, wl=-1, wr=-1, qoff=0, kvoff=0) -> int:
@@ -698,6 +699,13 @@ def main():
                "d2h_bytes_per_step": out_host.numel() * out_host.element_size(),
                "ms_per_step": e2e_ms}
 
+    # config 1 is fp32 on CUDA cores: its roofline is the FP32 pipe, not the tensor cores
+    fp32 = c["dtype"] == "fp32"
+    roof_peak = peak
+    if fp32:
+        props = torch.cuda.get_device_properties(dev)
+        max_mhz = clocks.max_mhz or 1965.0
+        roof_peak = FP32_LANES_PER_SM * 2 * props.multi_processor_count * max_mhz * 1e6 / 1e12
     line = None
     if rank == 0:
         line = {
@@ -711,13 +719,17 @@ def main():
             "tflops_per_gpu": value / world,
             "pct_of_bf16_peak": 100.0 * (value / world) / peak,
             "roofline": {
-                "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak,
+                "bound": "fp32" if fp32 else "tensor", "achieved": achieved,
+                "peak": roof_peak, "unit": "TFLOP/s", "frac": achieved / roof_peak,
                 # per-rank launches are the N=1 workload except for the ring
                 "traffic": NCU_TRAFFIC_BYTES.get(args.config) if c["api"] != "ring" else None,
                 "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + write.sum)",
                 "kernel": "attn_fwd_fp32_kernel" if c["dtype"] == "fp32" else "attn_fwd_sm100_kernel",
-                "peak_source": f"{peak_src}: bf16_tflops (burst); sustained {peak_sus}",
+                "peak_source": (f"nominal FP32 CUDA-core peak: {FP32_LANES_PER_SM} FMA lanes x 2 x "
+                                f"SMs x max SM clock (no measured fp32 figure); "
+                                f"{100.0 * achieved / peak:.1f} % of the bf16 tensor peak"
+                                if fp32 else
+                                f"{peak_src}: bf16_tflops (burst); sustained {peak_sus}"),
                 "algorithmic_flops_per_launch": flops,
                 "hbm_gbs_at_min_bytes": config_bytes(c) / (ms_local * 1e-3) / 1e9,
             },
