@@ -14,7 +14,9 @@ e2e = the same through the public API with pinned host tensors, H2D/D2H inside t
 region; roofline = the attention kernel against MEASURED_PEAKS.json; cpu_baseline = the CPU
 oracle (test infrastructure, the reference's algorithm restated) on a bounded sample.
 `--impl reference` times that CPU path alone on rank 0 (the reference's own MLX code cannot
-run on Linux without Apple hardware).
+run on Linux without Apple hardware).  Other workloads: --config c1 c3 c4 c5 (the other
+BASELINE configs), g2 (grouped-query), r2 (RoPE + attention), p4 (paged-KV decode, HBM
+roofline), b2 / b4 (backward).
 """
 
 from __future__ import annotations

@@ -28,7 +28,7 @@ oracle.attention_oracle.make_qkv, so tests regenerate them bit-for-bit from the 
 outputs (and a checksum of each input set) are stored.
 
 Run from the repository root, in a container that has the reference checkout:
-    python tests/golden/make_golden.py [--reference /path/to/mlx-primitives]
+    python tests/golden/make_golden.py --reference /path/to/mlx-primitives
 """
 
 from __future__ import annotations
@@ -177,7 +177,8 @@ def digest(*arrs) -> str:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="path of the zakkeown/mlx-primitives checkout (read only)")
     args = ap.parse_args()
     mods = load_reference(Path(args.reference))
     fl, sw, ch, osm, mk = (mods[n] for n in ["flash", "sliding_window", "chunked", "_online_softmax", "masking"])
