@@ -176,6 +176,10 @@ struct FwdParamsF32 {
   float* lse;  // [B][H][Sq] contiguous, nullable
   float scale_log2;
   MaskSpec mask;
+  // Key splits: CTA (query block, split) covers its share of the block's key tiles and writes
+  // a normalised partial at o + split * o_split, lse + split * lse_split (merged afterwards).
+  int splits;
+  long long o_split, lse_split;
 };
 
 }  // namespace mlxp

@@ -62,8 +62,10 @@ __global__ void __launch_bounds__(256) attn_fwd_fp32_kernel(const FwdParamsF32 p
   const int tid = threadIdx.x;
   const int ty = tid >> 4, tx = tid & 15;
   const int n_qblk = (p.Sq + C::BM - 1) / C::BM;
-  const int bh = blockIdx.x / n_qblk;
-  int qb = blockIdx.x - bh * n_qblk;
+  const int split = blockIdx.x % p.splits;
+  const int blk = blockIdx.x / p.splits;
+  const int bh = blk / n_qblk;
+  int qb = blk - bh * n_qblk;
   if (p.mask.causal) qb = n_qblk - 1 - qb;  // heaviest first
   const int h = bh % p.H, b = bh / p.H;
   const int q0 = qb * C::BM;
@@ -85,6 +87,12 @@ __global__ void __launch_bounds__(256) attn_fwd_fp32_kernel(const FwdParamsF32 p
   const long long r1 = (q0 + C::BM < p.Sq) ? q0 + C::BM : p.Sq;
   int tlo, thi;
   kv_tile_range(p.mask, r0, r1, C::BN, tlo, thi);
+  if (p.splits > 1) {  // this split's share of the block's key tiles
+    const int n = thi - tlo;
+    const int lo = tlo + (int)((long long)n * split / p.splits);
+    thi = tlo + (int)((long long)n * (split + 1) / p.splits);
+    tlo = lo;
+  }
 
   float m[4], l[4], acc[4][C::EPT];
 #pragma unroll
@@ -187,8 +195,8 @@ __global__ void __launch_bounds__(256) attn_fwd_fp32_kernel(const FwdParamsF32 p
     const int row = q0 + ty * 4 + i;
     if (row >= p.Sq) continue;
     const float inv_l = (l[i] > 0.f) ? 1.0f / l[i] : 0.f;
-    float* og = p.o + (long long)b * p.o_sb + (long long)h * p.o_sh + (long long)row * p.o_ss +
-                C::EPT * tx;
+    float* og = p.o + split * p.o_split + (long long)b * p.o_sb + (long long)h * p.o_sh +
+                (long long)row * p.o_ss + C::EPT * tx;
     if ((reinterpret_cast<uintptr_t>(og) & 7) == 0) {
 #pragma unroll
       for (int d = 0; d < C::EPT; d += 2)
@@ -198,7 +206,7 @@ __global__ void __launch_bounds__(256) attn_fwd_fp32_kernel(const FwdParamsF32 p
       for (int d = 0; d < C::EPT; ++d) og[d] = acc[i][d] * inv_l;
     }
     if (p.lse != nullptr && tx == 0)
-      p.lse[((long long)b * p.H + h) * p.Sq + row] =
+      p.lse[split * p.lse_split + ((long long)b * p.H + h) * p.Sq + row] =
           (l[i] > 0.f) ? (m[i] + log2f(l[i])) * 0.69314718055994531f : -INFINITY;
   }
 }

@@ -257,6 +257,19 @@ int choose_splits(const Problem& pr, int sms) {
   return s;
 }
 
+// Key splits of the fp32 kernel: its CTAs (64 query rows) are all resident at once for small
+// problems, so the time is the longest chain of key tiles (the last query block under a causal
+// mask).  Split until there are about four CTAs per resident slot (3 per SM), keeping at least
+// 4 key tiles per split and at most 8 splits.
+int choose_splits_f32(const Problem& pr, int sms) {
+  const int bm = 64, bn = pr.D >= 128 ? 32 : 64;
+  const long long base = (pr.Sq + bm - 1) / bm * pr.B * pr.H;
+  const long long kv_tiles = (pr.Skv + bn - 1) / bn;
+  int s = 1;
+  while (s < 8 && base * s < 4LL * 3 * sms && kv_tiles / (2 * s) >= 4) s *= 2;
+  return s;
+}
+
 size_t split_workspace(const Problem& pr, int splits) {
   if (splits <= 1) return 0;
   const size_t rows = (size_t)splits * pr.B * pr.H * pr.Sq;
@@ -327,7 +340,7 @@ int launch_f32_t(const FwdParamsF32& p, cudaStream_t s) {
   using C = F32Cfg<D>;
   auto kern = attn_fwd_fp32_kernel<D>;
   if (int rc = ensure_smem_attr(kern, C::SMEM_BYTES, 1u << (8 + (D / 32)))) return rc;
-  const long long grid = (long long)((p.Sq + C::BM - 1) / C::BM) * p.B * p.H;
+  const long long grid = (long long)((p.Sq + C::BM - 1) / C::BM) * p.B * p.H * p.splits;
   if (grid <= 0) return MLXP_OK;
   kern<<<(unsigned)grid, 256, C::SMEM_BYTES, s>>>(p);
   cudaError_t e = cudaGetLastError();
@@ -430,11 +443,41 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
     p.lse = lse;
     p.scale_log2 = scale_log2;
     p.mask = mask_of(pr);
-    switch (pr.D) {
-      case 32: return launch_f32_t<32>(p, stream);
-      case 64: return launch_f32_t<64>(p, stream);
-      default: return launch_f32_t<128>(p, stream);
+    int splits = 1;
+    if (!out_f32) {
+      if (kv_splits == 0) splits = choose_splits_f32(pr, sms);
+      else if (kv_splits > 1) splits = (int)std::min<int64_t>(kv_splits, (pr.Skv + 31) / 32);
     }
+    p.splits = splits;
+    float* o_parts = nullptr;
+    float* lse_parts = nullptr;
+    if (splits > 1) {  // partials in the workspace, then the LSE merge into o
+      const size_t need = split_workspace(pr, splits);
+      if (ws == nullptr || ws_bytes < need)
+        return fail(MLXP_ERR_WORKSPACE, "split-KV needs %zu bytes of workspace, got %zu", need,
+                    ws_bytes);
+      if (reinterpret_cast<uintptr_t>(ws) % 256)
+        return fail(MLXP_ERR_INVALID, "workspace must be 256-byte aligned");
+      const long long rows = pr.B * pr.H * pr.Sq;
+      o_parts = static_cast<float*>(ws);
+      lse_parts = reinterpret_cast<float*>(static_cast<char*>(ws) +
+                                           ((size_t)splits * rows * pr.D * 4 + 255) / 256 * 256);
+      p.o = o_parts;
+      p.o_sh = pr.Sq * pr.D;
+      p.o_sb = pr.H * p.o_sh;
+      p.o_ss = pr.D;
+      p.o_split = rows * pr.D;
+      p.lse = lse_parts;
+      p.lse_split = rows;
+    }
+    int rc;
+    switch (pr.D) {
+      case 32: rc = launch_f32_t<32>(p, stream); break;
+      case 64: rc = launch_f32_t<64>(p, stream); break;
+      default: rc = launch_f32_t<128>(p, stream); break;
+    }
+    if (rc || splits <= 1) return rc;
+    return merge_dispatch(o_parts, lse_parts, splits, o, lse, pr, os, stream);
   }
 
   const bool bf16 = pr.dtype == MLXP_DTYPE_BF16;
@@ -929,14 +972,15 @@ size_t mlxp_attn_workspace_size(int dtype, int64_t B, int64_t H, int64_t Sq, int
                                 int64_t kv_pos_offset, int64_t kv_splits) {
   Problem pr{dtype, B, H, Sq, Skv, D, causal ? 1 : 0, window_left, window_right, q_pos_offset,
              kv_pos_offset};
-  if (validate(pr) != MLXP_OK || dtype == MLXP_DTYPE_FP32 || Sq == 0 || Skv == 0) return 0;
+  if (validate(pr) != MLXP_OK || Sq == 0 || Skv == 0) return 0;
+  const bool fp32 = dtype == MLXP_DTYPE_FP32;
   int splits = 1;
   if (kv_splits == 0) {
     int sms = 148;
     if (device_info(nullptr, &sms) != MLXP_OK) sms = 148;
-    splits = choose_splits(pr, sms);
+    splits = fp32 ? choose_splits_f32(pr, sms) : choose_splits(pr, sms);
   } else if (kv_splits > 1) {
-    splits = (int)std::min<int64_t>(kv_splits, (Skv + kBN - 1) / kBN);
+    splits = (int)std::min<int64_t>(kv_splits, (Skv + (fp32 ? 31 : kBN - 1)) / (fp32 ? 32 : kBN));
   }
   return split_workspace(pr, splits);
 }

@@ -40,13 +40,14 @@ def _dims(t: torch.Tensor, layout: str):
 
 def attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, layout: str,
                       scale: float, causal: bool, window_left: int = -1, window_right: int = -1,
-                      q_offset: int = 0, kv_offset: int = 0, kv_splits: int = 1,
+                      q_offset: int = 0, kv_offset: int = 0, kv_splits: int = 0,
                       return_lse: bool = False):
     """O = softmax(scale * Q K^T + mask) V for 4-D q/k/v in `layout` ("BSHD" or "BHSD").
 
     Masking is in absolute positions (qpos = i + q_offset, kpos = j + kv_offset): causal keeps
     kpos <= qpos, window_left keeps qpos - kpos <= window_left, window_right keeps
-    kpos - qpos <= window_right (-1 = unbounded).  Returns O with q's layout and dtype and,
+    kpos - qpos <= window_right (-1 = unbounded).  kv_splits: 0 = the library's choice of key
+    splits (merged by log-sum-exp), 1 = none, n = n.  Returns O with q's layout and dtype and,
     if return_lse, the fp32 log-sum-exp [B, H, Sq].
 
     Differentiable: when autograd records and q, k or v requires grad, the backward runs the
@@ -87,7 +88,7 @@ _BWD_HEAD_DIMS = (32, 64, 128)
 
 def attention_backward(q, k, v, out, lse, dout, *, layout: str, scale: float, causal: bool,
                        window_left: int = -1, window_right: int = -1, q_offset: int = 0,
-                       kv_offset: int = 0, kv_splits: int = 1):
+                       kv_offset: int = 0, kv_splits: int = 0):
     """dQ, dK, dV of attention_forward (same arguments) from its output and log-sum-exp."""
     B, H, Sq, D = _dims(q, layout)
     _, Hkv, Skv, _ = _dims(k, layout)
@@ -125,7 +126,7 @@ def attention_backward(q, k, v, out, lse, dout, *, layout: str, scale: float, ca
 
 def _forward_impl(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, layout: str,
                   scale: float, causal: bool, window_left: int = -1, window_right: int = -1,
-                  q_offset: int = 0, kv_offset: int = 0, kv_splits: int = 1,
+                  q_offset: int = 0, kv_offset: int = 0, kv_splits: int = 0,
                   return_lse: bool = False):
     if q.dtype not in _lib.DTYPE_CODES:
         raise ValueError(f"unsupported dtype {q.dtype}; expected float32, bfloat16 or float16")
