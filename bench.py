@@ -40,10 +40,11 @@ for _p in (REPO, REPO / "mlx-primitives_b200"):
 
 METRIC = "attention fwd TFLOPS/GPU and % of BF16 tensor peak at 1/2/4/8 B200"
 
-# DRAM bytes (read + write) of one attention-kernel launch at N=1, from one ncu capture of the
-# same command (profiles/attn_fwd_sm100_c2_full.md, profiles/attn_fwd_sm100_c4_full.md);
-# null where no capture of that configuration has been summarised.
-NCU_TRAFFIC_BYTES = {"c2": 522.9e6, "c4": 2.409e9}
+# DRAM bytes (read + write) of one launch of the dominant kernel at N=1, from one ncu capture of
+# the same command (profiles/attn_fwd_sm100_c2_full.md, profiles/attn_fwd_sm100_c4_full.md,
+# profiles/paged_attn_tma_p4.md, profiles/attn_bwd_sm100_b2.md); null where no capture of that
+# configuration has been summarised.
+NCU_TRAFFIC_BYTES = {"c2": 522.9e6, "c4": 2.409e9, "p4": 541.18e6, "b2": 1.3016e9}
 
 CONFIGS = {
     "c1": dict(workload="flash_attention fp32 BSHD causal (config 1)", api="flash", dtype="fp32",
@@ -536,7 +537,9 @@ def bench_backward(args, c, world, rank, local):
             "config": config_json(c, world),
             "roofline": {"bound": "tensor", "achieved": flops / (ms_local * 1e-3) / 1e12,
                          "peak": peak, "unit": "TFLOP/s",
-                         "frac": flops / (ms_local * 1e-3) / 1e12 / peak, "traffic": None,
+                         "frac": flops / (ms_local * 1e-3) / 1e12 / peak,
+                         "traffic": NCU_TRAFFIC_BYTES.get(args.config),
+                         "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + write.sum)",
                          "kernel": "attn_bwd_sm100_kernel (+ prep, dQ convert)",
                          "peak_source": f"{peak_src}: bf16_tflops (the tensor-core target)",
                          "algorithmic_flops_per_launch": flops},
