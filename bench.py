@@ -211,6 +211,28 @@ def cpu_oracle_tflops(c, budget_s: float, max_units: int | None = None):
         q, k, v = (O.round_bf16(a) for a in (q, k, v))
     units, t_total = 0, 0.0
     cap = max_units or c["B"] * c["H"]
+    if S * Skv > (1 << 26):
+        # a dense score matrix of this unit would not fit in host memory (config 5: 128K x 128K):
+        # time exact rows (each against its whole admissible key range) on an even sample of
+        # query rows and count only their pairs
+        rows = np.linspace(0, S - 1, 64).astype(np.int64)
+        kpos = np.arange(Skv)[None, :]
+        qpos = rows[:, None] + qoff
+        ok = np.ones((len(rows), Skv), dtype=bool)
+        if c["causal"]:
+            ok &= kpos <= qpos
+        if c["window"] >= 0:
+            ok &= (qpos - kpos) <= c["window"]
+        if wr >= 0:
+            ok &= (kpos - qpos) <= wr
+        row_pairs = int(ok.sum())
+        while units < cap and (units == 0 or t_total < budget_s):
+            t0 = time.perf_counter()
+            O.attention_rows_bhsd(q, k, v, rows, 1.0 / math.sqrt(D), causal=c["causal"],
+                                  window_left=c["window"], window_right=wr, q_offset=qoff)
+            t_total += time.perf_counter() - t0
+            units += 1
+        return 4.0 * D * row_pairs * units / t_total / 1e12, units, t_total, threads
     while units < cap and (units == 0 or t_total < budget_s):
         t0 = time.perf_counter()
         O.attention_bhsd(q, k, v, 1.0 / math.sqrt(D), causal=c["causal"], window_left=c["window"],
@@ -238,7 +260,9 @@ def run_reference_arm(args, c, rank):
     unit_flops = 4.0 * D * admissible_pairs(c["S"], c["Skv"], c["causal"], c["window"], wr, qoff)
     secs = sum(per_step)
     value = unit_flops * total_units / secs / 1e12
-    sample = f"{total_units} (batch, head) units of {c['workload']}, one per step, fp32 numpy"
+    sample = (f"{total_units} x 64 evenly spaced query rows of one (batch, head) unit of "
+              f"{c['workload']}, exact fp64 rows, one per step" if c["S"] * c["Skv"] > (1 << 26)
+              else f"{total_units} (batch, head) units of {c['workload']}, one per step, fp32 numpy")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOPS",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -746,8 +770,11 @@ def main():
             tf, units, secs, threads = cpu_oracle_tflops(c, budget_s=args.cpu_budget)
             line["cpu_baseline"] = {
                 "value": tf, "unit": "TFLOPS", "cores": threads, "kind": "port",
-                "sample": f"{units} of {c['B'] * c['H']} (batch, head) units, dense fp32 numpy, "
-                          f"{secs:.1f} s"}
+                "sample": (f"{units} x 64 evenly spaced query rows of one (batch, head) unit "
+                           f"(exact fp64 rows; a dense unit does not fit in host memory), "
+                           f"{secs:.1f} s" if c["S"] * c["Skv"] > (1 << 26) else
+                           f"{units} of {c['B'] * c['H']} (batch, head) units, dense fp32 numpy, "
+                           f"{secs:.1f} s")}
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

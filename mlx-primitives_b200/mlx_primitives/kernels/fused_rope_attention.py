@@ -65,6 +65,19 @@ def fast_fused_rope_attention(
         raise ValueError(f"head_dim must be even for RoPE, got {head_dim}")
     if scale is None:
         scale = 1.0 / math.sqrt(head_dim)
+    if q.device.type == "cpu":
+        # host tensors: one copy in (from pinned memory when the caller pinned it), RoPE and
+        # attention on the device, one copy out into pinned memory
+        if not torch.cuda.is_available():
+            raise RuntimeError("fused_rope_attention requires a CUDA device (no CPU fallback)")
+        dev = torch.device("cuda", torch.cuda.current_device())
+        qd, kd, vd = (t.to(dev, non_blocking=True) for t in (q, k, v))
+        out = fast_fused_rope_attention(qd, kd, vd, scale, cos_cache, sin_cache, rope_base,
+                                        q_offset, kv_offset, causal, use_tiled)
+        host = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+        host.copy_(out, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+        return host
     if cos_cache is None or sin_cache is None:
         max_pos = max(seq_q + q_offset, seq_kv + kv_offset)
         dev = q.device if q.device.type == "cuda" else torch.device(
