@@ -248,18 +248,16 @@ def run_reference_arm(args, c, rank):
         return
     per_step = []
     total_units = 0
+    total_flops = 0.0
     threads = None
     for i in range(args.warmup + args.steps):
         tf, units, secs, threads = cpu_oracle_tflops(c, budget_s=0.0, max_units=1)
         if i >= args.warmup:
             per_step.append(secs)
             total_units += units
-    D = c["D"]
-    wr = -1 if c["causal"] else c["window"]
-    qoff = (c["Skv"] - c["S"]) if (c["api"] == "flash" and c["causal"]) else 0
-    unit_flops = 4.0 * D * admissible_pairs(c["S"], c["Skv"], c["causal"], c["window"], wr, qoff)
+            total_flops += tf * 1e12 * secs  # the sample's own algorithmic FLOPs
     secs = sum(per_step)
-    value = unit_flops * total_units / secs / 1e12
+    value = total_flops / secs / 1e12
     sample = (f"{total_units} x 64 evenly spaced query rows of one (batch, head) unit of "
               f"{c['workload']}, exact fp64 rows, one per step" if c["S"] * c["Skv"] > (1 << 26)
               else f"{total_units} (batch, head) units of {c['workload']}, one per step, fp32 numpy")
