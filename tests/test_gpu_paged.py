@@ -201,3 +201,30 @@ def test_deterministic_and_large_decode():
         sub_bt = np.arange(len(ids), dtype=np.int32)[None]
         want = _oracle(nq[b:b + 1], nk[ids], nv[ids], sub_bt, ctx[b:b + 1], block_size=16)
         assert _maxabs(o1[b:b + 1], want) <= 2e-2
+
+
+@pytest.mark.parametrize("seed", list(range(2000, 2040)))
+def test_paged_random(seed):
+    """Seeded random sweep: dtype, head_dim, block size (TMA and cp.async kernels), pool head
+    groups, decode and short prefill, causal, ALiBi, holes in the tables, empty and
+    over-long contexts, automatic and forced splits."""
+    rs = np.random.RandomState(seed)
+    dtype = [torch.bfloat16, torch.float16, torch.float32][rs.randint(3)]
+    D = int(rs.choice([32, 64, 128]))
+    bs = int(rs.choice([8, 16, 24, 32, 64]))
+    Hkv = int(rs.choice([1, 2, 4]))
+    H = Hkv * int(rs.choice([1, 2, 4]))
+    B = int(rs.randint(1, 5))
+    Sq = int(rs.choice([1, 1, 1, 3, 17]))
+    lens = [int(rs.choice([0, rs.randint(1, 40), rs.randint(40, 900)])) for _ in range(B)]
+    t, n, bt, ctx = _case(B, Sq, H, D, Hkv, bs, lens, dtype, seed=seed, holes=int(rs.randint(3)))
+    if rs.randint(4) == 0:  # a context longer than the table holds
+        ctx = ctx + bs * bt.shape[1]
+    causal = bool(rs.randint(2))
+    alibi = bool(rs.randint(2))
+    slopes = O.get_alibi_slopes(H) if alibi else None
+    splits = int(rs.choice([0, 0, 1, 5]))
+    out = _run(t, bt, ctx, kv_splits=splits, block_size=bs, causal=causal,
+               alibi_slopes=torch.from_numpy(slopes).cuda() if alibi else None)
+    want = _oracle(*n, bt, ctx, block_size=bs, causal=causal, alibi_slopes=slopes)
+    assert _maxabs(out, want) <= TOL[dtype], (seed, dtype, D, bs, H, Hkv, B, Sq, lens)
