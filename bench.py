@@ -589,6 +589,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--forward-kernel", default="single", choices=["single", "pair"],
+                    help="bf16 head_dim-128 forward: the default single-SM kernel or the opt-in "
+                         "CTA-pair kernel (mlxp_set_forward_kernel)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
@@ -619,6 +622,10 @@ def main():
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    pair = args.forward_kernel == "pair" and c["dtype"] != "fp32" and c["D"] == 128
+    if pair:
+        from mlx_primitives import _lib
+        _lib.lib().mlxp_set_forward_kernel(1)
 
     dtype = torch.float32 if c["dtype"] == "fp32" else torch.bfloat16
     B, H, S, Skv, D = c["B"], c["H"], c["S"], c["Skv"], c["D"]
@@ -742,16 +749,18 @@ def main():
             "scaling": "strong" if c["api"] == "ring" else "weak", "vs_baseline": None,
             "dtype": "f32" if c["dtype"] == "fp32" else "bf16",
             "data": "synthetic: seeded N(0, std^2) tensors generated on device (seed 42 + rank)",
-            "config": config_json(c, world),
+            "config": dict(config_json(c, world), **({"forward_kernel": "pair"} if pair else {})),
             "tflops_per_gpu": value / world,
             "pct_of_bf16_peak": 100.0 * (value / world) / peak,
             "roofline": {
                 "bound": "fp32" if fp32 else "tensor", "achieved": achieved,
                 "peak": roof_peak, "unit": "TFLOP/s", "frac": achieved / roof_peak,
                 # per-rank launches are the N=1 workload except for the ring
-                "traffic": NCU_TRAFFIC_BYTES.get(args.config) if c["api"] != "ring" else None,
+                "traffic": (NCU_TRAFFIC_BYTES.get(args.config)
+                            if c["api"] != "ring" and not pair else None),
                 "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + write.sum)",
-                "kernel": "attn_fwd_fp32_kernel" if c["dtype"] == "fp32" else "attn_fwd_sm100_kernel",
+                "kernel": ("attn_fwd_fp32_kernel" if c["dtype"] == "fp32" else
+                           "attn_fwd_2sm_kernel" if pair else "attn_fwd_sm100_kernel"),
                 "peak_source": (f"nominal FP32 CUDA-core peak: {FP32_LANES_PER_SM} FMA lanes x 2 x "
                                 f"SMs x max SM clock (no measured fp32 figure); "
                                 f"{100.0 * achieved / peak:.1f} % of the bf16 tensor peak"
