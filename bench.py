@@ -44,7 +44,7 @@ METRIC = "attention fwd TFLOPS/GPU and % of BF16 tensor peak at 1/2/4/8 B200"
 # the same command (profiles/attn_fwd_sm100_c2_full.md, profiles/attn_fwd_sm100_c4_full.md,
 # profiles/paged_attn_tma_p4.md, profiles/attn_bwd_sm100_b2.md); null where no capture of that
 # configuration has been summarised.
-NCU_TRAFFIC_BYTES = {"c2": 522.9e6, "c4": 2.409e9, "p4": 541.18e6, "b2": 1.3016e9}
+NCU_TRAFFIC_BYTES = {"c2": 522.9e6, "c4": 2.278e9, "p4": 541.18e6, "b2": 1.3016e9}
 
 CONFIGS = {
     "c1": dict(workload="flash_attention fp32 BSHD causal (config 1)", api="flash", dtype="fp32",
