@@ -40,10 +40,9 @@ for _p in (REPO, REPO / "mlx-primitives_b200"):
 
 METRIC = "attention fwd TFLOPS/GPU and % of BF16 tensor peak at 1/2/4/8 B200"
 
-# DRAM bytes (read + write) of one launch of the dominant kernel at N=1, from one ncu capture of
-# the same command (profiles/attn_fwd_sm100_c2_full.md, profiles/attn_fwd_sm100_c4_full.md,
-# profiles/paged_attn_tma_p4.md, profiles/attn_bwd_sm100_b2.md); null where no capture of that
-# configuration has been summarised.
+# DRAM bytes (read + write) of one launch of the dominant kernel at N=1 (attn_fwd_sm100_kernel
+# for c2 and c4, paged_attn_tma_kernel for p4, attn_bwd_sm100_kernel for b2), from one ncu
+# capture of the same command; null where no capture of that configuration was taken.
 NCU_TRAFFIC_BYTES = {"c2": 522.9e6, "c4": 2.278e9, "p4": 541.18e6, "b2": 1.3016e9}
 
 CONFIGS = {
@@ -188,17 +187,32 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------ CPU side
+def blas_threads() -> int:
+    """Threads of the BLAS pool the numpy oracle runs on (the cores the CPU baseline uses)."""
+    try:
+        from threadpoolctl import threadpool_info
+        return max((i.get("num_threads", 1) for i in threadpool_info()), default=os.cpu_count())
+    except Exception:  # noqa: BLE001
+        return os.cpu_count()
+
+
+def host_cores() -> dict:
+    """The GPU box's host: logical CPUs and torch's intra-op thread count."""
+    try:
+        import torch
+        torch_threads = torch.get_num_threads()
+    except Exception:  # noqa: BLE001
+        torch_threads = None
+    return {"os_cpu_count": os.cpu_count(), "torch_num_threads": torch_threads}
+
+
 def cpu_oracle_tflops(c, budget_s: float, max_units: int | None = None):
     """Time the CPU oracle (dense fp32 restatement of the reference's CPU path, numpy + BLAS)
     on whole (batch, head) units of config c until budget_s is used.  Returns (TFLOPS, units,
     seconds, threads)."""
     from oracle import attention_oracle as O
 
-    try:
-        from threadpoolctl import threadpool_info
-        threads = max((i.get("num_threads", 1) for i in threadpool_info()), default=os.cpu_count())
-    except Exception:  # noqa: BLE001
-        threads = os.cpu_count()
+    threads = blas_threads()
     D, S, Skv = c["D"], c["S"], c["Skv"]
     wr = -1 if c["causal"] else c["window"]
     qoff = (Skv - S) if (c["api"] == "flash" and c["causal"]) else 0
@@ -267,7 +281,7 @@ def run_reference_arm(args, c, rank):
         "ms_per_step": 1e3 * secs / max(len(per_step), 1), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": config_json(c, args.gpus),
-        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": threads, "kind": "port",
+        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": threads, **host_cores(), "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "MLX (the reference's runtime) cannot run on this Linux/NVIDIA box; this arm times "
@@ -314,11 +328,7 @@ def cpu_paged_sample(c, budget_s, max_seqs=None):
     """The oracle's paged_attention (fp32 numpy) on whole sequences of config c until budget_s
     is used.  Returns (TFLOPS, sequences, seconds, threads)."""
     from oracle import attention_oracle as O
-    try:
-        from threadpoolctl import threadpool_info
-        threads = max((i.get("num_threads", 1) for i in threadpool_info()), default=os.cpu_count())
-    except Exception:  # noqa: BLE001
-        threads = os.cpu_count()
+    threads = blas_threads()
     n = (c["Skv"] + c["block"] - 1) // c["block"]
     q, kp, vp = O.make_qkv((1, 1, c["H"], c["D"]), (n, c["block"], c["H"], c["D"]), seed=7)
     if c["dtype"] != "fp32":
@@ -357,7 +367,7 @@ def bench_paged(args, c, world, rank, local):
             "ms_per_step": 1e3 * sum(per) / len(per), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": paged_config_json(c, args.gpus),
-            "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": threads, "kind": "port",
+            "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": threads, **host_cores(), "kind": "port",
                              "sample": f"{seqs_total} sequences of {c['workload']}, one per step, "
                                        "fp32 numpy (gather + dense masked softmax, as the reference)"},
             "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0,
@@ -488,7 +498,7 @@ def bench_paged(args, c, world, rank, local):
         if world == 1 and args.cpu_budget > 0:
             tf, seqs, secs, threads = cpu_paged_sample(c, args.cpu_budget)
             line["cpu_baseline"] = {
-                "value": tf, "unit": "TFLOPS", "cores": threads, "kind": "port",
+                "value": tf, "unit": "TFLOPS", "cores": threads, **host_cores(), "kind": "port",
                 "sample": f"{seqs} of {B} sequences, oracle paged_attention fp32 numpy, "
                           f"{secs:.1f} s"}
     if world > 1:
@@ -589,9 +599,6 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-budget", type=float, default=15.0)
-    ap.add_argument("--forward-kernel", default="single", choices=["single", "pair"],
-                    help="bf16 head_dim-128 forward: the default single-SM kernel or the opt-in "
-                         "CTA-pair kernel (mlxp_set_forward_kernel)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
@@ -622,11 +629,6 @@ def main():
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    pair = args.forward_kernel == "pair" and c["dtype"] != "fp32" and c["D"] == 128
-    if pair:
-        from mlx_primitives import _lib
-        _lib.lib().mlxp_set_forward_kernel(1)
-
     dtype = torch.float32 if c["dtype"] == "fp32" else torch.bfloat16
     B, H, S, Skv, D = c["B"], c["H"], c["S"], c["Skv"], c["D"]
     shape_q = (B, H, S, D) if c["layout"] == "BHSD" else (B, S, H, D)
@@ -749,7 +751,7 @@ def main():
             "scaling": "strong" if c["api"] == "ring" else "weak", "vs_baseline": None,
             "dtype": "f32" if c["dtype"] == "fp32" else "bf16",
             "data": "synthetic: seeded N(0, std^2) tensors generated on device (seed 42 + rank)",
-            "config": dict(config_json(c, world), **({"forward_kernel": "pair"} if pair else {})),
+            "config": config_json(c, world),
             "tflops_per_gpu": value / world,
             "pct_of_bf16_peak": 100.0 * (value / world) / peak,
             "roofline": {
@@ -757,10 +759,10 @@ def main():
                 "peak": roof_peak, "unit": "TFLOP/s", "frac": achieved / roof_peak,
                 # per-rank launches are the N=1 workload except for the ring
                 "traffic": (NCU_TRAFFIC_BYTES.get(args.config)
-                            if c["api"] != "ring" and not pair else None),
+                            if c["api"] != "ring" else None),
                 "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + write.sum)",
                 "kernel": ("attn_fwd_fp32_kernel" if c["dtype"] == "fp32" else
-                           "attn_fwd_2sm_kernel" if pair else "attn_fwd_sm100_kernel"),
+                           "attn_fwd_sm100_kernel"),
                 "peak_source": (f"nominal FP32 CUDA-core peak: {FP32_LANES_PER_SM} FMA lanes x 2 x "
                                 f"SMs x max SM clock (no measured fp32 figure); "
                                 f"{100.0 * achieved / peak:.1f} % of the bf16 tensor peak"
@@ -776,7 +778,7 @@ def main():
         if world == 1 and args.cpu_budget > 0:
             tf, units, secs, threads = cpu_oracle_tflops(c, budget_s=args.cpu_budget)
             line["cpu_baseline"] = {
-                "value": tf, "unit": "TFLOPS", "cores": threads, "kind": "port",
+                "value": tf, "unit": "TFLOPS", "cores": threads, **host_cores(), "kind": "port",
                 "sample": (f"{units} x 64 evenly spaced query rows of one (batch, head) unit "
                            f"(exact fp64 rows; a dense unit does not fit in host memory), "
                            f"{secs:.1f} s" if c["S"] * c["Skv"] > (1 << 26) else

@@ -235,12 +235,6 @@ int mlxp_attn_bwd(const void* q, const void* k, const void* v, const void* o, co
  */
 int mlxp_set_backward_path(int cuda_cores_only);
 
-/* Which tensor-core forward serves head_dim 128 (bf16/fp16): 0 (default) = the single-SM
- * kernel (two 128-row query tiles per CTA, ping-pong); 1 = the CTA-pair kernel (clusters of two
- * CTAs, 2-SM MMAs, three S buffers per CTA) — same results, measured slower, kept for
- * cross-checking.  Process-wide; serves the same reference entry points as mlxp_attn_fwd. */
-int mlxp_set_forward_kernel(int pair);
-
 /* Bytes of workspace mlxp_attn_bwd needs (the per-row dO . O terms; for the tensor-core path
  * also the padded log-sum-exp rows and the fp32 dQ accumulator). */
 size_t mlxp_attn_bwd_workspace_size(int dtype, int64_t B, int64_t H, int64_t Sq, int64_t Skv,

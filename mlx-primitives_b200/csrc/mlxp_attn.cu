@@ -20,7 +20,6 @@
 #include "attn_common.cuh"
 #include "attn_fwd_fp32.cuh"
 #include "attn_fwd_sm100.cuh"
-#include "attn_fwd_2sm.cuh"
 #include "rope.cuh"
 #include "paged_attn.cuh"
 #include "attn_bwd.cuh"
@@ -56,9 +55,6 @@ int cuda_fail(cudaError_t e, const char* what) {
 std::atomic<unsigned long long> g_timeout_ns{2000000000ull};
 // Test hook (mlxp_set_backward_path): 1 = always the CUDA-core backward.
 std::atomic<int> g_bwd_force_cuda_cores{0};
-// mlxp_set_forward_kernel: 1 = head_dim 128 on the CTA-pair kernel (attn_fwd_2sm.cuh) instead
-// of the single-SM ping-pong kernel (the default: faster on every shape measured).
-std::atomic<int> g_fwd_pair{0};
 
 constexpr int kMaxDevices = 64;
 std::mutex g_dev_mu;
@@ -335,49 +331,8 @@ struct TcKernel {
   }
 };
 
-// head_dim 128 on CTA pairs (attn_fwd_2sm.cuh).  The grid is as many pairs as can be resident
-// at once (one CTA per SM, both CTAs of a pair on one TPC), at most one per work item.
-template <bool BF16>
-struct TcKernel2Sm {
-  using Cfg = Fwd2SmCfg<BF16>;
-  static constexpr unsigned kBit = 1u << (BF16 ? 4 : 5);
-  static int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                    const CUtensorMap& mo, const FwdParams& p, cudaStream_t stream) {
-    auto kern = attn_fwd_2sm_kernel<BF16>;
-    if (int rc = ensure_smem_attr(kern, Cfg::SMEM_ALLOC, kBit)) return rc;
-    const long long items = (long long)p.n_qblk * p.B * p.H * p.splits;
-    if (items <= 0) return MLXP_OK;
-    int dev;
-    if (int rc = current_device(dev)) return rc;
-    static int max_pairs[kMaxDevices] = {};
-    {
-      std::lock_guard<std::mutex> g(g_dev_mu);
-      if (max_pairs[dev] == 0) {
-        cudaLaunchConfig_t cfg{};
-        cfg.gridDim = dim3(2, 1, 1);
-        cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
-        cfg.dynamicSmemBytes = Cfg::SMEM_ALLOC;
-        int n = 0;
-        cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
-        if (e != cudaSuccess || n <= 0)
-          return e != cudaSuccess ? cuda_fail(e, "cudaOccupancyMaxActiveClusters")
-                                  : fail(MLXP_ERR_CUDA, "no CTA pair of the forward kernel fits");
-        max_pairs[dev] = n;
-      }
-    }
-    const long long pairs = std::min<long long>(items, max_pairs[dev]);
-    kern<<<(unsigned)(2 * pairs), Cfg::THREADS, Cfg::SMEM_ALLOC, stream>>>(mq, mk, mv, mo, p);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_fail(e, "attn_fwd_2sm launch");
-    return MLXP_OK;
-  }
-};
-
-int launch_tc(int D, bool bf16, bool pair, const CUtensorMap& mq, const CUtensorMap& mk,
+int launch_tc(int D, bool bf16, const CUtensorMap& mq, const CUtensorMap& mk,
               const CUtensorMap& mv, const CUtensorMap& mo, const FwdParams& p, cudaStream_t s) {
-  if (D == 128 && pair)
-    return bf16 ? TcKernel2Sm<true>::launch(mq, mk, mv, mo, p, s)
-                : TcKernel2Sm<false>::launch(mq, mk, mv, mo, p, s);
   if (D == 128) return bf16 ? TcKernel<128, true>::launch(mq, mk, mv, mo, p, s)
                             : TcKernel<128, false>::launch(mq, mk, mv, mo, p, s);
   return bf16 ? TcKernel<64, true>::launch(mq, mk, mv, mo, p, s)
@@ -536,10 +491,7 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
       bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   if (int rc = make_tmap(q, dt16, 2, pr.B, pr.H, pr.Sq, pr.D, qs, 128, 64, "q", &mq, &p.cq))
     return rc;
-  // the CTA-pair kernel (head_dim 128) loads K in halves of 64 keys
-  const bool pair = pr.D == 128 && g_fwd_pair.load() != 0;
-  const int k_box = pair ? kBN / 2 : kBN;
-  if (int rc = make_tmap(k, dt16, 2, pr.B, pr.kv_heads(), pr.Skv, pr.D, ks, k_box, 64, "k", &mk,
+  if (int rc = make_tmap(k, dt16, 2, pr.B, pr.kv_heads(), pr.Skv, pr.D, ks, kBN, 64, "k", &mk,
                          &p.ck))
     return rc;
   if (int rc = make_tmap(v, dt16, 2, pr.B, pr.kv_heads(), pr.Skv, pr.D, vs, kBN, 64, "v", &mv,
@@ -593,7 +545,7 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
                          : make_tmap(o, dt16, 2, pr.B, pr.H, pr.Sq, pr.D, os, 128, 64, "o", &mo,
                                      &p.co))
       return rc;
-    return launch_tc((int)pr.D, bf16, pair, mq, mk, mv, mo, p, stream);
+    return launch_tc((int)pr.D, bf16, mq, mk, mv, mo, p, stream);
   }
   const size_t need = split_workspace(pr, splits);
   if (ws == nullptr || ws_bytes < need)
@@ -615,7 +567,7 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
                            pr.H, pr.Sq, pr.D, ws_st, 128, 32, "split workspace", &mo, &p.co))
       return rc;
   }
-  if (int rc = launch_tc((int)pr.D, bf16, pair, mq, mk, mv, mo, p, stream)) return rc;
+  if (int rc = launch_tc((int)pr.D, bf16, mq, mk, mv, mo, p, stream)) return rc;
   return merge_dispatch(o_parts, lse_parts, splits, o, lse, pr, os, stream);
 }
 
@@ -1397,10 +1349,6 @@ int mlxp_set_backward_path(int cuda_cores_only) {
   return MLXP_OK;
 }
 
-int mlxp_set_forward_kernel(int pair) {
-  g_fwd_pair.store(pair ? 1 : 0);
-  return MLXP_OK;
-}
 
 int mlxp_set_wait_timeout_ns(uint64_t ns) {
   if (ns == 0) return fail(MLXP_ERR_INVALID, "timeout must be positive");

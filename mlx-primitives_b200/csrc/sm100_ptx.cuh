@@ -449,121 +449,4 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   }
 }
 
-// ------------------------------------------------------------------------------------------
-// CTA pairs (clusters of two) and the 2-SM tensor-core forms (cta_group::2).  The even CTA of
-// the pair issues every MMA; an M=256 MMA takes rows 0-127 of A and D from the even CTA's
-// shared memory / TMEM and rows 128-255 from the odd CTA's, and each CTA holds half of B's N
-// columns (the even CTA the first half) at the same shared-memory offset.
-// ------------------------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t cluster_cta_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-// Every thread of both CTAs: a full barrier over the pair (release / acquire).
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
-                   : "memory");
-}
-// Shared::cluster address of the same shared-memory offset in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t local, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
-  return r;
-}
-// Arrive (release, cluster scope) on an mbarrier given by its shared::cluster address.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-               : "memory");
-}
-// Arrive (default semantics) on an mbarrier of the other CTA of the pair: for signals whose
-// data travels through the tensor-core path (TMEM written and waited for with tcgen05.wait::st
-// and tcgen05.fence::before_thread_sync before the arrive), not through generic memory.
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-__device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
-  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait_acq_cluster(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait (as mbar_wait) with cluster-scope acquire: for phases completed by arrivals of
-// the other CTA of the pair.
-__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, const WaitCtx& w,
-                                                  int site) {
-  if (mbar_try_wait_acq_cluster(bar, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
-  for (uint32_t it = 1; it < (1u << 28); ++it) {
-    if (mbar_try_wait_acq_cluster(bar, parity)) return true;
-    if ((it & 15u) == 0) {
-      if (*reinterpret_cast<volatile int*>(w.abort_flag)) return false;
-      if (global_timer_ns() - t0 > w.timeout_ns) break;
-    }
-  }
-  *reinterpret_cast<volatile int*>(w.abort_flag) = 1;
-  atomicCAS(w.status, 0, kDevTimeout | (site << 8));
-  return false;
-}
-// TMEM allocation for a CTA pair: one warp of each CTA (the same warp index in both) executes
-// these; both get the same column base.
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
-               "r"(ncols)
-               : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish_pair() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
-               : "memory");
-}
-__device__ __forceinline__ void mma_ss_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
-                                            uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void mma_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
-                                            uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// Arrive on the mbarrier at offset `bar` in every CTA of `cta_mask` once all prior pair MMAs
-// of this thread are complete.
-__device__ __forceinline__ void tc_commit_pair(uint32_t bar, uint16_t cta_mask) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-      " [%0], %1;" ::"r"(bar),
-      "h"(cta_mask)
-      : "memory");
-}
-// Tiled 4-D load into this CTA's shared memory whose completion (complete_tx bytes) is counted
-// on an mbarrier that may live in the other CTA of the pair (`bar_cluster`: shared::cluster
-// address).  Plain unicast copy; coordinates as tma_load_4d.
-__device__ __forceinline__ void tma_load_4d_pair(uint32_t dst, const void* map, uint32_t bar_cluster,
-                                                 int c0, int c1, int c2, int c3) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
-      : "memory");
-}
-
 }  // namespace mlxp

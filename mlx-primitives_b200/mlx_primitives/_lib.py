@@ -74,7 +74,6 @@ _SIGNATURES = {
         ctypes.c_int, _i64, _i64, _i64, _i64, _p, ctypes.c_size_t, _p]),
     "mlxp_attn_bwd_workspace_size": (ctypes.c_size_t, [ctypes.c_int, _i64, _i64, _i64, _i64, _i64]),
     "mlxp_set_backward_path": (ctypes.c_int, [ctypes.c_int]),
-    "mlxp_set_forward_kernel": (ctypes.c_int, [ctypes.c_int]),
     "mlxp_paged_attn": (ctypes.c_int, [
         _p, _p, _p, _p, _p, _p, _p, ctypes.c_int, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
         _i64, _i64x4, _i64x4, _i64, _i64x4, ctypes.c_float, ctypes.c_int, _i64, _p,

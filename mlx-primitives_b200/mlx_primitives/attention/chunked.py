@@ -35,7 +35,12 @@ def chunked_cross_attention(
 ) -> torch.Tensor:
     """Cross-attention of q (batch, seq_q, heads, dim) over a long k/v (batch, seq_kv, heads,
     dim).  ``use_metal`` is ignored; ``dropout_p > 0`` with ``training`` raises
-    NotImplementedError."""
+    NotImplementedError.
+
+    ``chunk_size`` is validated (it must be positive, as in the reference) but does not pick
+    the work split: the kernel cuts the key range into as many splits as fill the GPU and
+    merges them by log-sum-exp.  Chunking never changes the mathematical result, so the output
+    equals the reference's for any ``chunk_size`` up to floating-point rounding."""
     if q.ndim != 4:
         raise ValueError(f"Expected 4D tensors (batch, seq, heads, dim), got {q.ndim}D")
     if k.ndim != 4 or v.ndim != 4:
