@@ -41,7 +41,7 @@ def _dims(t: torch.Tensor, layout: str):
 def attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, layout: str,
                       scale: float, causal: bool, window_left: int = -1, window_right: int = -1,
                       q_offset: int = 0, kv_offset: int = 0, kv_splits: int = 0,
-                      return_lse: bool = False):
+                      return_lse: bool = False, out: torch.Tensor | None = None):
     """O = softmax(scale * Q K^T + mask) V for 4-D q/k/v in `layout` ("BSHD" or "BHSD").
 
     Masking is in absolute positions (qpos = i + q_offset, kpos = j + kv_offset): causal keeps
@@ -50,6 +50,9 @@ def attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, layo
     splits (merged by log-sum-exp), 1 = none, n = n.  Returns O with q's layout and dtype and,
     if return_lse, the fp32 log-sum-exp [B, H, Sq].
 
+    ``out`` (optional): a tensor of O's shape, dtype and layout, e.g. a slice of a larger
+    output, that receives the result in place and is returned.
+
     Differentiable: when autograd records and q, k or v requires grad, the backward runs the
     library's backward kernels (mlxp_attn_bwd) from the saved O and log-sum-exp.
     """
@@ -57,12 +60,14 @@ def attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, layo
               window_right=window_right, q_offset=q_offset, kv_offset=kv_offset,
               kv_splits=kv_splits)
     if torch.is_grad_enabled() and any(t.requires_grad for t in (q, k, v)):
+        if out is not None:
+            raise ValueError("out= cannot be used while recording gradients")
         if q.device.type != "cuda":
             raise NotImplementedError("attention gradients need CUDA tensors (host tensors are "
                                       "only staged for the forward)")
         out, lse = _AttentionFn.apply(q, k, v, kw)
         return (out, lse) if return_lse else out
-    return _forward_impl(q, k, v, return_lse=return_lse, **kw)
+    return _forward_impl(q, k, v, return_lse=return_lse, out=out, **kw)
 
 
 class _AttentionFn(torch.autograd.Function):
@@ -127,14 +132,20 @@ def attention_backward(q, k, v, out, lse, dout, *, layout: str, scale: float, ca
 def _forward_impl(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, layout: str,
                   scale: float, causal: bool, window_left: int = -1, window_right: int = -1,
                   q_offset: int = 0, kv_offset: int = 0, kv_splits: int = 0,
-                  return_lse: bool = False):
+                  return_lse: bool = False, out: torch.Tensor | None = None):
+    """The forward launch.  ``out``: a tensor of the output's shape, dtype and layout (any
+    strides, e.g. a slice of a larger output) that receives the result; it is returned."""
     if q.dtype not in _lib.DTYPE_CODES:
         raise ValueError(f"unsupported dtype {q.dtype}; expected float32, bfloat16 or float16")
     if q.device.type == "cpu":
-        return _host_attention(q, k, v, layout=layout, scale=scale, causal=causal,
-                               window_left=window_left, window_right=window_right,
-                               q_offset=q_offset, kv_offset=kv_offset, kv_splits=kv_splits,
-                               return_lse=return_lse)
+        res = _host_attention(q, k, v, layout=layout, scale=scale, causal=causal,
+                              window_left=window_left, window_right=window_right,
+                              q_offset=q_offset, kv_offset=kv_offset, kv_splits=kv_splits,
+                              return_lse=return_lse)
+        if out is None:
+            return res
+        out.copy_(res[0] if return_lse else res)
+        return (out, res[1]) if return_lse else out
     if q.device.type != "cuda":
         raise ValueError(f"tensors must be on a CUDA device (or the host), got {q.device}")
     if k.device != q.device or v.device != q.device:
@@ -153,7 +164,18 @@ def _forward_impl(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, layout: 
     q, k, v = (t if t.stride(-1) == 1 else t.contiguous() for t in (q, k, v))
 
     shape = (B, H, Sq, Dp) if layout == "BHSD" else (B, Sq, H, Dp)
-    out = torch.empty(shape, dtype=q.dtype, device=q.device)
+    dest = None
+    if out is not None:
+        want = (B, H, Sq, D) if layout == "BHSD" else (B, Sq, H, D)
+        if tuple(out.shape) != want or out.dtype != q.dtype or out.device != q.device:
+            raise ValueError(f"out must be a {q.dtype} tensor of shape {want} on {q.device}, got "
+                             f"{out.dtype} {tuple(out.shape)} on {out.device}")
+        dest = out
+        # written in place when the kernel can store into it directly; otherwise (padded
+        # head_dim, strided columns) through a temporary
+        out = out if (Dp == D and out.stride(-1) == 1) else None
+    if out is None:
+        out = torch.empty(shape, dtype=q.dtype, device=q.device)
     lse = torch.empty((B, H, Sq), dtype=torch.float32, device=q.device) if return_lse else None
 
     L = _lib.lib()
@@ -179,6 +201,9 @@ def _forward_impl(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, layout: 
     _lib.check(rc, what)
     if Dp != D:
         out = out[..., :D]
+    if dest is not None and out is not dest:
+        dest.copy_(out)
+        out = dest
     return (out, lse) if return_lse else out
 
 
