@@ -5,8 +5,10 @@
 One step = one forward pass of the configured workload through the public API
 (mlx_primitives.*) on each rank's GPU.  Default workload (config "c2", the one BASELINE's
 metric is quoted on): flash_attention bf16, BHSD, causal, batch 4 x 32 heads x 4096 tokens x
-head_dim 128 per GPU.  Multi-GPU runs (torchrun, one process per GPU) give every rank its own
-(batch, head) units — no collective on the data path — so per-GPU work is fixed ("weak").
+head_dim 128.  Multi-GPU runs (torchrun, one process per GPU) split the fixed workload's
+(batch, head) units across the ranks (mlx_primitives.attention.partition: contiguous unit
+ranges, each rank computes its own in place, no collective on the data path), so the total
+work is fixed ("strong"); config 5 is one 128K-token sequence run as a zig-zag ring.
 
 Printed by rank 0, one JSON line: value = whole-job TFLOPS (algorithmic FLOPs: 4*D per
 admissible (query, key) pair, masked pairs not counted) over the max-over-ranks device time;
@@ -88,6 +90,8 @@ CONFIGS = {
 }
 
 L2_BYTES = 126 * 1024 * 1024
+# configs whose (batch, head) units are split across the GPUs of a multi-GPU run
+SPLIT_APIS = ("flash", "swa", "chunked", "gqa")
 FP32_LANES_PER_SM = 128  # FP32 FMA lanes per SM (4 sub-partitions x 32)
 
 
@@ -260,6 +264,8 @@ def run_reference_arm(args, c, rank):
     """--impl reference: the CPU path (oracle port) on rank 0's host cores."""
     if rank != 0:
         return
+    split = args.gpus > 1 and c["api"] in SPLIT_APIS
+    units_per_gpu = -(-c["B"] * c["H"] // args.gpus) if split else None
     per_step = []
     total_units = 0
     total_flops = 0.0
@@ -279,8 +285,10 @@ def run_reference_arm(args, c, rank):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOPS",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * secs / max(len(per_step), 1), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": config_json(c, args.gpus),
+        "scaling": "strong" if split or c["api"] == "ring" else "weak", "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": config_json(c, args.gpus, units_per_gpu),
         "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": threads, **host_cores(), "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -290,19 +298,24 @@ def run_reference_arm(args, c, rank):
     print(json.dumps(line), flush=True)
 
 
-def config_json(c, n):
+def config_json(c, n, units_per_gpu=None):
     if c["api"] == "ring":
         par = (f"sequence-parallel zig-zag ring over {n} GPUs (NCCL send/recv of K/V, LSE merge)"
                if n > 1 else "single GPU")
         return {"workload": c["workload"], "global_batch": c["B"], "heads": c["H"],
                 "seq_len": c["S"], "head_dim": c["D"], "layout": c["layout"], "causal": True,
                 "parallelism": par, "l2": "inputs larger than L2"}
-    return {"workload": c["workload"], "global_batch": c["B"] * n, "batch_per_gpu": c["B"],
+    split = units_per_gpu is not None
+    per_gpu_bytes = config_bytes(c) * (units_per_gpu / (c["B"] * c["H"]) if split else 1)
+    return {"workload": c["workload"], "global_batch": c["B"] if split else c["B"] * n,
+            "batch_per_gpu": None if split else c["B"],
             "heads": c["H"], "kv_heads": c.get("Hkv", c["H"]), "seq_len": c["S"],
             "kv_len": c["Skv"], "head_dim": c["D"],
             "layout": c["layout"], "causal": c["causal"], "window": c["window"],
-            "parallelism": f"dp{n} over (batch, head) units, no collective",
-            "l2": ("inputs larger than L2" if config_bytes(c) > L2_BYTES
+            "parallelism": (f"the fixed workload's {c['B'] * c['H']} (batch, head) units split "
+                            f"over {n} GPUs (up to {units_per_gpu} per GPU), no collective"
+                            if split else f"dp{n} over (batch, head) units, no collective"),
+            "l2": ("inputs larger than L2" if per_gpu_bytes > L2_BYTES
                    else "L2 flushed between timed iterations")}
 
 
@@ -635,8 +648,11 @@ def main():
     Hkv = c.get("Hkv", H)
     shape_kv = (B, Hkv, Skv, D) if c["layout"] == "BHSD" else (B, Skv, Hkv, D)
     ring = c["api"] == "ring" and world > 1
+    # configs 1-4 and g2 on N > 1 GPUs: the fixed workload's (batch, head) units are split
+    # across the ranks (strong scaling, no collective); every rank builds the same tensors
+    part = world > 1 and c["api"] in SPLIT_APIS
     g = torch.Generator(device=dev)
-    g.manual_seed(42 + (0 if c["api"] == "ring" else rank))  # the ring shares one sequence
+    g.manual_seed(42 + (0 if c["api"] == "ring" or part else rank))
     q = (torch.randn(shape_q, generator=g, device=dev) * c["std"]).to(dtype)
     k = (torch.randn(shape_kv, generator=g, device=dev) * c["std"]).to(dtype)
     v = (torch.randn(shape_kv, generator=g, device=dev) * c["std"]).to(dtype)
@@ -645,7 +661,44 @@ def main():
         q, k, v = (zigzag_shard(t, world, rank).contiguous() for t in (q, k, v))
         torch.cuda.empty_cache()
 
+    def api_call(qq, kk, vv):
+        """The config's public entry point on a whole call (or on one rank's piece)."""
+        if c["api"] in ("flash", "ring"):
+            return mp.flash_attention(qq, kk, vv, causal=c["causal"], layout=c["layout"])
+        if c["api"] == "swa":
+            return mp.sliding_window_attention(qq, kk, vv, window_size=c["window"], causal=c["causal"])
+        if c["api"] == "frope":
+            return mp.kernels.fused_rope_attention(qq, kk, vv, causal=c["causal"])
+        if c["api"] == "gqa":
+            return mp.attention.gqa_attention(qq, kk, vv, num_kv_groups=qq.shape[2] // kk.shape[2],
+                                              causal=c["causal"])
+        return mp.chunked_cross_attention(qq, kk, vv, chunk_size=4096, causal=c["causal"])
+
+    units = range(B * H)
+    if part:
+        from mlx_primitives.attention import partition as P
+        units = P.shard_units(B, H, world, rank)
+        pieces = P.rank_pieces(q, k, v, units, c["layout"])
+        out_full = torch.empty(q.shape, dtype=dtype, device=dev)
+
+        def part_step(qq, kk, vv):
+            """This rank's units of the fixed workload, written in place into out_full."""
+            if c["api"] == "flash":
+                return P.flash_attention_shard(qq, kk, vv, world, rank, causal=c["causal"],
+                                               layout=c["layout"], out=out_full)
+            if c["api"] == "swa":
+                return P.sliding_window_attention_shard(qq, kk, vv, c["window"], world, rank,
+                                                        causal=c["causal"], out=out_full)
+            if c["api"] == "chunked":
+                return P.chunked_cross_attention_shard(qq, kk, vv, world, rank,
+                                                       causal=c["causal"], out=out_full)
+            return P.attention_units(qq, kk, vv, units, layout=c["layout"], scale=D ** -0.5,
+                                     causal=c["causal"], q_offset=Skv - S if c["causal"] else 0,
+                                     out=out_full)
+
     def step(qq, kk, vv):
+        if part:
+            return part_step(qq, kk, vv)
         if ring:
             host = qq.device.type == "cpu"
             if host:
@@ -657,22 +710,16 @@ def main():
                 torch.cuda.current_stream(dev).synchronize()
                 return h
             return o
-        if c["api"] in ("flash", "ring"):
-            return mp.flash_attention(qq, kk, vv, causal=c["causal"], layout=c["layout"])
-        if c["api"] == "swa":
-            return mp.sliding_window_attention(qq, kk, vv, window_size=c["window"], causal=c["causal"])
-        if c["api"] == "frope":
-            return mp.kernels.fused_rope_attention(qq, kk, vv, causal=c["causal"])
-        if c["api"] == "gqa":
-            return mp.attention.gqa_attention(qq, kk, vv, num_kv_groups=H // Hkv,
-                                              causal=c["causal"])
-        return mp.chunked_cross_attention(qq, kk, vv, chunk_size=4096, causal=c["causal"])
+        return api_call(qq, kk, vv)
 
     if ring:  # per step and rank: partials + merges for the pairs below the diagonal, 2 casts
         launches_per_step = 2 * (2 * world) + 2
     else:
         launches_per_step = 2 if c["api"] in ("chunked", "frope") else 1
-    flush = config_bytes(c) <= L2_BYTES
+        if part:
+            launches_per_step *= len(pieces)
+    unit_frac = len(units) / (B * H)  # share of the workload this rank computes
+    flush = config_bytes(c) * unit_frac <= L2_BYTES
     scratch = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev) if flush else None
 
     def barrier():
@@ -705,35 +752,55 @@ def main():
     ms_local = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
     ms = max_over_ranks(ms_local)
 
-    flops = config_flops(c)  # per GPU per step (c5: the whole sequence, shared by the ranks)
+    # this rank's algorithmic FLOPs per step, and the whole job's
+    flops = config_flops(c)
     if c["api"] == "ring":
         flops = flops / world
-    value = world * flops / (ms * 1e-3) / 1e12
+        job_flops = config_flops(c)
+    elif part:
+        flops = flops * unit_frac
+        job_flops = config_flops(c)
+    else:  # every rank runs the whole config (weak scaling)
+        job_flops = world * flops
+    value = job_flops / (ms * 1e-3) / 1e12
     peak, peak_sus, hbm, peak_src = load_peaks()
     achieved = flops / (ms_local * 1e-3) / 1e12  # this rank's work per step / its step time
 
     # ---- e2e: public API with pinned host tensors (H2D and D2H inside the timed region)
     e2e = None
     if args.e2e_steps > 0:
-        hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+        # pinned host inputs: the whole call, or with the split this rank's pieces only (the
+        # shard a data loader would hand the rank), each a public-API call on host tensors
+        if part:
+            host_in = [tuple(t.contiguous().cpu().pin_memory() for t in pc[:3]) for pc in pieces]
+        else:
+            host_in = [tuple(t.cpu().pin_memory() for t in (q, k, v))]
+        call = api_call if part else step
+
+        def e2e_step():
+            return [call(*hin) for hin in host_in]
+
         # warm-up in the timed loop's own pattern (the previous result is still held while
         # the next call runs), so the pinned-memory cache holds both result buffers
         for _ in range(3):
-            out_host = step(hq, hk, hv)
+            out_host = e2e_step()
         torch.cuda.synchronize(dev)
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(args.e2e_steps):
-            out_host = step(hq, hk, hv)
+            out_host = e2e_step()
         e1.record(stream)
         torch.cuda.synchronize(dev)
         barrier()
         e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.e2e_steps)
-        e2e = {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS",
-               "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in (hq, hk, hv)),
-               "d2h_bytes_per_step": out_host.numel() * out_host.element_size(),
+        e2e = {"value": job_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOPS",
+               "h2d_bytes_per_step": sum(t.numel() * t.element_size() for hin in host_in
+                                         for t in hin),
+               "d2h_bytes_per_step": sum(o.numel() * o.element_size() for o in out_host),
                "ms_per_step": e2e_ms}
+        if part:
+            e2e["note"] = "bytes per rank: its own (batch, head) pieces copied in and out"
 
     # config 1 is fp32 on CUDA cores: its roofline is the FP32 pipe, not the tensor cores
     fp32 = c["dtype"] == "fp32"
@@ -748,10 +815,10 @@ def main():
             "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True,
-            "scaling": "strong" if c["api"] == "ring" else "weak", "vs_baseline": None,
+            "scaling": "strong" if c["api"] == "ring" or part else "weak", "vs_baseline": None,
             "dtype": "f32" if c["dtype"] == "fp32" else "bf16",
             "data": "synthetic: seeded N(0, std^2) tensors generated on device (seed 42 + rank)",
-            "config": config_json(c, world),
+            "config": config_json(c, world, len(units) if part else None),
             "tflops_per_gpu": value / world,
             "pct_of_bf16_peak": 100.0 * (value / world) / peak,
             "roofline": {

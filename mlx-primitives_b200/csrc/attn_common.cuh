@@ -144,7 +144,8 @@ struct FwdParams {
   int splits;           // >= 1 key-range splits
   int tiles_per_split;  // key tiles per split (splits > 1)
   int heavy_first;      // order query blocks by descending work (causal)
-  int group_bh;         // (batch, head) units per scheduling group (see decode_item)
+  int n_groups;         // scheduling groups of (batch, head) units, sizes differing by at
+                        // most one unit (see decode_item)
   int kv_group;         // query heads per K/V head (grouped / multi-query attention; 1 = MHA)
   // Output, written through the O tensor map: normal (dtype, normalised) or fp32 (normalised,
   // for merges).  Key split s of batch b is stored at batch coordinate s * o_split_b + b (the
@@ -181,5 +182,50 @@ struct FwdParamsF32 {
   int splits;
   long long o_split, lse_split;
 };
+
+// Work-item order of the persistent tensor-core kernel: item index idx in [0, n_qblk * B * H *
+// splits) -> (batch, head) unit bh, key split and query block qb.
+//   heavy_first (causal): the units are cut into n_groups consecutive groups whose sizes differ
+//   by at most one unit (the first BH % n_groups groups take one more); inside a group the
+//   query blocks go heaviest first across the whole group (longest-processing-time order),
+//   then the next group — a group's K/V stays L2-resident while its items run, and the last
+//   items of the launch are the lightest ones, which keeps the tail short.  Equal groups
+//   matter: a small last group would start its heaviest items only once the previous group had
+//   been handed out, and they would run on alone at the end.
+//   otherwise: every query block costs the same and the query block is the innermost index,
+//   so the items that read the same (unit, key split) K/V run side by side and share it
+//   through L2.
+__host__ __device__ inline void item_coords(const FwdParams& p, int idx, int& bh, int& split,
+                                            int& qb) {
+  const int per_unit = p.n_qblk * p.splits;
+  if (p.heavy_first) {
+    const int BH = p.B * p.H;
+    const int base = BH / p.n_groups, n_big = BH % p.n_groups;
+    const int big_items = (base + 1) * per_unit;  // items of each of the first n_big groups
+    int g0, gsize, local;
+    if (idx < n_big * big_items) {
+      const int grp = idx / big_items;
+      g0 = grp * (base + 1);
+      gsize = base + 1;
+      local = idx - grp * big_items;
+    } else {
+      const int r = idx - n_big * big_items;
+      const int k = r / (base * per_unit);
+      g0 = n_big * (base + 1) + k * base;
+      gsize = base;
+      local = r - k * base * per_unit;
+    }
+    const int qrank = local / (gsize * p.splits);
+    const int rem = local - qrank * gsize * p.splits;
+    bh = g0 + rem / p.splits;
+    split = rem % p.splits;
+    qb = p.n_qblk - 1 - qrank;
+  } else {
+    bh = idx / per_unit;
+    const int rem = idx - bh * per_unit;
+    split = rem / p.n_qblk;
+    qb = rem % p.n_qblk;
+  }
+}
 
 }  // namespace mlxp

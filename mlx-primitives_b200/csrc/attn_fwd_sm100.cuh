@@ -164,34 +164,12 @@ struct WorkItem {
   int lo, hi;              // union range
 };
 
-// Item order.  Causal: (batch, head) units are taken in groups of p.group_bh; inside a group
-// the query blocks go heaviest first across the whole group (longest-processing-time order),
-// then the next group — a group's K/V stays L2-resident while its items run, and the last
-// items of the launch are the lightest ones, which keeps the tail short.  Otherwise every query
-// block costs the same and the query block is the innermost index, so the items that read the
-// same (unit, key split) K/V run side by side and share it through L2.
+// One work item, decoded identically by every role from its index (item_coords in
+// attn_common.cuh gives its unit, key split and query block).
 __device__ __forceinline__ WorkItem decode_item(const FwdParams& p, int idx, int BN) {
   WorkItem w;
   int bh, qb;
-  if (p.heavy_first) {
-    const int BH = p.B * p.H;
-    const int per_unit = p.n_qblk * p.splits;
-    const int grp = idx / (p.group_bh * per_unit);
-    const int g0 = grp * p.group_bh;
-    const int gsize = min(p.group_bh, BH - g0);
-    const int local = idx - g0 * per_unit;
-    const int qrank = local / (gsize * p.splits);
-    const int rem = local - qrank * gsize * p.splits;
-    bh = g0 + rem / p.splits;
-    w.split = rem % p.splits;
-    qb = p.n_qblk - 1 - qrank;
-  } else {
-    const int per_unit = p.n_qblk * p.splits;
-    bh = idx / per_unit;
-    const int rem = idx - bh * per_unit;
-    w.split = rem / p.n_qblk;
-    qb = rem % p.n_qblk;
-  }
+  item_coords(p, idx, bh, w.split, qb);
   w.h = bh % p.H;
   w.b = bh / p.H;
   w.q0 = qb * 256;

@@ -513,13 +513,13 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
   const int kv_tiles = (int)((pr.Skv + kBN - 1) / kBN);
   p.tiles_per_split = (kv_tiles + splits - 1) / splits;
   p.heavy_first = pr.causal ? 1 : 0;
-  // About two waves of items per scheduling group: enough to balance, small enough that the
-  // group's K/V (2 * Skv * D * 2 bytes per unit) stays in L2.
+  // Scheduling groups of at least about two waves of items: enough to balance, small enough
+  // that a group's K/V (2 * Skv * D * 2 bytes per unit) stays in L2.  The units are spread over
+  // floor(units / target) groups of equal size (+-1), so no group is much smaller than that.
   {
     const long long per_unit = (long long)p.n_qblk * splits;
-    long long g = (2LL * sms + per_unit - 1) / per_unit;
-    g = std::max<long long>(1, std::min<long long>(g, pr.B * pr.H));
-    p.group_bh = (int)g;
+    const long long target = (2LL * sms + per_unit - 1) / per_unit;
+    p.n_groups = (int)std::max<long long>(1, (pr.B * pr.H) / std::max<long long>(1, target));
   }
   p.scale_log2 = scale_log2;
   p.mask = mask_of(pr);

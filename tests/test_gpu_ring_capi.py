@@ -1,5 +1,6 @@
 """The C-ABI ring (mlxp_ring_*: NCCL loaded by the library, no torch.distributed) against
-single-GPU flash attention of the whole sequence, bf16 tolerance 2e-2.  One rank runs on one
+single-GPU flash attention of the whole sequence and, for two ranks, against the fp64 oracle on
+every zig-zag chunk boundary, bf16 tolerance 2e-2.  One rank runs on one
 GPU (a ring of one is plain causal attention of the shard, which is then the whole sequence);
 two ranks need two GPUs and are skipped otherwise."""
 
@@ -58,6 +59,8 @@ def _worker(rank, world, uid, shape, errq):
         import mlx_primitives as mp_
         from mlx_primitives.attention.ring import NcclRing, zigzag_shard
 
+        from test_gpu_multi import check_shard_vs_oracle
+
         q, k, v = _inputs(shape, dev, seed=9)
         want = zigzag_shard(mp_.flash_attention(q, k, v, causal=True, layout="BHSD"), world,
                             rank)
@@ -65,6 +68,9 @@ def _worker(rank, world, uid, shape, errq):
         with NcclRing(uid, world, rank) as ring:
             out = ring.forward(shard(q), shard(k), shard(v))
             torch.cuda.synchronize()
+        # the fp64 oracle on every zig-zag chunk boundary of this rank's chunks, all heads
+        check_shard_vs_oracle(out, q, k, v, range(shape[1]), shape[2], world, rank,
+                              shape[3] ** -0.5)
         err = (out.float() - want.float()).abs().max().item()
         if not err <= 2e-2:
             raise AssertionError(f"rank {rank}: max-abs {err}")
