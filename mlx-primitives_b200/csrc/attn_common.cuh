@@ -148,12 +148,21 @@ struct FwdParams {
                         // most one unit (see decode_item)
   int kv_group;         // query heads per K/V head (grouped / multi-query attention; 1 = MHA)
   // Output, written through the O tensor map: normal (dtype, normalised) or fp32 (normalised,
-  // for merges).  Key split s of batch b is stored at batch coordinate s * o_split_b + b (the
-  // split workspace is [split][B][H][Sq][D], i.e. o_split_b = B; 0 without splits).
+  // for callers that merge partial results themselves; no key splits then).
   int out_f32;
-  int o_split_b;
-  float* lse;                           // [split][B][H][Sq] contiguous, nullable unless out_f32
-  long long lse_split;
+  float* lse;                           // [B][H][Sq] contiguous, nullable unless out_f32
+  // Key splits (splits > 1) are merged inside the kernel.  The query tiles (128 rows) that
+  // more than one split touches get a partial per split: the normalised fp32 O of the split
+  // at part_o + slot * 128 * D, laid out [D/4][128 rows][4] so that the 32 rows of a warp
+  // store and load 512 contiguous bytes, and its natural-log LSE at part_lse + slot * 128,
+  // slot = ((unit * n_qtile) + query tile) * splits + split.  Each split adds one to the query
+  // tile's counter (tile_cnt[unit * n_qtile + query tile], zero at launch) after its partial is
+  // visible, and the split that completes the count merges every partial and writes O.
+  float* part_o;
+  float* part_lse;
+  unsigned* tile_cnt;
+  long long part_tiles; // query tiles the workspace has room for (checked before every use)
+  int n_qtile;          // query tiles of 128 rows per unit
   float scale_log2;     // softmax scale * log2(e)
   MaskSpec mask;
   TmaCoordMap cq, ck, cv, co;

@@ -50,6 +50,7 @@ namespace mlxp {
 #if MLXP_TRACE
 __device__ long long g_mlxp_trace[4 * 64 * 8];
 __device__ long long g_mlxp_cta_trace[8192 * 4];  // per item: start ns, end ns, SM id, key tiles
+__device__ long long g_mlxp_cta_life[1024 * 3];   // per CTA: entry ns, prologue done ns, exit ns
 #define MLXP_TR(cond, role, it, k)                                                    \
   do {                                                                                \
     if ((cond) && blockIdx.x == 0 && (it) < 64)                                       \
@@ -94,8 +95,9 @@ struct Sm100Cfg {
   static constexpr int B_WE = B_WF + 2;    // 2: work-item slot read by every consumer
   static constexpr int B_DR = B_WE + 2;    // 1: MMA drain
   static constexpr int NBAR = B_DR + 1;
-  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;  // tmem slot, abort flag, 2 item slots
-  static constexpr int SMEM_BYTES = OFF_MISC + 16;
+  // tmem slot, abort flag, 2 item slots, 2 per-tile "merge the key splits" flags
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int SMEM_BYTES = OFF_MISC + 24;
   static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024 B
   // Three warpgroups: WG0/WG1 softmax (tiles 0/1), WG2 = MMA warp, TMA warp, two spare warps.
   // Registers are split per SM sub-partition, so the launch gets 65536/384 -> 168 per thread
@@ -121,7 +123,8 @@ enum : int {
   kSiteSoftmaxO = 5,
   kSiteDrain = 6,
   kSiteSelfTest = 7,
-  kSiteWork = 8
+  kSiteWork = 8,
+  kSiteEpilogue = 10
 };
 
 // Of every 8 column pairs of a score row, this many are exponentiated with exp2_poly2 (FMA pipe)
@@ -210,11 +213,15 @@ __global__ void __launch_bounds__(384, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   int* abort_flag = reinterpret_cast<int*>(smem + C::OFF_MISC + 4);
   volatile int* work_slot = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8);
+  volatile int* merge_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 16);
   auto BAR = [&](int i) -> uint32_t { return sbase + C::OFF_BAR + 8 * i; };
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int n_items = p.n_qblk * p.B * p.H * p.splits;
+#if MLXP_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 1024) g_mlxp_cta_life[blockIdx.x * 3] = (long long)global_timer_ns();
+#endif
 
   if (threadIdx.x == 0) {
     mbar_init(BAR(C::B_QF), 1);
@@ -244,6 +251,9 @@ __global__ void __launch_bounds__(384, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const WaitCtx wctx{abort_flag, p.status, p.timeout_ns};
+#if MLXP_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 1024) g_mlxp_cta_life[blockIdx.x * 3 + 1] = (long long)global_timer_ns();
+#endif
 
   if (warp >= 8) {
     // ================================ control warpgroup ================================
@@ -265,7 +275,10 @@ __global__ void __launch_bounds__(384, 1)
             ok = mbar_wait(BAR(C::B_WE + slot), ((item >> 1) - 1) & 1, wctx, kSiteWork);
             if (!ok) break;
           }
-          const int idx = (int)atomicAdd(p.work_counter, 1u);
+          // the first item of every CTA is its block index (no atomic on the launch's
+          // critical path); later ones come from the counter, past the first gridDim.x
+          const int idx = item == 0 ? (int)blockIdx.x
+                                    : (int)(gridDim.x + atomicAdd(p.work_counter, 1u));
           work_slot[slot] = idx;
           MLXP_TR(true, 3, item, 1);
           mbar_arrive(BAR(C::B_WF + slot));  // release: the slot write is visible to waiters
@@ -641,6 +654,19 @@ __global__ void __launch_bounds__(384, 1)
       // ------------------------------------ epilogue ------------------------------------
       const bool has_rows = qrow < p.Sq;
       const int n_it = thi - tlo;
+      // Key splits: the splits whose key tiles reach this query tile are [s_first, s_first +
+      // nparts).  With one of them (or none: split 0 then writes the empty rows) the item
+      // writes O directly; with more, each writes its partial and the one that completes the
+      // tile's count merges them all.  A split that does not reach the tile writes nothing.
+      // (Every quantity here is the same for the 128 threads of the tile.)
+      int nparts = 1, s_first = 0;
+      if (p.splits > 1) {
+        int ulo = 0, uhi = 0;
+        if (r1 > r0) kv_tile_range(p.mask, r0, r1, C::BN, ulo, uhi);
+        s_first = ulo / p.tiles_per_split;
+        nparts = (uhi > ulo) ? (uhi - 1) / p.tiles_per_split - s_first + 1 : 0;
+        if (nparts == 0 ? w.split != 0 : n_it == 0) continue;
+      }
       if (n_it > 0) {
         ok = mbar_wait(BAR(C::B_OF + t), n_o & 1, wctx, kSiteSoftmaxO);
         ok = named_bar_and(1 + t, 128, ok);
@@ -654,32 +680,103 @@ __global__ void __launch_bounds__(384, 1)
       const bool valid = n_it > 0 && l > 0.f && m != -INFINITY;
       const float inv_l = valid ? 1.0f / l : 0.f;
       const float lse_v = valid ? (m + log2f(l)) * 0.69314718055994531f : -INFINITY;
+      const bool elected = (wq == 0 && lane == 0);
+      const long long tile_id = (long long)(w.b * p.H + w.h) * p.n_qtile + (w.q0 >> 7) + t;
+      bool merge = false;
+      if (nparts >= 2 && tile_id >= p.part_tiles) {
+        // the workspace does not cover this tile (a host-side sizing error): report, write nothing
+        if (elected) atomicCAS(p.status, 0, kDevWorkspace | (kSiteEpilogue << 8));
+        continue;
+      }
+      if (nparts >= 2) {
+        // this split's partial: normalised O and LSE, rows interleaved by 16-byte chunks
+        float* po = p.part_o + (tile_id * p.splits + w.split) * (128LL * D) + row * 4;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t ov[32];
+          tmem_ld_x32(tO + c * 32, ov);
+          tmem_wait_ld();
+          reg_fence(ov);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            *reinterpret_cast<float4*>(po + (c * 8 + i) * 128 * 4) = make_float4(
+                __uint_as_float(ov[4 * i]) * inv_l, __uint_as_float(ov[4 * i + 1]) * inv_l,
+                __uint_as_float(ov[4 * i + 2]) * inv_l, __uint_as_float(ov[4 * i + 3]) * inv_l);
+        }
+        p.part_lse[(tile_id * p.splits + w.split) * 128 + row] = lse_v;
+        // publish: every thread's stores reach the device scope before the count moves
+        __threadfence();
+        named_bar_sync(1 + t, 128);
+        if (elected) {
+          const unsigned prev = atomicAdd(p.tile_cnt + tile_id, 1u);
+          const int last = prev == (unsigned)(nparts - 1);
+          if (last) {
+            p.tile_cnt[tile_id] = 0u;  // every split of the tile has counted: ready for reuse
+            __threadfence();
+          }
+          merge_flag[t] = last;
+        }
+        named_bar_sync(1 + t, 128);
+        merge = merge_flag[t] != 0;
+        if (!merge) continue;
+      }
+      // The merge: w_s = exp(lse_s - max lse) / sum of them; O = sum_s w_s O_s; LSE = max +
+      // log(sum).  Partials are read through L2 (ld.global.cg): other SMs wrote them.
+      const float* pl = p.part_lse + (tile_id * p.splits + s_first) * 128 + row;
+      const float* pb = p.part_o + (tile_id * p.splits + s_first) * (128LL * D) + row * 4;
+      float m_tot = -INFINITY, inv_w = 0.f, lse_out = lse_v;
+      if (merge) {
+        for (int s = 0; s < nparts; ++s) m_tot = fmaxf(m_tot, __ldcg(pl + s * 128));
+        float wsum = 0.f;
+        if (m_tot != -INFINITY)
+          for (int s = 0; s < nparts; ++s) wsum += expf(__ldcg(pl + s * 128) - m_tot);
+        inv_w = wsum > 0.f ? 1.0f / wsum : 0.f;
+        lse_out = wsum > 0.f ? m_tot + logf(wsum) : -INFINITY;
+      }
       if (has_rows && p.lse != nullptr)
-        p.lse[(long long)w.split * p.lse_split + ((long long)w.b * p.H + w.h) * p.Sq + qrow] =
-            lse_v;
+        p.lse[((long long)w.b * p.H + w.h) * p.Sq + qrow] = lse_out;
       // O leaves through the tile's staging box: each thread writes its row (128-byte swizzle:
       // 16-byte chunk k of row r at chunk k ^ (r % 8), which spreads a warp's writes over all
       // banks), then one thread stores the box with TMA, which writes whole lines of O (rows
       // past Sq are clipped by the tensor map).  A box is 64 bf16/fp16 or 32 fp32 columns, so
-      // one 32-column TMEM chunk fills half a box (bf16/fp16) or a whole one (fp32).
+      // one 32-column chunk of O fills half a box (bf16/fp16) or a whole one (fp32).
       {
         const uint32_t stage = sbase + C::OFF_STAGE + t * C::STAGE_BYTES;
         const uint32_t row_base = stage + (uint32_t)row * 128u;
         const uint32_t sw = (uint32_t)(row & 7);
-        const bool elected = (wq == 0 && lane == 0);
         const bool f32 = p.out_f32 != 0;
         int c1, c2, c3;
-        tma_coords(p.co, w.q0 + t * 128, w.h, w.split * p.o_split_b + w.b, c1, c2, c3);
+        tma_coords(p.co, w.q0 + t * 128, w.h, w.b, c1, c2, c3);
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
-          uint32_t ov[32];
-          if (n_it > 0) {
-            tmem_ld_x32(tO + c * 32, ov);
+          float ov[32];
+          if (merge) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ov[i] = 0.f;
+#pragma unroll 1
+            for (int s = 0; s < nparts; ++s) {
+              const float ls = __ldcg(pl + s * 128);
+              const float ws = (ls == -INFINITY) ? 0.f : expf(ls - m_tot) * inv_w;
+              const float* ps = pb + s * (128LL * D) + c * 8 * 128 * 4;
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float4 v4 = __ldcg(reinterpret_cast<const float4*>(ps + i * 128 * 4));
+                ov[4 * i] += ws * v4.x;
+                ov[4 * i + 1] += ws * v4.y;
+                ov[4 * i + 2] += ws * v4.z;
+                ov[4 * i + 3] += ws * v4.w;
+              }
+            }
+          } else if (n_it > 0) {
+            uint32_t ou[32];
+            tmem_ld_x32(tO + c * 32, ou);
             tmem_wait_ld();
-            reg_fence(ov);
+            reg_fence(ou);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ov[i] = __uint_as_float(ou[i]) * inv_l;
           } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) ov[i] = 0u;
+            for (int i = 0; i < 32; ++i) ov[i] = 0.f;
           }
           if (f32 || !(c & 1)) {
             // the previous store from this box has finished reading it
@@ -689,24 +786,17 @@ __global__ void __launch_bounds__(384, 1)
           if (f32) {
 #pragma unroll
             for (int i = 0; i < 8; ++i)
-              st_shared_v4(row_base + ((((uint32_t)i) ^ sw) << 4),
-                           __float_as_uint(__uint_as_float(ov[4 * i]) * inv_l),
-                           __float_as_uint(__uint_as_float(ov[4 * i + 1]) * inv_l),
-                           __float_as_uint(__uint_as_float(ov[4 * i + 2]) * inv_l),
-                           __float_as_uint(__uint_as_float(ov[4 * i + 3]) * inv_l));
+              st_shared_v4(row_base + ((((uint32_t)i) ^ sw) << 4), __float_as_uint(ov[4 * i]),
+                           __float_as_uint(ov[4 * i + 1]), __float_as_uint(ov[4 * i + 2]),
+                           __float_as_uint(ov[4 * i + 3]));
           } else {
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const uint32_t k = (uint32_t)((c & 1) * 4 + i);
-              st_shared_v4(row_base + ((k ^ sw) << 4),
-                           pack2<kBF16>(__uint_as_float(ov[8 * i + 0]) * inv_l,
-                                        __uint_as_float(ov[8 * i + 1]) * inv_l),
-                           pack2<kBF16>(__uint_as_float(ov[8 * i + 2]) * inv_l,
-                                        __uint_as_float(ov[8 * i + 3]) * inv_l),
-                           pack2<kBF16>(__uint_as_float(ov[8 * i + 4]) * inv_l,
-                                        __uint_as_float(ov[8 * i + 5]) * inv_l),
-                           pack2<kBF16>(__uint_as_float(ov[8 * i + 6]) * inv_l,
-                                        __uint_as_float(ov[8 * i + 7]) * inv_l));
+              st_shared_v4(row_base + ((k ^ sw) << 4), pack2<kBF16>(ov[8 * i + 0], ov[8 * i + 1]),
+                           pack2<kBF16>(ov[8 * i + 2], ov[8 * i + 3]),
+                           pack2<kBF16>(ov[8 * i + 4], ov[8 * i + 5]),
+                           pack2<kBF16>(ov[8 * i + 6], ov[8 * i + 7]));
             }
           }
           if (f32 || (c & 1)) {
@@ -729,6 +819,9 @@ __global__ void __launch_bounds__(384, 1)
     if (wq == 0 && lane == 0) bulk_wait_group0();
     tc_fence_before();
     __syncthreads();  // teardown barrier (pairs with the control warpgroup's)
+#if MLXP_TRACE
+    if (threadIdx.x == 0 && blockIdx.x < 1024) g_mlxp_cta_life[blockIdx.x * 3 + 2] = (long long)global_timer_ns();
+#endif
     // The last CTA to finish resets the launch's work counter for the next launch.
     if (threadIdx.x == 0) {
       __threadfence();

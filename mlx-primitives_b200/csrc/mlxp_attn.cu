@@ -14,7 +14,9 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <queue>
 #include <string>
+#include <vector>
 
 #include "../../include/mlxp_attn.h"
 #include "attn_common.cuh"
@@ -241,24 +243,146 @@ int validate(const Problem& pr) {
 constexpr int kBM2 = 256;  // query rows per tensor-core CTA
 constexpr int kBN = 128;   // keys per tensor-core tile
 
-// Key-range split count for non-causal, unwindowed problems (the only ones with long uniform
-// key ranges).  The persistent kernel schedules items dynamically, so splits serve two ends:
-// enough items to fill every SM several times, and items short enough (<= 128 key tiles) that
-// the end-of-launch tail stays small; each split costs one fp32 partial write and read in
-// the LSE merge, so no more splits than that.  (A 64-tile cap measured 5-19 % slower: config 4
-// 645 against 678 TFLOPS with 8 instead of 4 splits, 16K x 16K head_dim 128 957 against 1142
-// with 2 instead of 1, 4K x 64K 966 against 1031 with 8 instead of 4.)
+// Scheduling groups of the persistent kernel (FwdParams::n_groups): groups of at least about
+// two waves of items — enough to balance, small enough that a group's K/V (2 * Skv * D * 2
+// bytes per unit) stays in L2 — spread evenly: floor(units / target) groups of equal size (+-1),
+// so that no group is much smaller than the target.
+int sched_groups(long long units, long long per_unit, int sms) {
+  const long long target = std::max<long long>(1, (2LL * sms + per_unit - 1) / per_unit);
+  return (int)std::max<long long>(1, units / target);
+}
+
+// Key-range split count, uniform rule for long unmasked key ranges: enough items to fill every
+// SM several times, and items short enough (<= 128 key tiles) that the end-of-launch tail stays
+// small; each split costs one fp32 partial write and read, so no more splits than that.  (A
+// 64-tile cap measured 5-19 % slower: config 4 645 against 678 TFLOPS with 8 instead of 4
+// splits, 16K x 16K head_dim 128 957 against 1142 with 2 instead of 1, 4K x 64K 966 against 1031
+// with 8 instead of 4.)
 constexpr int kMaxTilesPerSplit = 128;
-int choose_splits(const Problem& pr, int sms) {
+int uniform_splits(const Problem& pr, int sms) {
   const long long n_qblk = (pr.Sq + kBM2 - 1) / kBM2;
   const long long base = n_qblk * pr.B * pr.H;
   const long long kv_tiles = (pr.Skv + kBN - 1) / kBN;
-  if (base <= 0 || kv_tiles < 16 || pr.causal || pr.wl >= 0 || pr.wr >= 0) return 1;
+  if (base <= 0 || kv_tiles < 16) return 1;
   int s = 1;
   while (s < 32 && ((kv_tiles + s - 1) / s > kMaxTilesPerSplit || base * s < 4LL * sms) &&
          kv_tiles / (2 * s) >= 8)
     s *= 2;
   return s;
+}
+
+// Modelled duration (in key-tile steps) of one launch with `splits` key splits: the items in
+// the kernel's own order (item_coords) handed to the earliest free SM, each costing its key
+// tiles + a per-item overhead (~2 steps: Q load, first and last steps without the other tile,
+// epilogue; measured by tracing item start/end times), + for every query tile split into
+// several parts the partial written to and read back from L2 (128 rows x head_dim fp32 each).
+double model_launch_steps(const Problem& pr, int splits, int sms) {
+  constexpr double kItemOverhead = 2.0;
+  const double part_cost = pr.D >= 128 ? 0.35 : 0.18;
+  FwdParams p{};
+  p.B = (int)pr.B;
+  p.H = (int)pr.H;
+  p.Sq = (int)pr.Sq;
+  p.Skv = (int)pr.Skv;
+  p.n_qblk = (int)((pr.Sq + kBM2 - 1) / kBM2);
+  p.splits = splits;
+  const int kv_tiles = (int)((pr.Skv + kBN - 1) / kBN);
+  p.tiles_per_split = (kv_tiles + splits - 1) / splits;
+  p.heavy_first = pr.causal ? 1 : 0;
+  p.n_groups = sched_groups(pr.B * pr.H, (long long)p.n_qblk * splits, sms);
+  const MaskSpec m = mask_of(pr);
+  // every unit has the same items: cost per (query block, split), computed once
+  std::vector<double> cost((size_t)p.n_qblk * splits, 0.0);
+  for (int qb = 0; qb < p.n_qblk; ++qb) {
+    int ulo[2], uhi[2], nparts[2];
+    for (int t = 0; t < 2; ++t) {
+      const long long r0 = (long long)qb * 256 + t * 128;
+      const long long r1 = std::min<long long>(r0 + 128, pr.Sq);
+      kv_tile_range(m, r0, r1, kBN, ulo[t], uhi[t]);
+      nparts[t] = uhi[t] > ulo[t] ? (uhi[t] - 1) / p.tiles_per_split - ulo[t] / p.tiles_per_split + 1 : 0;
+    }
+    for (int sp = 0; sp < splits; ++sp) {
+      const int s_lo = sp * p.tiles_per_split, s_hi = s_lo + p.tiles_per_split;
+      int lo = 1 << 30, hi = -1;
+      double extra = 0.0;
+      for (int t = 0; t < 2; ++t) {
+        const int a = std::max(ulo[t], s_lo), b = std::min(uhi[t], s_hi);
+        if (b <= a) continue;
+        lo = std::min(lo, a);
+        hi = std::max(hi, b);
+        if (nparts[t] >= 2)  // write the partial; the last part (modelled: the final split) merges
+          extra += part_cost * (1.0 + (sp == (uhi[t] - 1) / p.tiles_per_split ? nparts[t] : 0));
+      }
+      if (hi > lo) cost[(size_t)qb * splits + sp] = (hi - lo) + kItemOverhead + extra;
+    }
+  }
+  const long long n_items = (long long)p.n_qblk * pr.B * pr.H * splits;
+  std::priority_queue<double, std::vector<double>, std::greater<double>> free_at;
+  for (int i = 0; i < sms; ++i) free_at.push(0.0);
+  double makespan = 0.0;
+  for (long long idx = 0; idx < n_items; ++idx) {
+    int bh, sp, qb;
+    item_coords(p, (int)idx, bh, sp, qb);
+    const double c = cost[(size_t)qb * splits + sp];
+    if (c <= 0.0) continue;
+    const double t = free_at.top() + c;
+    free_at.pop();
+    free_at.push(t);
+    makespan = std::max(makespan, t);
+  }
+  return makespan;
+}
+
+// Key-range split count of the tensor-core kernel.  Long unmasked key ranges over many items
+// use the uniform rule.  Otherwise (causal or windowed masks, or few items per SM) the launch
+// is modelled for no split and for splits of 128 down to 8 key tiles, and the count with the
+// shortest modelled launch is taken (a split must save 3 %): with few (batch, head) units per
+// GPU — e.g. one GPU's share of a call split across GPUs — the heaviest causal query blocks or
+// the last wave of window items would otherwise run on alone at the end of the launch.
+// Decisions are cached per shape and SM count.
+int choose_splits(const Problem& pr, int sms) {
+  const long long n_qblk = (pr.Sq + kBM2 - 1) / kBM2;
+  const long long units = pr.B * pr.H;
+  const int kv_tiles = (int)((pr.Skv + kBN - 1) / kBN);
+  const bool masked = pr.causal || pr.wl >= 0 || pr.wr >= 0;
+  const int uniform = masked ? 1 : uniform_splits(pr, sms);
+  const long long items = n_qblk * units;
+  // many items per SM and short items: the dispatch order already balances the launch
+  if (items <= 0 || kv_tiles < 4 || items >= 16LL * sms || items * 64 > (1LL << 24))
+    return uniform;
+  struct Key {
+    long long units, Sq, Skv, wl, wr, qoff, kvoff;
+    int causal, D, sms;
+    bool operator==(const Key& o) const {
+      return units == o.units && Sq == o.Sq && Skv == o.Skv && wl == o.wl && wr == o.wr &&
+             qoff == o.qoff && kvoff == o.kvoff && causal == o.causal && D == o.D && sms == o.sms;
+    }
+  };
+  static std::mutex mu;
+  static std::vector<std::pair<Key, int>> cache;
+  const Key key{units, pr.Sq, pr.Skv, pr.wl, pr.wr, pr.qoff, pr.kvoff, pr.causal, (int)pr.D, sms};
+  {
+    std::lock_guard<std::mutex> g(mu);
+    for (const auto& e : cache)
+      if (e.first == key) return e.second;
+  }
+  int best = uniform;
+  double best_t = model_launch_steps(pr, uniform, sms);
+  const double base_t = best_t;
+  for (int T : {128, 96, 64, 48, 32, 24, 16, 12, 8}) {
+    if (T >= kv_tiles) continue;
+    const int sp = std::min(32, (kv_tiles + T - 1) / T);
+    if (sp == best || sp <= 1) continue;
+    const double t = model_launch_steps(pr, sp, sms);
+    if (t < best_t && t < 0.97 * base_t) {
+      best_t = t;
+      best = sp;
+    }
+  }
+  std::lock_guard<std::mutex> g(mu);
+  if (cache.size() >= 256) cache.erase(cache.begin());
+  cache.emplace_back(key, best);
+  return best;
 }
 
 // Key splits of the fp32 kernel: its CTAs (64 query rows) are all resident at once for small
@@ -274,11 +398,36 @@ int choose_splits_f32(const Problem& pr, int sms) {
   return s;
 }
 
-size_t split_workspace(const Problem& pr, int splits) {
+// Workspace of the fp32 kernel's key splits: fp32 partials [split][B][H][Sq][D], then their
+// LSEs [split][B][H][Sq] (merged by lse_merge_kernel).
+size_t split_workspace_f32(const Problem& pr, int splits) {
   if (splits <= 1) return 0;
   const size_t rows = (size_t)splits * pr.B * pr.H * pr.Sq;
   const size_t o_bytes = ((rows * pr.D * 4) + 255) / 256 * 256;
   return o_bytes + rows * 4;
+}
+
+// Workspace of the tensor-core kernel's key splits (merged inside the kernel): one counter per
+// query tile of 128 rows, then per (query tile, split) the partial's 128 LSEs and its 128 x D
+// normalised fp32 outputs (FwdParams::part_o / part_lse / tile_cnt).
+struct TcSplitLayout {
+  size_t tiles, cnt_bytes, lse_bytes, o_bytes;
+  size_t total() const { return cnt_bytes + lse_bytes + o_bytes; }
+};
+TcSplitLayout tc_split_layout(const Problem& pr, int splits) {
+  TcSplitLayout l{0, 0, 0, 0};
+  if (splits <= 1) return l;
+  // query tiles as the kernel numbers them: two per 256-row query block (FwdParams::n_qtile)
+  const size_t tiles = (size_t)pr.B * pr.H * 2 * ((pr.Sq + kBM2 - 1) / kBM2);
+  l.tiles = tiles;
+  l.cnt_bytes = (tiles * 4 + 255) / 256 * 256;
+  l.lse_bytes = tiles * splits * 128 * 4;
+  l.o_bytes = tiles * splits * 128 * pr.D * 4;
+  return l;
+}
+size_t split_workspace(const Problem& pr, int splits) {
+  return pr.dtype == MLXP_DTYPE_FP32 ? split_workspace_f32(pr, splits)
+                                     : tc_split_layout(pr, splits).total();
 }
 
 // Scratch of mlxp_attn_fwd_split_noalloc: a fixed array in the library's device image, so the
@@ -509,18 +658,12 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
   p.Sq = (int)pr.Sq;
   p.Skv = (int)pr.Skv;
   p.n_qblk = (int)((pr.Sq + kBM2 - 1) / kBM2);
+  p.n_qtile = 2 * p.n_qblk;
   p.splits = splits;
   const int kv_tiles = (int)((pr.Skv + kBN - 1) / kBN);
   p.tiles_per_split = (kv_tiles + splits - 1) / splits;
   p.heavy_first = pr.causal ? 1 : 0;
-  // Scheduling groups of at least about two waves of items: enough to balance, small enough
-  // that a group's K/V (2 * Skv * D * 2 bytes per unit) stays in L2.  The units are spread over
-  // floor(units / target) groups of equal size (+-1), so no group is much smaller than that.
-  {
-    const long long per_unit = (long long)p.n_qblk * splits;
-    const long long target = (2LL * sms + per_unit - 1) / per_unit;
-    p.n_groups = (int)std::max<long long>(1, (pr.B * pr.H) / std::max<long long>(1, target));
-  }
+  p.n_groups = sched_groups(pr.B * pr.H, (long long)p.n_qblk * splits, sms);
   p.scale_log2 = scale_log2;
   p.mask = mask_of(pr);
   p.status = status;
@@ -535,40 +678,31 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
   // O is written through a tensor map: 128-row boxes of 128 bytes (64 bf16/fp16 or 32 fp32
   // columns).  The output was validated above (16-byte aligned base, 16-byte strides).
   CUtensorMap mo;
-  if (splits == 1) {
-    p.out_f32 = out_f32 ? 1 : 0;
-    p.o_split_b = 0;
-    p.lse = lse;
-    p.lse_split = 0;
-    if (int rc = out_f32 ? make_tmap(o, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, pr.B, pr.H, pr.Sq,
-                                     pr.D, os, 128, 32, "o", &mo, &p.co)
-                         : make_tmap(o, dt16, 2, pr.B, pr.H, pr.Sq, pr.D, os, 128, 64, "o", &mo,
-                                     &p.co))
-      return rc;
-    return launch_tc((int)pr.D, bf16, mq, mk, mv, mo, p, stream);
+  p.out_f32 = out_f32 ? 1 : 0;
+  p.lse = lse;
+  if (int rc = out_f32 ? make_tmap(o, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, pr.B, pr.H, pr.Sq, pr.D,
+                                   os, 128, 32, "o", &mo, &p.co)
+                       : make_tmap(o, dt16, 2, pr.B, pr.H, pr.Sq, pr.D, os, 128, 64, "o", &mo,
+                                   &p.co))
+    return rc;
+  if (splits > 1) {
+    // key splits are merged inside the kernel; the workspace holds the partials and the
+    // per-query-tile counters, which must start at zero
+    const TcSplitLayout lay = tc_split_layout(pr, splits);
+    if (ws == nullptr || ws_bytes < lay.total())
+      return fail(MLXP_ERR_WORKSPACE, "workspace of %zu bytes needed for %d key splits, got %zu",
+                  lay.total(), splits, ws_bytes);
+    if (reinterpret_cast<uintptr_t>(ws) % 256)
+      return fail(MLXP_ERR_INVALID, "workspace must be 256-byte aligned");
+    char* base = static_cast<char*>(ws);
+    p.tile_cnt = reinterpret_cast<unsigned*>(base);
+    p.part_lse = reinterpret_cast<float*>(base + lay.cnt_bytes);
+    p.part_o = reinterpret_cast<float*>(base + lay.cnt_bytes + lay.lse_bytes);
+    p.part_tiles = (long long)lay.tiles;
+    cudaError_t e = cudaMemsetAsync(base, 0, lay.cnt_bytes, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(split counters)");
   }
-  const size_t need = split_workspace(pr, splits);
-  if (ws == nullptr || ws_bytes < need)
-    return fail(MLXP_ERR_WORKSPACE, "workspace of %zu bytes needed for %d key splits, got %zu",
-                need, splits, ws_bytes);
-  if (reinterpret_cast<uintptr_t>(ws) % 256)
-    return fail(MLXP_ERR_INVALID, "workspace must be 256-byte aligned");
-  const long long rows = pr.B * pr.H * pr.Sq;
-  float* o_parts = static_cast<float*>(ws);
-  float* lse_parts = reinterpret_cast<float*>(static_cast<char*>(ws) +
-                                              ((size_t)splits * rows * pr.D * 4 + 255) / 256 * 256);
-  p.out_f32 = 1;
-  p.o_split_b = (int)pr.B;  // [split][B][H][Sq][D]: split s of batch b is batch s * B + b
-  p.lse = lse_parts;
-  p.lse_split = rows;
-  {
-    const int64_t ws_st[4] = {pr.H * pr.Sq * pr.D, pr.Sq * pr.D, pr.D, 1};
-    if (int rc = make_tmap(o_parts, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (int64_t)splits * pr.B,
-                           pr.H, pr.Sq, pr.D, ws_st, 128, 32, "split workspace", &mo, &p.co))
-      return rc;
-  }
-  if (int rc = launch_tc((int)pr.D, bf16, mq, mk, mv, mo, p, stream)) return rc;
-  return merge_dispatch(o_parts, lse_parts, splits, o, lse, pr, os, stream);
+  return launch_tc((int)pr.D, bf16, mq, mk, mv, mo, p, stream);
 }
 
 // RoPE of one or two tensors ([B][H][S][D] in element strides) in one launch.
@@ -1362,6 +1496,17 @@ int mlxp_trace_read(long long* dst, int n) {
   const int cap = 4 * 64 * 8;
   cudaError_t e = cudaMemcpyFromSymbol(dst, g_mlxp_trace, sizeof(long long) * (n < cap ? n : cap));
   return e == cudaSuccess ? MLXP_OK : cuda_fail(e, "trace read");
+}
+// Trace builds only: the split model's launch estimate (key-tile steps) for a shape.
+double mlxp_model_steps(int64_t B, int64_t H, int64_t Sq, int64_t Skv, int64_t D, int causal,
+                        int64_t wl, int64_t wr, int64_t qoff, int splits, int sms) {
+  Problem pr{MLXP_DTYPE_BF16, B, H, Sq, Skv, D, causal, wl, wr, qoff, 0};
+  return model_launch_steps(pr, splits, sms);
+}
+int mlxp_cta_life_read(long long* dst, int n) {
+  const int cap = 1024 * 3;
+  cudaError_t e = cudaMemcpyFromSymbol(dst, g_mlxp_cta_life, sizeof(long long) * (n < cap ? n : cap));
+  return e == cudaSuccess ? MLXP_OK : cuda_fail(e, "cta life read");
 }
 int mlxp_cta_trace_read(long long* dst, int n) {
   const int cap = 8192 * 4;

@@ -14,6 +14,7 @@ namespace mlxp {
 
 // Device status word values (low byte = code, next byte = wait site).
 constexpr int kDevTimeout = 5;
+constexpr int kDevWorkspace = 6;  // a kernel found its workspace too small (nothing written)
 
 struct WaitCtx {
   int* abort_flag;       // shared memory, CTA-local
