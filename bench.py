@@ -748,6 +748,21 @@ def main():
     for i in range(max(args.warmup, rot)):
         step(*inputs[i % rot])
     stream = torch.cuda.current_stream(dev)
+    # The timed steps replay a CUDA graph of the same public-API call (one graph per input
+    # copy): the device runs exactly the eager step's kernels, without the Python call path in
+    # between (at 8 GPUs one rank's step is ~80 us, about the host time of an eager call).
+    # The ring's steps are NCCL-bound and long; they run eagerly.
+    graphs = None
+    if not ring:
+        torch.cuda.synchronize(dev)
+        graphs = []
+        for i in range(rot):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                step(*inputs[i])
+            graphs.append(gr)
+        for i in range(rot):
+            graphs[i].replay()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     barrier()
@@ -755,7 +770,10 @@ def main():
     with ClockSampler(local) as clocks:
         for i in range(args.steps):
             starts[i].record(stream)
-            step(*inputs[i % rot])
+            if graphs is not None:
+                graphs[i % rot].replay()
+            else:
+                step(*inputs[i % rot])
             ends[i].record(stream)
         torch.cuda.synchronize(dev)
     barrier()
@@ -850,6 +868,8 @@ def main():
             },
             "e2e": e2e,
             "gpu_launches": args.steps * launches_per_step,
+            "launch": ("CUDA graph replay of the public-API step" if graphs is not None
+                       else "eager public-API calls"),
             "clocks": clocks.summary(),
         }
         if world == 1 and args.cpu_budget > 0:
