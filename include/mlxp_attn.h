@@ -121,14 +121,19 @@ size_t mlxp_attn_workspace_size(int dtype, int64_t B, int64_t H, int64_t Sq, int
  * block on a lock).
  *
  * Same arguments and results as mlxp_attn_fwd with kv_splits >= 2 (bf16/fp16 only), except that
- * the per-split partial outputs live in a static device array of 32 MiB inside the library
- * (held by every GPU that loads the library until process exit) instead of a workspace.
- * Sizes whose partials need more than that (splits * B*H*Sq rows * (head_dim + 1) floats) are
- * rejected with MLXP_ERR_WORKSPACE and a message; the caller can use fewer splits.
- * The first call on a device looks up the array's device address (cudaGetSymbolAddress) and
- * caches it; make that first call before any stream capture.  Every call shares the array:
- * calls that overlap on the GPU (other streams, other threads) race on it and must be
- * serialised by the caller.  Nothing in the array needs to start at zero.
+ * the per-split partial outputs and the per-query-tile counters live in a static device array
+ * of 32 MiB inside the library (held by every GPU that loads the library until process exit)
+ * instead of a workspace.  The split count is kv_splits clamped to the number of 128-key tiles,
+ * ceil(Skv / 128); a key range of one tile therefore runs unsplit and leaves the array unused.
+ * Sizes whose scratch needs more than 32 MiB (about splits * B*H*Sq rows * (head_dim + 1)
+ * floats, see mlxp_attn_workspace_size) are rejected with MLXP_ERR_WORKSPACE and a message;
+ * the caller can use fewer splits.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress) and caches it for the life of the process; make that first
+ * call before any stream capture, and do not keep using the library on a device after
+ * cudaDeviceReset (the cached address may no longer be the array's).  Every call shares the
+ * array and clears the counters it needs (cudaMemsetAsync on the call's stream) before its
+ * kernel: calls that overlap on the GPU (other streams, other threads) race on the array and
+ * must be serialised by the caller.
  */
 int mlxp_attn_fwd_split_noalloc(const void* q, const void* k, const void* v, void* o,
                                 float* lse, int dtype, int64_t B, int64_t H, int64_t Sq,
@@ -277,7 +282,9 @@ size_t mlxp_paged_attn_workspace_size(int dtype, int64_t B, int64_t H, int64_t S
 
 /*
  * Device-side status word of the current device: 0 when every bounded wait completed,
- * otherwise MLXP_ERR_TIMEOUT | (site << 8).  Synchronises the device.  reset != 0 clears it.
+ * otherwise MLXP_ERR_TIMEOUT | (site << 8), or MLXP_ERR_WORKSPACE | (site << 8) when a kernel
+ * found its workspace smaller than its work (it then wrote nothing there).  Synchronises the
+ * device.  reset != 0 clears it.
  */
 int mlxp_device_status(int* status_out, int reset);
 

@@ -1123,11 +1123,12 @@ size_t mlxp_attn_workspace_size(int dtype, int64_t B, int64_t H, int64_t Sq, int
   return split_workspace(pr, splits);
 }
 
-// Split-KV attention whose scratch (the per-split fp32 partial outputs and LSEs) lives in the
-// library's static device array instead of a caller-provided workspace; see mlxp_attn.h.
-// Nothing in the scratch needs to start at zero: every (split, row) partial is written by the
-// attention kernel (a split with no admissible keys writes O = 0, LSE = -inf) before the merge
-// kernel reads it, so the contents left by an earlier call are never used.
+// Split-KV attention whose scratch (the per-split fp32 partial outputs and LSEs and the
+// per-query-tile counters) lives in the library's static device array instead of a
+// caller-provided workspace; see mlxp_attn.h.  Only the counters must start at zero, and the
+// split path clears them on the call's stream before the kernel; every partial the kernel
+// merges was written by the same launch, so the contents left by an earlier call are never
+// read.
 int mlxp_attn_fwd_split_noalloc(const void* q, const void* k, const void* v, void* o,
                                 float* lse, int dtype, int64_t B, int64_t H, int64_t Sq,
                                 int64_t Skv, int64_t D, const int64_t q_strides[4],

@@ -3,11 +3,14 @@ one (mlxp_attn_fwd with a caller workspace), through the C-ABI.
 
 It serves callers that cannot allocate device memory (plugins handed only input/output
 pointers, loops that must not trigger cudaMalloc), so it keeps its scratch in a static device
-array shared by every call.  The test makes two calls in a row — the second finds the first
-call's partials still in the array — and compares each with the regular entry point within the
-bf16 tolerance the other GPU tests use (2e-2 max-abs; the LSE within 1e-2).  It also checks that
-a size whose scratch exceeds the array is rejected with a clear error before anything runs.
-This file is collected last on purpose; it must also pass when run alone.
+array shared by every call.  The test makes calls in a row on different data and shapes — each
+finds the previous call's partials and counters still in the array: a non-causal case, then a
+causal one with explicit key splits of which some reach no key of some query tiles, then the
+first again — and compares each with the regular entry point given a NaN-filled workspace.  Both
+run the same kernel with the same splits and merge the partials in the same order, so output and
+LSE must agree bit for bit (which also keeps them within the bf16 tolerance, 2e-2 max-abs, of
+the other GPU tests).  A size whose scratch exceeds the array is rejected with a clear error
+before anything runs.  This file is collected last on purpose; it must also pass when run alone.
 """
 
 import ctypes
@@ -29,39 +32,49 @@ def _case(B, H, Sq, Skv, D, seed):
     return q, k, v
 
 
-def test_no_alloc_split_matches_workspace_split_twice():
+def _run(L, _lib, q, k, v, causal, splits, noalloc):
+    B, Sq, H, D = q.shape
+    Skv = k.shape[1]
+    st = lambda t: _lib.strides4(t, "BSHD")
+    stream = torch.cuda.current_stream().cuda_stream
+    o = torch.full_like(q, float("nan"))
+    lse = torch.full((B, H, Sq), float("nan"), device="cuda")
+    qoff = (Skv - Sq) if causal else 0
+    args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(), 1, B, H, Sq,
+            Skv, D, st(q), st(k), st(v), st(o), ctypes.c_float(D ** -0.5), int(causal), -1, -1,
+            qoff, 0, splits)
+    if noalloc:
+        _lib.check(L.mlxp_attn_fwd_split_noalloc(*args, stream), "mlxp_attn_fwd_split_noalloc")
+    else:
+        ws_bytes = L.mlxp_attn_workspace_size(1, B, H, Sq, Skv, D, int(causal), -1, -1, qoff, 0,
+                                              splits)
+        assert ws_bytes > 0
+        ws = torch.full((ws_bytes // 4,), float("nan"), device="cuda")  # stale garbage
+        _lib.check(L.mlxp_attn_fwd(*args, ws.data_ptr(), ws_bytes, stream), "mlxp_attn_fwd")
+    torch.cuda.synchronize()
+    return o, lse
+
+
+def test_no_alloc_split_matches_workspace_split_on_calls_in_a_row():
     from mlx_primitives import _lib
 
     L = _lib.lib()
-    B, H, Sq, Skv, D, splits = 2, 8, 384, 9000, 128, 4
-    scale = D ** -0.5
-    stream = torch.cuda.current_stream().cuda_stream
-    st = lambda t: _lib.strides4(t, "BSHD")
-
-    q, k, v = _case(B, H, Sq, Skv, D, seed=5)
-    o_ref = torch.empty_like(q)
-    lse_ref = torch.empty((B, H, Sq), device="cuda")
-    ws_bytes = L.mlxp_attn_workspace_size(1, B, H, Sq, Skv, D, 0, -1, -1, 0, 0, splits)
-    assert ws_bytes > 0
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
-    _lib.check(L.mlxp_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o_ref.data_ptr(),
-                               lse_ref.data_ptr(), 1, B, H, Sq, Skv, D, st(q), st(k), st(v),
-                               st(o_ref), ctypes.c_float(scale), 0, -1, -1, 0, 0, splits,
-                               ws.data_ptr(), ws_bytes, stream), "mlxp_attn_fwd")
-
-    for call in range(2):
-        o = torch.full_like(q, float("nan"))
-        lse = torch.full((B, H, Sq), float("nan"), device="cuda")
-        rc = L.mlxp_attn_fwd_split_noalloc(q.data_ptr(), k.data_ptr(), v.data_ptr(),
-                                           o.data_ptr(), lse.data_ptr(), 1, B, H, Sq, Skv, D,
-                                           st(q), st(k), st(v), st(o), ctypes.c_float(scale),
-                                           0, -1, -1, 0, 0, splits, stream)
-        _lib.check(rc, "mlxp_attn_fwd_split_noalloc")
-        torch.cuda.synchronize()
-        assert torch.isfinite(o.float()).all(), f"call {call}"
-        err = (o.float() - o_ref.float()).abs().max().item()
-        assert err <= TOL, f"call {call}: max-abs {err}"
-        assert (lse - lse_ref).abs().max().item() <= 1e-2, f"call {call}"
+    cases = [
+        # (B, H, Sq, Skv, D, seed, causal, splits)
+        (2, 8, 384, 9000, 128, 5, False, 4),
+        # causal, 4 splits of 8 key tiles: query tiles near the start reach only split 0, so
+        # the other splits write nothing for them; later tiles merge 2 to 4 partials
+        (3, 4, 1000, 3968, 64, 6, True, 4),
+        (2, 8, 384, 9000, 128, 5, False, 4),
+    ]
+    for n, (B, H, Sq, Skv, D, seed, causal, splits) in enumerate(cases):
+        q, k, v = _case(B, H, Sq, Skv, D, seed)
+        o_ref, lse_ref = _run(L, _lib, q, k, v, causal, splits, noalloc=False)
+        o, lse = _run(L, _lib, q, k, v, causal, splits, noalloc=True)
+        assert torch.isfinite(o.float()).all(), f"call {n}"
+        assert torch.equal(o, o_ref), f"call {n}: max-abs {(o.float() - o_ref.float()).abs().max()}"
+        assert torch.equal(lse, lse_ref), f"call {n}"
+        assert (o.float() - o_ref.float()).abs().max().item() <= TOL
 
 
 def test_no_alloc_rejects_sizes_beyond_its_scratch():
