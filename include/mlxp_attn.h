@@ -159,6 +159,27 @@ int mlxp_attn_fwd_partial(const void* q, const void* k, const void* v, float* o_
                           int64_t kv_pos_offset, void* cuda_stream);
 
 /*
+ * Accumulating attention forward: as mlxp_attn_fwd_partial, but instead of writing this key
+ * range's result it merges it into a running one — the per-key-range fold of the reference's
+ * chunk loop (compute_chunk_attention + online_softmax_merge, _online_softmax.py:42-176), in
+ * LSE form, done in the attention kernel's epilogue:
+ *   (o_acc, lse_acc) <- merge((o_acc, lse_acc), (O, LSE) of q against this k/v range).
+ * o_acc: fp32 [B,H,Sq,D] with acc_strides (normalised running output); lse_acc: fp32 [B,H,Sq]
+ * contiguous, natural log, required.  Rows whose lse_acc is -inf take the new result alone
+ * (their o_acc is not read, so it need not be initialised; it gets O = 0 when this range has
+ * no admissible key for the row either); other rows this range gives no admissible key keep
+ * their values.  Start with lse_acc = -inf and cast o_acc at the end (mlxp_cast_output).
+ * bf16/fp16 inputs, head_dim 64 or 128; no split.  Used by the ring pass.
+ */
+int mlxp_attn_fwd_accumulate(const void* q, const void* k, const void* v, float* o_acc,
+                             float* lse_acc, int dtype, int64_t B, int64_t H, int64_t Sq,
+                             int64_t Skv, int64_t D, const int64_t q_strides[4],
+                             const int64_t k_strides[4], const int64_t v_strides[4],
+                             const int64_t acc_strides[4], float scale, int causal,
+                             int64_t window_left, int64_t window_right, int64_t q_pos_offset,
+                             int64_t kv_pos_offset, void* cuda_stream);
+
+/*
  * LSE merge of n_parts partial results (online_softmax_merge, _online_softmax.py:42-106, in
  * LSE form):  w_i = exp(lse_i - max_j lse_j);  O = sum_i w_i O_i / sum_i w_i;
  * lse = max_j lse_j + log(sum_i w_i).

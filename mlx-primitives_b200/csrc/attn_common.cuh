@@ -151,6 +151,14 @@ struct FwdParams {
   // for callers that merge partial results themselves; no key splits then).
   int out_f32;
   float* lse;                           // [B][H][Sq] contiguous, nullable unless out_f32
+  // Accumulate (with out_f32): O and lse hold a running fp32 result (normalised O, natural-log
+  // LSE) of earlier key ranges; the kernel merges its own into them (LSE weights) and writes
+  // them back.  acc_o is the same fp32 tensor the O tensor map writes, read with these element
+  // strides.  A row whose accumulated LSE is -inf takes the new result alone (its O is not
+  // read; if the new result is empty too, the row is written as O = 0, LSE = -inf).
+  int accumulate;
+  const float* acc_o;
+  long long acc_sb, acc_sh, acc_ss;
   // Key splits (splits > 1) are merged inside the kernel.  The query tiles (128 rows) that
   // more than one split touches get a partial per split: the normalised fp32 O of the split
   // at part_o + slot * 128 * D, laid out [D/4][128 rows][4] so that the 32 rows of a warp

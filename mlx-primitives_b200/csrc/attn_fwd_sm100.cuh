@@ -667,6 +667,7 @@ __global__ void __launch_bounds__(384, 1)
         nparts = (uhi > ulo) ? (uhi - 1) / p.tiles_per_split - s_first + 1 : 0;
         if (nparts == 0 ? w.split != 0 : n_it == 0) continue;
       }
+      if (p.accumulate && n_it == 0) continue;  // no key of this range reaches the tile
       if (n_it > 0) {
         ok = mbar_wait(BAR(C::B_OF + t), n_o & 1, wctx, kSiteSoftmaxO);
         ok = named_bar_and(1 + t, 128, ok);
@@ -733,6 +734,28 @@ __global__ void __launch_bounds__(384, 1)
         inv_w = wsum > 0.f ? 1.0f / wsum : 0.f;
         lse_out = wsum > 0.f ? m_tot + logf(wsum) : -INFINITY;
       }
+      // accumulate: weights of the running result and of this one (LSE form of the merge)
+      float a_old = 0.f, a_new = 1.f;
+      const float* acc_row = nullptr;
+      if (p.accumulate && has_rows) {
+        const float lse_old = p.lse[((long long)w.b * p.H + w.h) * p.Sq + qrow];
+        const float mm = fmaxf(lse_old, lse_v);
+        if (mm == -INFINITY) {  // neither has an admissible key: an empty row (O = 0)
+          a_old = 0.f;
+          a_new = 0.f;
+          lse_out = -INFINITY;
+        } else {
+          const float w_old = lse_old == -INFINITY ? 0.f : expf(lse_old - mm);
+          const float w_new = lse_v == -INFINITY ? 0.f : expf(lse_v - mm);
+          const float wsum = w_old + w_new;
+          a_old = w_old / wsum;
+          a_new = w_new / wsum;
+          lse_out = mm + logf(wsum);
+        }
+        if (a_old != 0.f)
+          acc_row = p.acc_o + (long long)w.b * p.acc_sb + (long long)w.h * p.acc_sh +
+                    (long long)qrow * p.acc_ss;
+      }
       if (has_rows && p.lse != nullptr)
         p.lse[((long long)w.b * p.H + w.h) * p.Sq + qrow] = lse_out;
       // O leaves through the tile's staging box: each thread writes its row (128-byte swizzle:
@@ -773,7 +796,17 @@ __global__ void __launch_bounds__(384, 1)
             tmem_wait_ld();
             reg_fence(ou);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) ov[i] = __uint_as_float(ou[i]) * inv_l;
+            for (int i = 0; i < 32; ++i) ov[i] = __uint_as_float(ou[i]) * (inv_l * a_new);
+            if (acc_row != nullptr) {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float4 o4 = *reinterpret_cast<const float4*>(acc_row + c * 32 + 4 * i);
+                ov[4 * i] += a_old * o4.x;
+                ov[4 * i + 1] += a_old * o4.y;
+                ov[4 * i + 2] += a_old * o4.z;
+                ov[4 * i + 3] += a_old * o4.w;
+              }
+            }
           } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i) ov[i] = 0.f;

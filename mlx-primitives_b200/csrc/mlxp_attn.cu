@@ -547,10 +547,16 @@ int merge_dispatch(const float* o_parts, const float* lse_parts, int n, void* o,
 }
 
 // Shared implementation of mlxp_attn_fwd (out_f32 = 0) and mlxp_attn_fwd_partial (out_f32 = 1).
+// Output modes of attn_fwd_impl: the input dtype (mlxp_attn_fwd), normalised fp32 + LSE
+// (mlxp_attn_fwd_partial), or merged into a running fp32 result (mlxp_attn_fwd_accumulate).
+enum FwdMode { kOutNormal = 0, kOutPartial = 1, kOutAccumulate = 2 };
+
 int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* lse,
                   const Problem& pr, const int64_t* qs, const int64_t* ks, const int64_t* vs,
                   const int64_t* os, float scale, int64_t kv_splits, void* ws, size_t ws_bytes,
-                  bool out_f32, cudaStream_t stream) {
+                  int mode, cudaStream_t stream) {
+  const bool out_f32 = mode != kOutNormal;
+  const bool accumulate = mode == kOutAccumulate;
   if (int rc = validate(pr)) return rc;
   if (!(scale > 0.f) || !std::isfinite(scale))
     return fail(MLXP_ERR_INVALID, "scale must be positive and finite");
@@ -560,6 +566,8 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
   if (!qs || !ks || !vs || !os) return fail(MLXP_ERR_INVALID, "stride arrays must be non-null");
   if (out_f32 && lse == nullptr) return fail(MLXP_ERR_INVALID, "partial output needs lse");
   const bool fp32 = pr.dtype == MLXP_DTYPE_FP32;
+  if (out_f32 && fp32)
+    return fail(MLXP_ERR_UNSUPPORTED, "partial and accumulating outputs take bf16/fp16 inputs");
   if (int rc = check_out_strides(o, os, (fp32 || out_f32) ? 4 : 8, "o")) return rc;
   if (reinterpret_cast<uintptr_t>(lse) % 4) return fail(MLXP_ERR_INVALID, "lse misaligned");
   if (pr.Sq == 0) return MLXP_OK;
@@ -569,7 +577,7 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
 
   Problem pe = pr;
   if (out_f32) pe.dtype = MLXP_DTYPE_FP32;  // output element type for the empty fill
-  if (pr.Skv == 0) return fill_empty(pe, o, lse, os, stream);
+  if (pr.Skv == 0) return accumulate ? MLXP_OK : fill_empty(pe, o, lse, os, stream);
 
   const float scale_log2 = scale * 1.4426950408889634f;
   if (fp32) {
@@ -680,6 +688,13 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
   CUtensorMap mo;
   p.out_f32 = out_f32 ? 1 : 0;
   p.lse = lse;
+  if (accumulate) {
+    p.accumulate = 1;
+    p.acc_o = static_cast<const float*>(o);
+    p.acc_sb = os[0];
+    p.acc_sh = os[1];
+    p.acc_ss = os[2];
+  }
   if (int rc = out_f32 ? make_tmap(o, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, pr.B, pr.H, pr.Sq, pr.D,
                                    os, 128, 32, "o", &mo, &p.co)
                        : make_tmap(o, dt16, 2, pr.B, pr.H, pr.Sq, pr.D, os, 128, 64, "o", &mo,
@@ -1085,7 +1100,7 @@ int mlxp_attn_fwd(const void* q, const void* k, const void* v, void* o, float* l
   Problem pr{dtype, B, H, Sq, Skv, D, causal ? 1 : 0, window_left, window_right, q_pos_offset,
              kv_pos_offset};
   return attn_fwd_impl(q, k, v, o, lse, pr, q_strides, k_strides, v_strides, o_strides, scale,
-                       kv_splits, workspace, ws_bytes, false,
+                       kv_splits, workspace, ws_bytes, kOutNormal,
                        static_cast<cudaStream_t>(cuda_stream));
 }
 
@@ -1100,7 +1115,7 @@ int mlxp_attn_fwd_gqa(const void* q, const void* k, const void* v, void* o, floa
              kv_pos_offset, H_kv};
   if (H_kv < 1) return fail(MLXP_ERR_INVALID, "num_kv_heads must be >= 1");
   return attn_fwd_impl(q, k, v, o, lse, pr, q_strides, k_strides, v_strides, o_strides, scale,
-                       kv_splits, workspace, ws_bytes, false,
+                       kv_splits, workspace, ws_bytes, kOutNormal,
                        static_cast<cudaStream_t>(cuda_stream));
 }
 
@@ -1156,7 +1171,7 @@ int mlxp_attn_fwd_split_noalloc(const void* q, const void* k, const void* v, voi
   void* scratch = nullptr;
   if (int rc = noalloc_scratch(&scratch)) return rc;
   return attn_fwd_impl(q, k, v, o, lse, pr, q_strides, k_strides, v_strides, o_strides, scale,
-                       splits, scratch, kNoAllocScratchBytes, false,
+                       splits, scratch, kNoAllocScratchBytes, kOutNormal,
                        static_cast<cudaStream_t>(cuda_stream));
 }
 
@@ -1172,7 +1187,21 @@ int mlxp_attn_fwd_partial(const void* q, const void* k, const void* v, float* o_
   Problem pr{dtype, B, H, Sq, Skv, D, causal ? 1 : 0, window_left, window_right, q_pos_offset,
              kv_pos_offset};
   return attn_fwd_impl(q, k, v, o_part, lse_part, pr, q_strides, k_strides, v_strides,
-                       o_strides, scale, 1, nullptr, 0, true,
+                       o_strides, scale, 1, nullptr, 0, kOutPartial,
+                       static_cast<cudaStream_t>(cuda_stream));
+}
+
+int mlxp_attn_fwd_accumulate(const void* q, const void* k, const void* v, float* o_acc,
+                             float* lse_acc, int dtype, int64_t B, int64_t H, int64_t Sq,
+                             int64_t Skv, int64_t D, const int64_t q_strides[4],
+                             const int64_t k_strides[4], const int64_t v_strides[4],
+                             const int64_t acc_strides[4], float scale, int causal,
+                             int64_t window_left, int64_t window_right, int64_t q_pos_offset,
+                             int64_t kv_pos_offset, void* cuda_stream) {
+  Problem pr{dtype, B, H, Sq, Skv, D, causal ? 1 : 0, window_left, window_right, q_pos_offset,
+             kv_pos_offset};
+  return attn_fwd_impl(q, k, v, o_acc, lse_acc, pr, q_strides, k_strides, v_strides,
+                       acc_strides, scale, 1, nullptr, 0, kOutAccumulate,
                        static_cast<cudaStream_t>(cuda_stream));
 }
 

@@ -1,13 +1,14 @@
 // ring_nccl.cuh — sequence-parallel causal attention over NCCL: the C-ABI ring (mlxp_ring_*).
 //
 // Included at the end of mlxp_attn.cu: it drives the library's own entry points
-// (mlxp_attn_fwd_partial, mlxp_lse_merge_accumulate, mlxp_cast_output) from C++, for callers
+// (mlxp_attn_fwd_accumulate, mlxp_cast_output) from C++, for callers
 // that are not Python.  The schedule is the zig-zag ring of mlx_primitives/attention/ring.py:
 // the sequence of S = P * S_local tokens is cut into 2P chunks of C = S_local / 2; rank r holds
 // chunks r and 2P-1-r back to back; in P steps every rank attends its two query chunks to the
 // K/V shard it holds while the shard moves one rank on (NCCL send to r+1, receive from r-1 on
-// a separate stream, so the transfer overlaps the kernels), and folds each partial into an
-// fp32 accumulator with the LSE form of online_softmax_merge
+// a separate stream, so the transfer overlaps the kernels), and folds each (query chunk, key
+// chunk) result into an fp32 accumulator, inside the attention kernel, with the LSE form of
+// online_softmax_merge
 // (mlx_primitives/attention/_online_softmax.py:42-106).
 //
 // NCCL is loaded at run time (dlopen of libnccl.so.2): a process that already holds an NCCL
@@ -104,17 +105,16 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const char* __restrict
 }
 
 // Workspace of one ring call: two K/V shard buffers (the one being computed on and the one
-// being received), the fp32 accumulators of both query chunks and one partial.
+// being received) and the fp32 accumulators of both query chunks.
 struct RingWs {
   size_t kv_bytes = 0;                  // one of K or V, contiguous [B][H][S_local][D]
   size_t off_k[2] = {0, 0}, off_v[2] = {0, 0};
-  size_t off_oacc = 0, off_lacc = 0, off_opart = 0, off_lpart = 0;
+  size_t off_oacc = 0, off_lacc = 0;
   size_t total = 0;
 };
 
 RingWs ring_ws_layout(int64_t B, int64_t H, int64_t S_local, int64_t D, int es) {
   auto up = [](size_t x) { return (x + 255) / 256 * 256; };
-  const size_t C = (size_t)S_local / 2;
   RingWs w;
   w.kv_bytes = (size_t)B * H * S_local * D * es;
   size_t off = 0;
@@ -128,10 +128,6 @@ RingWs ring_ws_layout(int64_t B, int64_t H, int64_t S_local, int64_t D, int es) 
   off += up((size_t)B * H * S_local * D * 4);
   w.off_lacc = off;
   off += up((size_t)B * H * S_local * 4);
-  w.off_opart = off;
-  off += up((size_t)B * H * C * D * 4);
-  w.off_lpart = off;
-  off += up((size_t)B * H * C * 4);
   w.total = off;
   return w;
 }
@@ -182,8 +178,6 @@ int ring_fwd(RingComm* rc, const void* q, const void* k, const void* v, void* o,
   char* vb[2] = {base + L.off_v[0], base + L.off_v[1]};
   float* o_acc = reinterpret_cast<float*>(base + L.off_oacc);
   float* l_acc = reinterpret_cast<float*>(base + L.off_lacc);
-  float* o_part = reinterpret_cast<float*>(base + L.off_opart);
-  float* l_part = reinterpret_cast<float*>(base + L.off_lpart);
   const int64_t C = S_local / 2;
   const int P = rc->nranks, r = rc->rank;
   const int nxt = (r + 1) % P, prv = (r + P - 1) % P;
@@ -232,13 +226,11 @@ int ring_fwd(RingComm* rc, const void* q, const void* k, const void* v, void* o,
         if (kchunk[ki] > qchunk[qi]) continue;  // every key after every query of the chunk
         const char* kv_ = kb[cur] + ki * C * D * es;
         const char* vv = vb[cur] + ki * C * D * es;
-        if (int e = mlxp_attn_fwd_partial(qv, kv_, vv, o_part, l_part, dtype, B, H, C, C, D, qs,
-                                          kv_st, kv_st, part_st, scale, 1, -1, -1,
-                                          (int64_t)qchunk[qi] * C, (int64_t)kchunk[ki] * C,
-                                          stream))
-          return e;
-        if (int e = mlxp_lse_merge_accumulate(o_acc + qi * B * H * C * D, l_acc + qi * B * H * C,
-                                              o_part, l_part, B, H, C, D, stream))
+        if (int e = mlxp_attn_fwd_accumulate(qv, kv_, vv, o_acc + qi * B * H * C * D,
+                                             l_acc + qi * B * H * C, dtype, B, H, C, C, D, qs,
+                                             kv_st, kv_st, part_st, scale, 1, -1, -1,
+                                             (int64_t)qchunk[qi] * C, (int64_t)kchunk[ki] * C,
+                                             stream))
           return e;
       }
     }

@@ -56,6 +56,10 @@ _SIGNATURES = {
         _p, _p, _p, _p, _p, ctypes.c_int, _i64, _i64, _i64, _i64, _i64,
         _i64x4, _i64x4, _i64x4, _i64x4, ctypes.c_float, ctypes.c_int, _i64, _i64, _i64, _i64,
         _p]),
+    "mlxp_attn_fwd_accumulate": (ctypes.c_int, [
+        _p, _p, _p, _p, _p, ctypes.c_int, _i64, _i64, _i64, _i64, _i64,
+        _i64x4, _i64x4, _i64x4, _i64x4, ctypes.c_float, ctypes.c_int, _i64, _i64, _i64, _i64,
+        _p]),
     "mlxp_lse_merge": (ctypes.c_int, [
         _p, _p, _i64, _p, _p, ctypes.c_int, _i64, _i64, _i64, _i64, _i64x4, _p]),
     "mlxp_lse_merge_accumulate": (ctypes.c_int, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _p]),

@@ -12,7 +12,10 @@ it are unmasked.  Partials are merged in fp32 with the LSE form of the reference
 online_softmax_merge (mlx_primitives/attention/_online_softmax.py:42-106).
 
 The compute backend is pluggable: ``CudaRingBackend`` runs the sm_100a kernels through the
-C-ABI (mlxp_attn_fwd_partial, mlxp_lse_merge_accumulate, mlxp_cast_output).
+C-ABI — mlxp_attn_fwd_accumulate folds each chunk pair into the rank's fp32 accumulator inside
+the attention kernel's epilogue (one launch per pair), mlxp_cast_output writes the result.  A
+backend without ``accumulate`` (the CPU oracle backend of the tests) gets ``partial`` + ``merge``
+calls instead.
 """
 
 from __future__ import annotations
@@ -66,6 +69,18 @@ class CudaRingBackend:
             ctypes.c_float(scale), 1, -1, -1, q_off, kv_off, _lib.stream_handle(q.device))
         _lib.check(rc, "mlxp_attn_fwd_partial")
 
+    def accumulate(self, q, k, v, scale, q_off, kv_off, o_acc, lse_acc):
+        """(o_acc, lse_acc) <- merge with attention of q against this k/v range, in place."""
+        L = _lib.lib()
+        B, H, Sq, D = q.shape
+        Skv = k.shape[2]
+        rc = L.mlxp_attn_fwd_accumulate(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), o_acc.data_ptr(), lse_acc.data_ptr(),
+            _lib.DTYPE_CODES[q.dtype], B, H, Sq, Skv, D, _lib.strides4(q, "BHSD"),
+            _lib.strides4(k, "BHSD"), _lib.strides4(v, "BHSD"), _lib.strides4(o_acc, "BHSD"),
+            ctypes.c_float(scale), 1, -1, -1, q_off, kv_off, _lib.stream_handle(q.device))
+        _lib.check(rc, "mlxp_attn_fwd_accumulate")
+
     def merge(self, o_acc, lse_acc, o_new, lse_new):
         B, H, S, D = o_acc.shape
         rc = _lib.lib().mlxp_lse_merge_accumulate(o_acc.data_ptr(), lse_acc.data_ptr(),
@@ -109,10 +124,12 @@ def ring_flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         prv = dist.get_global_rank(group, prv)
 
     dev = q.device
+    fused = hasattr(backend, "accumulate")
     o_acc = torch.zeros((2, B, H, C, D), dtype=torch.float32, device=dev)
     lse_acc = torch.full((2, B, H, C), float("-inf"), dtype=torch.float32, device=dev)
-    o_part = torch.empty((B, H, C, D), dtype=torch.float32, device=dev)
-    lse_part = torch.empty((B, H, C), dtype=torch.float32, device=dev)
+    if not fused:
+        o_part = torch.empty((B, H, C, D), dtype=torch.float32, device=dev)
+        lse_part = torch.empty((B, H, C), dtype=torch.float32, device=dev)
     bufs = [(torch.empty_like(k), torch.empty_like(v)) for _ in range(2 if world > 1 else 0)]
     q_chunks = zigzag_chunks(world, rank)
 
@@ -134,8 +151,11 @@ def ring_flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                     continue  # every key after every query of this chunk
                 ks = kv[0][:, :, ki * C:(ki + 1) * C]
                 vs = kv[1][:, :, ki * C:(ki + 1) * C]
-                backend.partial(qs, ks, vs, scale, qc * C, kc * C, o_part, lse_part)
-                backend.merge(o_acc[qi], lse_acc[qi], o_part, lse_part)
+                if fused:
+                    backend.accumulate(qs, ks, vs, scale, qc * C, kc * C, o_acc[qi], lse_acc[qi])
+                else:
+                    backend.partial(qs, ks, vs, scale, qc * C, kc * C, o_part, lse_part)
+                    backend.merge(o_acc[qi], lse_acc[qi], o_part, lse_part)
         for req in reqs:
             req.wait()
         if step + 1 < world:

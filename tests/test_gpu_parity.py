@@ -186,6 +186,56 @@ def test_partial_and_merge_entry_points():
     assert maxabs(out2, want) <= TOL[torch.bfloat16]
 
 
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("layout", ["BHSD", "BSHD"])
+def test_accumulate_entry_point_folds_key_ranges(D, layout):
+    """mlxp_attn_fwd_accumulate folds key ranges into a running fp32 (O, LSE) in the attention
+    kernel's epilogue: the result equals attention over the union (fp64 oracle).  The ranges
+    include one no query row reaches (rows left unchanged), one that only some rows reach, and
+    an accumulator whose O starts as NaN garbage (rows with LSE -inf must not read it)."""
+    from mlx_primitives import _lib
+    L = _lib.lib()
+    B, H, S, Skv = 2, 3, 300, 1100
+    (q, k, v), (nq, nk, nv) = inputs((B, H, S, D), (B, H, Skv, D), torch.bfloat16, seed=17 + D)
+    qoff = 520  # causal: query i sees keys j <= i + 520
+    cuts = [(850, 1100), (0, 400), (400, 401), (401, 850)]
+    if layout == "BSHD":
+        q, k, v = (t.transpose(1, 2).contiguous() for t in (q, k, v))
+    acc = torch.full((B, H, S, D), float("nan"), device=dev())
+    acc_lse = torch.full((B, H, S), float("-inf"), device=dev())
+    stream = torch.cuda.current_stream().cuda_stream
+    kv_view = (lambda t, a, b: t[:, :, a:b]) if layout == "BHSD" else (lambda t, a, b: t[:, a:b])
+    for a, b in cuts:
+        kk, vv = kv_view(k, a, b), kv_view(v, a, b)
+        rc = L.mlxp_attn_fwd_accumulate(q.data_ptr(), kk.data_ptr(), vv.data_ptr(), acc.data_ptr(),
+                                        acc_lse.data_ptr(), 1, B, H, S, b - a, D,
+                                        _lib.strides4(q, layout), _lib.strides4(kk, layout),
+                                        _lib.strides4(vv, layout), _lib.strides4(acc, "BHSD"),
+                                        ctypes.c_float(D ** -0.5), 1, -1, -1, qoff, a, stream)
+        _lib.check(rc, "mlxp_attn_fwd_accumulate")
+    torch.cuda.synchronize()
+    want, want_lse = O.attention_bhsd(nq, nk, nv, D ** -0.5, causal=True, q_offset=qoff,
+                                      return_lse=True)
+    assert torch.isfinite(acc).all()
+    assert maxabs(acc, want) <= 1e-2
+    assert np.max(np.abs(acc_lse.cpu().numpy() - want_lse)) < 1e-2
+    out = torch.empty((B, H, S, D), dtype=torch.bfloat16, device=dev())
+    _lib.check(L.mlxp_cast_output(acc.data_ptr(), out.data_ptr(), 1, B, H, S, D,
+                                  _lib.strides4(out, "BHSD"), stream), "cast")
+    assert maxabs(out, want) <= TOL[torch.bfloat16]
+    # a key range that reaches no row leaves the accumulator bit-for-bit as it was
+    before, before_lse = acc.clone(), acc_lse.clone()
+    kk, vv = kv_view(k, 0, 10), kv_view(v, 0, 10)
+    _lib.check(L.mlxp_attn_fwd_accumulate(q.data_ptr(), kk.data_ptr(), vv.data_ptr(), acc.data_ptr(),
+                                          acc_lse.data_ptr(), 1, B, H, S, 10, D,
+                                          _lib.strides4(q, layout), _lib.strides4(kk, layout),
+                                          _lib.strides4(vv, layout), _lib.strides4(acc, "BHSD"),
+                                          ctypes.c_float(D ** -0.5), 1, -1, -1, qoff, 5000, stream),
+               "accumulate (no admissible key)")
+    torch.cuda.synchronize()
+    assert torch.equal(acc, before) and torch.equal(acc_lse, before_lse)
+
+
 # ----------------------------------------------------------------------------- fp32 CUDA-core path
 @pytest.mark.parametrize("D", [32, 64, 128])
 @pytest.mark.parametrize("S", [1, 31, 64, 65, 200])
