@@ -719,8 +719,8 @@ def main():
             return o
         return api_call(qq, kk, vv)
 
-    if ring:  # per step and rank: partials + merges for the pairs below the diagonal, 2 casts
-        launches_per_step = 2 * (2 * world) + 2
+    if ring:  # per ring call and rank: one accumulate per admissible chunk pair (2P + 1), 2 casts
+        launches_per_step = (2 * world + 1) + 2
     else:
         launches_per_step = 2 if c["api"] in ("chunked", "frope") else 1
         if part:
