@@ -220,8 +220,9 @@ int mlxp_rope(const void* x, void* y, int dtype, int64_t B, int64_t H, int64_t S
 /*
  * RoPE of Q and K in one launch (rope.py:384-448, fast_rope_qk), with their own head counts,
  * lengths and position offsets (grouped K/V heads, a KV cache longer than the queries).
- * This is the rotation step of fused_rope_attention (kernels/fused_rope_attention.py:939-985),
- * which then runs mlxp_attn_fwd on the rotated tensors.
+ * The rotation step of fused_rope_attention (kernels/fused_rope_attention.py:939-985) where
+ * mlxp_rope_attn_fwd does not apply (grouped K/V heads, head_dims other than 64 and 128),
+ * followed by mlxp_attn_fwd on the rotated tensors.
  */
 int mlxp_rope_qk(const void* q, const void* k, void* q_out, void* k_out, int dtype, int64_t B,
                  int64_t Hq, int64_t Hk, int64_t Sq, int64_t Sk, int64_t D,
@@ -229,6 +230,38 @@ int mlxp_rope_qk(const void* q, const void* k, void* q_out, void* k_out, int dty
                  const int64_t qo_strides[4], const int64_t ko_strides[4],
                  const float* cos_cache, const float* sin_cache, int64_t n_pos,
                  int64_t q_pos_offset, int64_t k_pos_offset, void* cuda_stream);
+
+/*
+ * RoPE and attention in one launch: O = softmax(scale * rope(Q) rope(K)^T + mask) V, the
+ * rotation of mlxp_rope (half-split, fp32 cos/sin tables [n_pos][D/2], rounded once to the
+ * element type) applied to Q at positions q_rope_offset + i and to K at k_rope_offset + j.
+ * Replaces the reference's fused kernel, which rotates Q and K as it loads them
+ * (mlx_primitives/kernels/fused_rope_attention.py:52-198, called by fused_rope_attention
+ * :939-985).  Here the persistent attention kernel also runs rotation work items: chunks of
+ * 256 rows of Q and K are rotated into the workspace (rotation for the next scheduling group of
+ * (batch, head) units is handed out before attention of the current one, so the rotated rows
+ * are read back from L2), and the attention items read them through TMA.  The result is bit
+ * for bit that of mlxp_rope_qk followed by mlxp_attn_fwd.  Masks (causal, windows, offsets) as
+ * mlxp_attn_fwd — independent of the RoPE positions.  bf16/fp16, head_dim 64 or 128, as many
+ * K/V heads as query heads; q and k rows 16-byte aligned.  workspace: >=
+ * mlxp_rope_attn_workspace_size bytes, 256-byte aligned (the rotated copies of Q and K, counters,
+ * and any key-split scratch).
+ */
+int mlxp_rope_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
+                       int dtype, int64_t B, int64_t H, int64_t Sq, int64_t Skv, int64_t D,
+                       const int64_t q_strides[4], const int64_t k_strides[4],
+                       const int64_t v_strides[4], const int64_t o_strides[4],
+                       const float* cos_cache, const float* sin_cache, int64_t n_pos,
+                       int64_t q_rope_offset, int64_t k_rope_offset, float scale, int causal,
+                       int64_t window_left, int64_t window_right, int64_t q_pos_offset,
+                       int64_t kv_pos_offset, int64_t kv_splits, void* workspace,
+                       size_t ws_bytes, void* cuda_stream);
+
+/* Bytes of workspace mlxp_rope_attn_fwd needs for these arguments (0 for an invalid shape). */
+size_t mlxp_rope_attn_workspace_size(int dtype, int64_t B, int64_t H, int64_t Sq, int64_t Skv,
+                                     int64_t D, int causal, int64_t window_left,
+                                     int64_t window_right, int64_t q_pos_offset,
+                                     int64_t kv_pos_offset, int64_t kv_splits);
 
 /*
  * Backward pass of attention: dQ, dK, dV of O = softmax(scale * Q K^T + mask) V, the gradient

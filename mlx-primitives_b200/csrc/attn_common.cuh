@@ -159,6 +159,24 @@ struct FwdParams {
   int accumulate;
   const float* acc_o;
   long long acc_sb, acc_sh, acc_ss;
+  // RoPE in the same launch (rope_items > 0): besides its attention items every unit has
+  // rope_items rotation items — chunks of 256 rows of its Q (the first rope_q_items) and of its
+  // K — which rotate the rows with the cos/sin tables (the half-split rotation of the RoPE
+  // kernel, rounded once to the element type) into contiguous BHSD copies that the Q and K
+  // tensor maps read.  Rotation items of scheduling group g+1 are handed out before the
+  // attention items of group g (see item_coords_rope); the TMA producer waits for
+  // rot_done[g] == 2 x rotation items of group g (each is counted by both softmax warpgroups)
+  // before loading a group-g item's Q and K.
+  int rope_items, rope_q_items;
+  const void* rq_src;
+  const void* rk_src;
+  long long rq_s[3], rk_s[3];   // element strides (batch, head, seq) of the unrotated q and k
+  void* rq_dst;
+  void* rk_dst;                 // rotated copies: [B][H][Sq][D], [B][H][Skv][D]
+  const float* rope_cos;
+  const float* rope_sin;        // fp32 [n_pos][D/2]
+  long long rope_q_pos, rope_k_pos;  // position of row 0 of q and of k
+  unsigned* rot_done;           // per scheduling group, zero at launch
   // Key splits (splits > 1) are merged inside the kernel.  The query tiles (128 rows) that
   // more than one split touches get a partial per split: the normalised fp32 O of the split
   // at part_o + slot * 128 * D, laid out [D/4][128 rows][4] so that the 32 rows of a warp
@@ -242,6 +260,66 @@ __host__ __device__ inline void item_coords(const FwdParams& p, int idx, int& bh
     const int rem = idx - bh * per_unit;
     split = rem / p.n_qblk;
     qb = rem % p.n_qblk;
+  }
+}
+
+// Item order with RoPE rotation items (rope_items > 0).  Group g's rotation items R_g
+// (rope_items per unit, unit-major) and attention items A_g (in item_coords' order inside the
+// group) are laid out as  R_0 | R_1 A_0 | R_2 A_1 | ... | R_{G-1} A_{G-2} | A_{G-1}:  every
+// attention item comes after all rotation items of its group, and every item depends only on
+// items with smaller indices, so a persistent grid that hands items out in index order always
+// has one it can finish.  Returns rot = -1 for an attention item (bh, split, qb set), otherwise
+// the rotation chunk (bh set); grp = the item's scheduling group either way.
+__host__ __device__ inline void item_coords_rope(const FwdParams& p, int idx, int& bh, int& split,
+                                                 int& qb, int& rot, int& grp) {
+  const int BH = p.B * p.H, G = p.n_groups;
+  const int base = BH / G, n_big = BH % G;
+  const long long rpu = p.rope_items, apu = (long long)p.n_qblk * p.splits;
+  auto cum = [&](long long n) -> long long { return n * base + (n < n_big ? n : n_big); };
+  auto gsz = [&](long long g) -> long long { return base + (g < n_big ? 1 : 0); };
+  const long long r0 = gsz(0) * rpu;
+  // start of segment g (1 <= g <= G): R_g A_{g-1} for g < G, the final A_{G-1} for g = G
+  auto start = [&](long long g) -> long long {
+    return r0 + rpu * (cum(g) - cum(1)) + apu * cum(g - 1);
+  };
+  split = 0;
+  qb = 0;
+  if (idx < r0) {
+    grp = 0;
+    bh = (int)(idx / rpu);
+    rot = (int)(idx % rpu);
+    return;
+  }
+  long long lo = 1, hi = G;  // largest g in [1, G] with start(g) <= idx
+  while (lo < hi) {
+    const long long mid = (lo + hi + 1) / 2;
+    if (start(mid) <= idx) lo = mid;
+    else hi = mid - 1;
+  }
+  const long long g = lo;
+  long long local = idx - start(g);
+  if (g < G && local < gsz(g) * rpu) {  // rotation item of group g
+    grp = (int)g;
+    bh = (int)(cum(g) + local / rpu);
+    rot = (int)(local % rpu);
+    return;
+  }
+  if (g < G) local -= gsz(g) * rpu;
+  // attention item of group g - 1
+  grp = (int)(g - 1);
+  rot = -1;
+  const long long g0 = cum(g - 1), gs = gsz(g - 1);
+  if (p.heavy_first) {
+    const long long qrank = local / (gs * p.splits);
+    const long long rem = local - qrank * gs * p.splits;
+    bh = (int)(g0 + rem / p.splits);
+    split = (int)(rem % p.splits);
+    qb = p.n_qblk - 1 - (int)qrank;
+  } else {
+    bh = (int)(g0 + local / apu);
+    const long long rem = local % apu;
+    split = (int)(rem / p.n_qblk);
+    qb = (int)(rem % p.n_qblk);
   }
 }
 

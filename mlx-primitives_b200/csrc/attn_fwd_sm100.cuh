@@ -38,6 +38,7 @@
 #include <type_traits>
 
 #include "attn_common.cuh"
+#include "rope.cuh"
 #include "sm100_ptx.cuh"
 
 namespace mlxp {
@@ -124,7 +125,8 @@ enum : int {
   kSiteDrain = 6,
   kSiteSelfTest = 7,
   kSiteWork = 8,
-  kSiteEpilogue = 10
+  kSiteEpilogue = 10,
+  kSiteRope = 11
 };
 
 // Of every 8 column pairs of a score row, this many are exponentiated with exp2_poly2 (FMA pipe)
@@ -162,6 +164,7 @@ __device__ __forceinline__ void tma_coords(const TmaCoordMap& cm, int s, int h, 
 
 // One work item, decoded identically by every role from its index.
 struct WorkItem {
+  int rot, grp;            // rotation chunk (-1: an attention item) and scheduling group
   int b, h, split, q0;
   int lo0, hi0, lo1, hi1;  // key-tile ranges of Q tiles 0 and 1 (empty: lo == hi)
   int lo, hi;              // union range
@@ -172,9 +175,20 @@ struct WorkItem {
 __device__ __forceinline__ WorkItem decode_item(const FwdParams& p, int idx, int BN) {
   WorkItem w;
   int bh, qb;
-  item_coords(p, idx, bh, w.split, qb);
+  if (p.rope_items > 0) {
+    item_coords_rope(p, idx, bh, w.split, qb, w.rot, w.grp);
+  } else {
+    item_coords(p, idx, bh, w.split, qb);
+    w.rot = -1;
+    w.grp = 0;
+  }
   w.h = bh % p.H;
   w.b = bh / p.H;
+  if (w.rot >= 0) {  // a rotation item: no query block, no key range
+    w.q0 = 0;
+    w.lo0 = w.hi0 = w.lo1 = w.hi1 = w.lo = w.hi = 0;
+    return w;
+  }
   w.q0 = qb * 256;
   int lo_t[2], hi_t[2];
 #pragma unroll
@@ -199,6 +213,53 @@ __device__ __forceinline__ WorkItem decode_item(const FwdParams& p, int idx, int
   return w;
 }
 
+// A rotation item, run by the 256 softmax threads: rows [chunk * 256, +256) of one unit's Q
+// or K, rotated with the half-split RoPE (rope_pair: the RoPE kernel's exact arithmetic) into
+// the contiguous copy that the tensor maps read.  Per thread 8 + 8 elements of one row at a
+// time (16-byte loads and stores), so a warp moves 4 whole rows (D = 128) together.
+template <int D, bool kBF16>
+__device__ __forceinline__ void rope_rotate_rows(const FwdParams& p, const WorkItem& w, int tid) {
+  using T = std::conditional_t<kBF16, __nv_bfloat16, __half>;
+  constexpr int CP = D / 16;  // chunk pairs (8 elements of each half) per row
+  const bool isq = w.rot < p.rope_q_items;
+  const int chunk = isq ? w.rot : w.rot - p.rope_q_items;
+  const long long S = isq ? p.Sq : p.Skv;
+  const long long r0 = (long long)chunk * 256;
+  const int nrows = (int)(S - r0 < 256 ? S - r0 : 256);
+  const long long* st = isq ? p.rq_s : p.rk_s;
+  const T* src = static_cast<const T*>(isq ? p.rq_src : p.rk_src) + (long long)w.b * st[0] +
+                 (long long)w.h * st[1] + r0 * st[2];
+  T* dst = static_cast<T*>(isq ? p.rq_dst : p.rk_dst) +
+           (((long long)w.b * p.H + w.h) * S + r0) * D;
+  const long long pos0 = (isq ? p.rope_q_pos : p.rope_k_pos) + r0;
+#pragma unroll 4
+  for (int i = tid; i < nrows * CP; i += 256) {
+    const int r = i / CP, j = i - r * CP;
+    const T* x = src + r * st[2] + 8 * j;
+    const uint4 v1 = *reinterpret_cast<const uint4*>(x);
+    const uint4 v2 = *reinterpret_cast<const uint4*>(x + D / 2);
+    const float4* cr = reinterpret_cast<const float4*>(p.rope_cos + (pos0 + r) * (D / 2) + 8 * j);
+    const float4* sr = reinterpret_cast<const float4*>(p.rope_sin + (pos0 + r) * (D / 2) + 8 * j);
+    const float4 c0 = __ldg(cr), c1 = __ldg(cr + 1), s0 = __ldg(sr), s1 = __ldg(sr + 1);
+    const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    const T* x1 = reinterpret_cast<const T*>(&v1);
+    const T* x2 = reinterpret_cast<const T*>(&v2);
+    uint4 o1, o2;
+    T* y1 = reinterpret_cast<T*>(&o1);
+    T* y2 = reinterpret_cast<T*>(&o2);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float a, b;
+      rope_pair(to_f<T>(x1[e]), to_f<T>(x2[e]), c[e], sn[e], a, b);
+      y1[e] = from_f<T>(a);
+      y2[e] = from_f<T>(b);
+    }
+    *reinterpret_cast<uint4*>(dst + r * D + 8 * j) = o1;
+    *reinterpret_cast<uint4*>(dst + r * D + D / 2 + 8 * j) = o2;
+  }
+}
+
 template <int D, bool kBF16, int NS>
 __global__ void __launch_bounds__(384, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -218,7 +279,7 @@ __global__ void __launch_bounds__(384, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n_items = p.n_qblk * p.B * p.H * p.splits;
+  const int n_items = p.n_qblk * p.B * p.H * p.splits + p.B * p.H * p.rope_items;
 #if MLXP_TRACE
   if (threadIdx.x == 0 && blockIdx.x < 1024) g_mlxp_cta_life[blockIdx.x * 3] = (long long)global_timer_ns();
 #endif
@@ -267,6 +328,7 @@ __global__ void __launch_bounds__(384, 1)
         tma_prefetch_desc(&tm_o);
         const uint32_t sQ = sbase + C::OFF_Q, sK = sbase + C::OFF_K, sV = sbase + C::OFF_V;
         int fk = 0, n_q = 0;  // key-tile fills (K and V) and Q loads issued so far
+        int rot_ready = -1;   // scheduling groups up to this one have their Q and K rotated
         bool ok = true;
         for (int item = 0; ok; ++item) {
           const int slot = item & 1;
@@ -276,15 +338,28 @@ __global__ void __launch_bounds__(384, 1)
             if (!ok) break;
           }
           // the first item of every CTA is its block index (no atomic on the launch's
-          // critical path); later ones come from the counter, past the first gridDim.x
-          const int idx = item == 0 ? (int)blockIdx.x
-                                    : (int)(gridDim.x + atomicAdd(p.work_counter, 1u));
+          // critical path); later ones come from the counter, past the first gridDim.x.  With
+          // rotation items every item comes from the counter: an item may wait for smaller
+          // ones, which must then belong to CTAs that are running.
+          const int idx = p.rope_items > 0 ? (int)atomicAdd(p.work_counter, 1u)
+                          : item == 0      ? (int)blockIdx.x
+                                           : (int)(gridDim.x + atomicAdd(p.work_counter, 1u));
           work_slot[slot] = idx;
           MLXP_TR(true, 3, item, 1);
           mbar_arrive(BAR(C::B_WF + slot));  // release: the slot write is visible to waiters
           if (idx >= n_items) break;
           const WorkItem w = decode_item(p, idx, C::BN);
-          if (w.hi <= w.lo) continue;
+          if (w.hi <= w.lo) continue;  // rotation items and empty items load nothing
+          if (p.rope_items > 0 && w.grp > rot_ready) {
+            // Q and K of this group are rotated by other items: wait until all are done
+            const int base = p.B * p.H / p.n_groups, n_big = p.B * p.H % p.n_groups;
+            // two arrivals (one per softmax warpgroup) per rotation item
+            const unsigned need = (unsigned)((base + (w.grp < n_big ? 1 : 0)) * p.rope_items * 2);
+            ok = wait_count_geq(p.rot_done + w.grp, need, wctx, kSiteRope);
+            if (!ok) break;
+            fence_proxy_async_global();  // the rotated rows, written by generic stores, for TMA
+            rot_ready = w.grp;
+          }
 #if MLXP_TRACE
           if (idx < 8192) {
             uint32_t smid;
@@ -496,6 +571,18 @@ __global__ void __launch_bounds__(384, 1)
       mbar_arrive(BAR(C::B_WE + slot));
       if (idx >= n_items) break;
       const WorkItem w = decode_item(p, idx, C::BN);
+      if (w.rot >= 0) {
+        // rotation item: both warpgroups rotate their share of the rows, then each counts
+        // itself done for the group (release: its rows are visible at device scope, to
+        // generic and async-proxy readers, first).  Each warpgroup syncs only its own 128
+        // threads, which all reach the barrier: the other may have left on an abort.
+        rope_rotate_rows<D, kBF16>(p, w, (int)threadIdx.x);
+        fence_proxy_async_global();
+        __threadfence();
+        named_bar_sync(1 + t, 128);
+        if (wq == 0 && lane == 0) atomicAdd(p.rot_done + w.grp, 1u);
+        continue;
+      }
       const int tlo = t ? w.lo1 : w.lo0, thi = t ? w.hi1 : w.hi0;
       const int qrow = w.q0 + t * 128 + row;
       const long long r0 = w.q0 + t * 128;

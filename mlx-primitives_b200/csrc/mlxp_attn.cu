@@ -547,6 +547,30 @@ int merge_dispatch(const float* o_parts, const float* lse_parts, int n, void* o,
 }
 
 // Shared implementation of mlxp_attn_fwd (out_f32 = 0) and mlxp_attn_fwd_partial (out_f32 = 1).
+// RoPE applied inside the attention launch (mlxp_rope_attn_fwd): fp32 cos/sin tables
+// [n_pos][D/2] and the position of row 0 of q and of k.
+struct RopeArgs {
+  const float* cosc;
+  const float* sinc;
+  int64_t n_pos, q_pos, k_pos;
+};
+
+// Workspace of RoPE inside the attention launch: one counter per (batch, head) unit (an upper
+// bound on the scheduling groups), then the rotated Q and K copies (contiguous BHSD); the
+// key-split workspace, when splits are used, follows.
+struct RopeLayout {
+  size_t cnt_bytes, q_bytes, k_bytes;
+  size_t total() const { return cnt_bytes + q_bytes + k_bytes; }
+};
+RopeLayout rope_layout(const Problem& pr) {
+  auto up = [](size_t x) { return (x + 255) / 256 * 256; };
+  RopeLayout l;
+  l.cnt_bytes = up((size_t)pr.B * pr.H * 4);
+  l.q_bytes = up((size_t)pr.B * pr.H * pr.Sq * pr.D * 2);
+  l.k_bytes = up((size_t)pr.B * pr.H * pr.Skv * pr.D * 2);
+  return l;
+}
+
 // Output modes of attn_fwd_impl: the input dtype (mlxp_attn_fwd), normalised fp32 + LSE
 // (mlxp_attn_fwd_partial), or merged into a running fp32 result (mlxp_attn_fwd_accumulate).
 enum FwdMode { kOutNormal = 0, kOutPartial = 1, kOutAccumulate = 2 };
@@ -554,7 +578,7 @@ enum FwdMode { kOutNormal = 0, kOutPartial = 1, kOutAccumulate = 2 };
 int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* lse,
                   const Problem& pr, const int64_t* qs, const int64_t* ks, const int64_t* vs,
                   const int64_t* os, float scale, int64_t kv_splits, void* ws, size_t ws_bytes,
-                  int mode, cudaStream_t stream) {
+                  int mode, cudaStream_t stream, const RopeArgs* rope = nullptr) {
   const bool out_f32 = mode != kOutNormal;
   const bool accumulate = mode == kOutAccumulate;
   if (int rc = validate(pr)) return rc;
@@ -646,10 +670,68 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
   FwdParams p{};
   const CUtensorMapDataType dt16 =
       bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  if (int rc = make_tmap(q, dt16, 2, pr.B, pr.H, pr.Sq, pr.D, qs, 128, 64, "q", &mq, &p.cq))
+  // With RoPE the kernel's rotation items write rotated Q and K into the workspace, and the
+  // Q/K tensor maps read those contiguous copies instead of q and k.
+  const void* q_map = q;
+  const void* k_map = k;
+  const int64_t* qs_map = qs;
+  const int64_t* ks_map = ks;
+  int64_t rq_st[4], rk_st[4];
+  RopeLayout rlay{0, 0, 0};
+  if (rope) {
+    if (pr.kv_heads() != pr.H)
+      return fail(MLXP_ERR_UNSUPPORTED, "RoPE inside the attention launch needs as many K/V "
+                                        "heads as query heads");
+    if (!rope->cosc || !rope->sinc) return fail(MLXP_ERR_INVALID, "cos/sin tables must be non-null");
+    if ((reinterpret_cast<uintptr_t>(rope->cosc) | reinterpret_cast<uintptr_t>(rope->sinc)) % 16)
+      return fail(MLXP_ERR_INVALID, "cos/sin tables must be 16-byte aligned");
+    if (rope->q_pos < 0 || rope->k_pos < 0 || rope->q_pos + pr.Sq > rope->n_pos ||
+        rope->k_pos + pr.Skv > rope->n_pos)
+      return fail(MLXP_ERR_INVALID,
+                  "positions [%lld, %lld) / [%lld, %lld) exceed the cos/sin table of %lld positions",
+                  (long long)rope->q_pos, (long long)(rope->q_pos + pr.Sq), (long long)rope->k_pos,
+                  (long long)(rope->k_pos + pr.Skv), (long long)rope->n_pos);
+    if (int rc = check_out_strides(q, qs, 8, "q")) return rc;  // 16-byte row accesses
+    if (int rc = check_out_strides(k, ks, 8, "k")) return rc;
+    rlay = rope_layout(pr);
+    if (ws == nullptr || ws_bytes < rlay.total())
+      return fail(MLXP_ERR_WORKSPACE, "RoPE in the attention launch needs %zu bytes of workspace, "
+                  "got %zu", rlay.total(), ws_bytes);
+    if (reinterpret_cast<uintptr_t>(ws) % 256)
+      return fail(MLXP_ERR_INVALID, "workspace must be 256-byte aligned");
+    char* base = static_cast<char*>(ws);
+    p.rot_done = reinterpret_cast<unsigned*>(base);
+    p.rq_dst = base + rlay.cnt_bytes;
+    p.rk_dst = base + rlay.cnt_bytes + rlay.q_bytes;
+    p.rq_src = q;
+    p.rk_src = k;
+    for (int i = 0; i < 3; ++i) {
+      p.rq_s[i] = qs[i];
+      p.rk_s[i] = ks[i];
+    }
+    p.rope_cos = rope->cosc;
+    p.rope_sin = rope->sinc;
+    p.rope_q_pos = rope->q_pos;
+    p.rope_k_pos = rope->k_pos;
+    p.rope_q_items = (int)((pr.Sq + 255) / 256);
+    p.rope_items = p.rope_q_items + (int)((pr.Skv + 255) / 256);
+    const int64_t qc[4] = {pr.H * pr.Sq * pr.D, pr.Sq * pr.D, pr.D, 1};
+    const int64_t kc[4] = {pr.H * pr.Skv * pr.D, pr.Skv * pr.D, pr.D, 1};
+    std::memcpy(rq_st, qc, sizeof(qc));
+    std::memcpy(rk_st, kc, sizeof(kc));
+    q_map = p.rq_dst;
+    k_map = p.rk_dst;
+    qs_map = rq_st;
+    ks_map = rk_st;
+    // what follows (key splits) uses the rest of the workspace
+    ws = base + rlay.total();
+    ws_bytes -= rlay.total();
+  }
+  if (int rc = make_tmap(q_map, dt16, 2, pr.B, pr.H, pr.Sq, pr.D, qs_map, 128, 64, "q", &mq,
+                         &p.cq))
     return rc;
-  if (int rc = make_tmap(k, dt16, 2, pr.B, pr.kv_heads(), pr.Skv, pr.D, ks, kBN, 64, "k", &mk,
-                         &p.ck))
+  if (int rc = make_tmap(k_map, dt16, 2, pr.B, pr.kv_heads(), pr.Skv, pr.D, ks_map, kBN, 64, "k",
+                         &mk, &p.ck))
     return rc;
   if (int rc = make_tmap(v, dt16, 2, pr.B, pr.kv_heads(), pr.Skv, pr.D, vs, kBN, 64, "v", &mv,
                          &p.cv))
@@ -716,6 +798,10 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
     p.part_tiles = (long long)lay.tiles;
     cudaError_t e = cudaMemsetAsync(base, 0, lay.cnt_bytes, stream);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(split counters)");
+  }
+  if (rope) {
+    cudaError_t e = cudaMemsetAsync(p.rot_done, 0, rlay.cnt_bytes, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(rotation counters)");
   }
   return launch_tc((int)pr.D, bf16, mq, mk, mv, mo, p, stream);
 }
@@ -1203,6 +1289,37 @@ int mlxp_attn_fwd_accumulate(const void* q, const void* k, const void* v, float*
   return attn_fwd_impl(q, k, v, o_acc, lse_acc, pr, q_strides, k_strides, v_strides,
                        acc_strides, scale, 1, nullptr, 0, kOutAccumulate,
                        static_cast<cudaStream_t>(cuda_stream));
+}
+
+size_t mlxp_rope_attn_workspace_size(int dtype, int64_t B, int64_t H, int64_t Sq, int64_t Skv,
+                                     int64_t D, int causal, int64_t window_left,
+                                     int64_t window_right, int64_t q_pos_offset,
+                                     int64_t kv_pos_offset, int64_t kv_splits) {
+  Problem pr{dtype, B, H, Sq, Skv, D, causal ? 1 : 0, window_left, window_right, q_pos_offset,
+             kv_pos_offset};
+  if (validate(pr) != MLXP_OK || dtype == MLXP_DTYPE_FP32 || Sq == 0 || Skv == 0) return 0;
+  return rope_layout(pr).total() +
+         mlxp_attn_workspace_size(dtype, B, H, Sq, Skv, D, causal, window_left, window_right,
+                                  q_pos_offset, kv_pos_offset, kv_splits);
+}
+
+int mlxp_rope_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
+                       int dtype, int64_t B, int64_t H, int64_t Sq, int64_t Skv, int64_t D,
+                       const int64_t q_strides[4], const int64_t k_strides[4],
+                       const int64_t v_strides[4], const int64_t o_strides[4],
+                       const float* cos_cache, const float* sin_cache, int64_t n_pos,
+                       int64_t q_rope_offset, int64_t k_rope_offset, float scale, int causal,
+                       int64_t window_left, int64_t window_right, int64_t q_pos_offset,
+                       int64_t kv_pos_offset, int64_t kv_splits, void* workspace,
+                       size_t ws_bytes, void* cuda_stream) {
+  Problem pr{dtype, B, H, Sq, Skv, D, causal ? 1 : 0, window_left, window_right, q_pos_offset,
+             kv_pos_offset};
+  if (dtype == MLXP_DTYPE_FP32)
+    return fail(MLXP_ERR_UNSUPPORTED, "RoPE inside the attention launch takes bf16/fp16 inputs");
+  const RopeArgs ra{cos_cache, sin_cache, n_pos, q_rope_offset, k_rope_offset};
+  return attn_fwd_impl(q, k, v, o, lse, pr, q_strides, k_strides, v_strides, o_strides, scale,
+                       kv_splits, workspace, ws_bytes, kOutNormal,
+                       static_cast<cudaStream_t>(cuda_stream), &ra);
 }
 
 int mlxp_lse_merge(const float* o_parts, const float* lse_parts, int64_t n_parts, void* o,

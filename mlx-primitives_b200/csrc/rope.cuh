@@ -49,6 +49,15 @@ __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return
 template <>
 __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
 
+// One rotated pair (x1, x2) -> (x1 cos - x2 sin, x1 sin + x2 cos), each product and sum rounded
+// separately (no contraction into FMAs), so that every kernel that rotates (this one and the
+// attention kernel's rotation items) produces the same bits.
+__device__ __forceinline__ void rope_pair(float a, float b, float c, float sn, float& y1,
+                                          float& y2) {
+  y1 = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sn));
+  y2 = __fadd_rn(__fmul_rn(a, sn), __fmul_rn(b, c));
+}
+
 // VEC pairs per thread: 16 / sizeof(T) (one 16-byte access per half) when half is a multiple
 // of it and every row starts on 16 bytes, else 1.  A block handles one token (batch, position)
 // at a time: its threads cover the token's heads x (half / VEC) pair groups, so the index
@@ -88,8 +97,10 @@ __global__ void __launch_bounds__(256) rope_kernel(const RopeParams p) {
       for (int e = 0; e < VEC; ++e) {
         const float a = to_f<T>(x1[e]), bb = to_f<T>(x2[e]);
         const float c = __ldg(crow + g * VEC + e), sn = __ldg(srow + g * VEC + e);
-        y1[e] = from_f<T>(a * c - bb * sn);
-        y2[e] = from_f<T>(a * sn + bb * c);
+        float r1, r2;
+        rope_pair(a, bb, c, sn, r1, r2);
+        y1[e] = from_f<T>(r1);
+        y2[e] = from_f<T>(r2);
       }
       if constexpr (VEC * sizeof(T) == 16) {
         *reinterpret_cast<uint4*>(y + g * VEC) = *reinterpret_cast<const uint4*>(y1);

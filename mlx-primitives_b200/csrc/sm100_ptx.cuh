@@ -96,6 +96,31 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const W
   return mbar_wait_slow(bar, parity, w, site);
 }
 
+// Bounded wait until *ctr >= target, a counter other CTAs raise with atomics (acquire load at
+// device scope, so their writes that precede the raise are visible afterwards).  Gives up like
+// mbar_wait: abort flag, time limit, poll cap; returns false then.
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ bool wait_count_geq(const unsigned* ctr, unsigned target,
+                                               const WaitCtx& w, int site) {
+  if (ld_acquire_gpu(ctr) >= target) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 1; it < (1u << 26); ++it) {
+    __nanosleep(100);
+    if (ld_acquire_gpu(ctr) >= target) return true;
+    if ((it & 15u) == 0) {
+      if (*reinterpret_cast<volatile int*>(w.abort_flag)) return false;
+      if (global_timer_ns() - t0 > w.timeout_ns) break;
+    }
+  }
+  *reinterpret_cast<volatile int*>(w.abort_flag) = 1;
+  atomicCAS(w.status, 0, kDevTimeout | (site << 8));
+  return false;
+}
+
 // ------------------------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor) — every load in this library is a unicast copy.
 // ------------------------------------------------------------------------------------------
@@ -156,6 +181,12 @@ __device__ __forceinline__ void bulk_wait_group0() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 // Make this thread's generic-proxy shared-memory writes visible to the async proxy (TMA).
+// Orders this thread's generic-proxy accesses of global memory with its async-proxy (TMA)
+// accesses that follow, e.g. a TMA load of rows other CTAs wrote with plain stores.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

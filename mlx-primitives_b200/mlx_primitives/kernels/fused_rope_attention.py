@@ -1,9 +1,13 @@
 """RoPE + flash attention on B200 (drop-in for mlx_primitives/kernels/fused_rope_attention.py).
 
 ``fused_rope_attention`` (fused_rope_attention.py:939-985), ``fast_fused_rope_attention``
-(:637-733) and ``FusedRoPEFlashAttention`` (:988-1080): the reference rotates Q and K with its
-RoPE kernel and then runs scaled-dot-product attention.  Here one launch rotates Q and K
-(mlxp_rope_qk, memory-bound) and the tcgen05 attention kernel runs on the rotated tensors.
+(:637-733) and ``FusedRoPEFlashAttention`` (:988-1080): the reference rotates Q and K inside
+its attention kernel (fused_rope_attention.py:52-198).  Here too RoPE and attention are one
+launch (mlxp_rope_attn_fwd): the persistent tcgen05 attention kernel also runs rotation work
+items that rotate 256-row chunks of Q and K into an L2-resident workspace one scheduling group
+ahead of the attention items that read them.  Where that launch does not apply (grouped K/V
+heads, head_dims other than 64 and 128, fp32, autograd) Q and K are rotated by one RoPE launch
+(mlxp_rope_qk) and attention runs on the rotated tensors — the same arithmetic, bit for bit.
 Q/K/V are (batch, seq, heads, head_dim); Q positions start at ``q_offset``, K positions at
 ``kv_offset``; the causal mask is the reference's: bottom-right aligned (SDPA "causal"),
 independent of the offsets.
@@ -17,6 +21,9 @@ from typing import Optional, Tuple
 import torch
 from torch import nn
 
+import ctypes
+
+from .. import _lib
 from ..attention._core import attention_forward
 from .rope import fast_rope_qk, precompute_rope_cache
 
@@ -83,9 +90,55 @@ def fast_fused_rope_attention(
         dev = q.device if q.device.type == "cuda" else torch.device(
             "cuda", torch.cuda.current_device())
         cos_cache, sin_cache = _default_cache(max_pos, head_dim, rope_base, dev)
+    mask_off = (seq_kv - seq_q) if causal else 0
+    if _single_launch_applies(q, k, v, cos_cache, sin_cache):
+        return _rope_attention_launch(q, k, v, cos_cache, sin_cache, q_offset, kv_offset,
+                                      float(scale), bool(causal), mask_off)
     q_rot, k_rot = fast_rope_qk(q, k, cos_cache, sin_cache, q_offset, k_offset=kv_offset)
     return attention_forward(q_rot, k_rot, v, layout="BSHD", scale=float(scale),
-                             causal=bool(causal), q_offset=(seq_kv - seq_q) if causal else 0)
+                             causal=bool(causal), q_offset=mask_off)
+
+
+def _single_launch_applies(q, k, v, cos_cache, sin_cache) -> bool:
+    """mlxp_rope_attn_fwd covers bf16/fp16 CUDA tensors with head_dim 64 or 128, as many K/V
+    heads as query heads, 16-byte aligned rows, fp32 tables, and no gradient to record."""
+    if q.device.type != "cuda" or q.dtype not in (torch.bfloat16, torch.float16):
+        return False
+    if q.shape[-1] not in (64, 128) or k.shape[2] != q.shape[2] or k.shape[0] != q.shape[0]:
+        return False
+    if torch.is_grad_enabled() and any(t.requires_grad for t in (q, k, v)):
+        return False
+    if cos_cache.dtype != torch.float32 or sin_cache.dtype != torch.float32:
+        return False
+    for t in (q, k):
+        if t.stride(-1) != 1 or t.data_ptr() % 16 or any(st % 8 for st in t.stride()[:3]):
+            return False
+    return True
+
+
+def _rope_attention_launch(q, k, v, cos_cache, sin_cache, q_offset, kv_offset, scale, causal,
+                           mask_off):
+    """One mlxp_rope_attn_fwd launch on (batch, seq, heads, head_dim) tensors."""
+    B, Sq, H, D = q.shape
+    Skv = k.shape[1]
+    v = v if v.stride(-1) == 1 else v.contiguous()
+    cos_cache, sin_cache = (t.contiguous() for t in (cos_cache, sin_cache))
+    out = torch.empty((B, Sq, H, D), dtype=q.dtype, device=q.device)
+    L = _lib.lib()
+    dt = _lib.DTYPE_CODES[q.dtype]
+    with torch.cuda.device(q.device):
+        ws_bytes = L.mlxp_rope_attn_workspace_size(dt, B, H, Sq, Skv, D, int(causal), -1, -1,
+                                                   mask_off, 0, 0)
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
+        rc = L.mlxp_rope_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), None,
+                                  dt, B, H, Sq, Skv, D, _lib.strides4(q, "BSHD"),
+                                  _lib.strides4(k, "BSHD"), _lib.strides4(v, "BSHD"),
+                                  _lib.strides4(out, "BSHD"), cos_cache.data_ptr(),
+                                  sin_cache.data_ptr(), cos_cache.shape[0], q_offset, kv_offset,
+                                  ctypes.c_float(scale), int(causal), -1, -1, mask_off, 0, 0,
+                                  ws.data_ptr(), ws_bytes, _lib.stream_handle(q.device))
+    _lib.check(rc, "mlxp_rope_attn_fwd")
+    return out
 
 
 def fused_rope_attention(

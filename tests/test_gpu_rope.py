@@ -98,3 +98,65 @@ def test_fused_rope_module_with_cache():
     x1 = torch.randn(2, 1, 256, device="cuda")
     out1, cache1 = mod(x1, cache=cache, offset=40)
     assert cache1[0].shape == (2, 41, 4, 64) and out1.shape == (2, 1, 256)
+
+
+def _two_launch(q, k, v, cos, sin, q_off, k_off, causal):
+    """mlxp_rope_qk, then attention on the rotated tensors (the path the single launch replaces)."""
+    from mlx_primitives.attention._core import attention_forward
+    from mlx_primitives.kernels import fast_rope_qk
+
+    qr, kr = fast_rope_qk(q, k, cos, sin, q_off, k_offset=k_off)
+    Sq, Skv = q.shape[1], k.shape[1]
+    return attention_forward(qr, kr, v, layout="BSHD", scale=q.shape[-1] ** -0.5, causal=causal,
+                             q_offset=(Skv - Sq) if causal else 0)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("shape,causal,offsets", [
+    ((2, 1000, 4), True, (0, 0)),       # S not a multiple of the 256-row rotation chunk
+    ((1, 300, 3, 700), True, (400, 0)),  # cached keys: Sq < Skv, query positions after them
+    ((3, 257, 2, 257), False, (7, 7)),
+])
+def test_rope_attention_single_launch_is_the_two_launch_result(dtype, D, shape, causal, offsets):
+    """mlxp_rope_attn_fwd (rotation items inside the attention launch) against mlxp_rope_qk +
+    attention: bit-identical (same rotation arithmetic and rounding, same attention kernel),
+    and within the bf16/fp16 tolerance of the oracle's rope + attention."""
+    import mlx_primitives.kernels.fused_rope_attention as M
+    from mlx_primitives.kernels import fused_rope_attention, precompute_rope_cache
+
+    B, Sq, H = shape[:3]
+    Skv = shape[3] if len(shape) > 3 else Sq
+    q, nq = _x((B, Sq, H, D), dtype, seed=D + Sq)
+    k, nk = _x((B, Skv, H, D), dtype, seed=D + Skv + 1)
+    v, nv = _x((B, Skv, H, D), dtype, seed=D + 2)
+    q_off, k_off = offsets
+    n_pos = max(Sq + q_off, Skv + k_off)
+    cos, sin = precompute_rope_cache(n_pos, D)
+    assert M._single_launch_applies(q, k, v, cos, sin)
+    got = fused_rope_attention(q, k, v, cos_cache=cos, sin_cache=sin, q_offset=q_off,
+                               kv_offset=k_off, causal=causal)
+    want2 = _two_launch(q, k, v, cos, sin, q_off, k_off, causal)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want2)
+    ncos, nsin = O.precompute_rope_cache(n_pos, D)
+    want = O.fused_rope_attention(nq, nk, nv, cos_cache=ncos, sin_cache=nsin, q_offset=q_off,
+                                  kv_offset=k_off, causal=causal)
+    assert np.max(np.abs(got.float().cpu().numpy() - want)) <= 2e-2
+
+
+def test_rope_attention_single_launch_config2_shape_and_repeat():
+    """The config-2 shape (B4 S4096 H32 D128, BSHD, causal) twice in a row: bit-identical to
+    the two-launch path each time (the workspace counters are cleared per launch)."""
+    from mlx_primitives.kernels import fused_rope_attention, precompute_rope_cache
+
+    g = torch.Generator(device="cuda")
+    g.manual_seed(11)
+    q, k, v = (torch.randn((4, 4096, 32, 128), generator=g, device="cuda").bfloat16()
+               for _ in range(3))
+    cos, sin = precompute_rope_cache(4096, 128)
+    want = _two_launch(q, k, v, cos, sin, 0, 0, True)
+    for _ in range(2):
+        got = fused_rope_attention(q, k, v, cos_cache=cos, sin_cache=sin, causal=True)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)
