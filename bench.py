@@ -722,7 +722,7 @@ def main():
     if ring:  # per ring call and rank: one accumulate per admissible chunk pair (2P + 1), 2 casts
         launches_per_step = (2 * world + 1) + 2
     else:
-        launches_per_step = 2 if c["api"] in ("chunked", "frope") else 1
+        launches_per_step = 1  # splits and RoPE run inside the one attention launch
         if part:
             launches_per_step *= len(pieces)
     unit_frac = len(units) / (B * H)  # share of the workload this rank computes
