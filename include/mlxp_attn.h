@@ -103,6 +103,27 @@ int mlxp_attn_fwd_gqa(const void* q, const void* k, const void* v, void* o, floa
                       void* cuda_stream);
 
 /*
+ * Attention with an additive mask: as mlxp_attn_fwd_gqa, with
+ *   scores = scale * Q K^T + mask[b][h][i][j]   (before causal / window masking and softmax)
+ * the custom `mask` of the reference's gqa_attention and mqa_attention, added to the scores
+ * after the causal mask (mlx_primitives/attention/grouped_query.py:253-254,
+ * multi_query.py:218-219).  mask: fp32, element strides (batch, head, query row, key) in
+ * mask_strides — 0 for broadcast dims, key stride 1, the others multiples of 4 with a 16-byte
+ * aligned base; -inf entries exclude keys.  A row left with no admissible key gives O = 0,
+ * LSE = -inf.  bf16/fp16 run a separate instantiation of the tensor-core kernel that adds the
+ * mask row by row to the scores (the unmasked kernel is unchanged); fp32 the CUDA-core kernel.
+ * The workspace is mlxp_attn_fwd's (mlxp_attn_workspace_size).
+ */
+int mlxp_attn_fwd_masked(const void* q, const void* k, const void* v, void* o, float* lse,
+                         int dtype, int64_t B, int64_t H, int64_t H_kv, int64_t Sq, int64_t Skv,
+                         int64_t D, const int64_t q_strides[4], const int64_t k_strides[4],
+                         const int64_t v_strides[4], const int64_t o_strides[4],
+                         const float* mask, const int64_t mask_strides[4], float scale,
+                         int causal, int64_t window_left, int64_t window_right,
+                         int64_t q_pos_offset, int64_t kv_pos_offset, int64_t kv_splits,
+                         void* workspace, size_t ws_bytes, void* cuda_stream);
+
+/*
  * Bytes of workspace mlxp_attn_fwd needs for these arguments (0 when no split is used).
  * kv_splits as for mlxp_attn_fwd (0 = the automatic choice mlxp_attn_fwd would make).
  * Replaces the reference's implicit MLX allocation of intermediate arrays (chunked.py:142-166).

@@ -177,6 +177,13 @@ struct FwdParams {
   const float* rope_sin;        // fp32 [n_pos][D/2]
   long long rope_q_pos, rope_k_pos;  // position of row 0 of q and of k
   unsigned* rot_done;           // per scheduling group, zero at launch
+  // Additive score bias (the custom mask of gqa_attention / mqa_attention), fp32, element
+  // strides (batch, head, query row) — 0 for broadcast dims — and unit stride along keys:
+  // scores become scale * q.k + bias[b][h][i][j] before the softmax.  Only the kernel
+  // instantiation built for it reads this.
+  const float* bias;
+  long long bias_sb, bias_sh, bias_sq;
+  float inv_scale;              // 1 / scale: the bias is added in units of the raw q.k
   // Key splits (splits > 1) are merged inside the kernel.  The query tiles (128 rows) that
   // more than one split touches get a partial per split: the normalised fp32 O of the split
   // at part_o + slot * 128 * D, laid out [D/4][128 rows][4] so that the 32 rows of a warp
@@ -216,6 +223,9 @@ struct FwdParamsF32 {
   // a normalised partial at o + split * o_split, lse + split * lse_split (merged afterwards).
   int splits;
   long long o_split, lse_split;
+  // additive score bias (nullable), as FwdParams::bias
+  const float* bias;
+  long long bias_sb, bias_sh, bias_sq;
 };
 
 // Work-item order of the persistent tensor-core kernel: item index idx in [0, n_qblk * B * H *

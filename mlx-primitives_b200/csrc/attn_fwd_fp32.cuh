@@ -152,6 +152,17 @@ __global__ void __launch_bounds__(256) attn_fwd_fp32_kernel(const FwdParamsF32 p
         s[i][c] = (col < c_lo || col > c_hi) ? -INFINITY : s[i][c] * sl2;
         mx = fmaxf(mx, s[i][c]);
       }
+      if (p.bias != nullptr && row < p.Sq) {  // additive bias (log2 units: times log2(e))
+        const float* br = p.bias + (long long)b * p.bias_sb + (long long)h * p.bias_sh +
+                          (long long)row * p.bias_sq + c0;
+        mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < C::NC; ++c) {
+          const int col = tx + 16 * c;
+          if (c0 + col < p.Skv) s[i][c] += __ldg(br + col) * 1.4426950408889634f;
+          mx = fmaxf(mx, s[i][c]);
+        }
+      }
 #pragma unroll
       for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off, 16));
       const float m_new = fmaxf(m[i], mx);

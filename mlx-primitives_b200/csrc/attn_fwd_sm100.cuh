@@ -260,7 +260,7 @@ __device__ __forceinline__ void rope_rotate_rows(const FwdParams& p, const WorkI
   }
 }
 
-template <int D, bool kBF16, int NS>
+template <int D, bool kBF16, int NS, bool kBias>
 __global__ void __launch_bounds__(384, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                           const __grid_constant__ CUtensorMap tm_k,
@@ -661,6 +661,30 @@ __global__ void __launch_bounds__(384, 1)
           for (int c = 0; c < 32; ++c) {
             s[64 + c] = __uint_as_float(ra[c]);
             s[96 + c] = __uint_as_float(rb[c]);
+          }
+        }
+        if constexpr (kBias) {
+          // additive bias (the custom mask of gqa/mqa attention), in units of the raw q.k so
+          // that everything below is unchanged; columns past Skv stay -inf
+          if (qrow < p.Sq) {
+            const float* br = p.bias + (long long)w.b * p.bias_sb + (long long)w.h * p.bias_sh +
+                              (long long)qrow * p.bias_sq + (long long)j * C::BN;
+            const float isc = p.inv_scale;
+            if ((long long)(j + 1) * C::BN <= p.Skv) {
+#pragma unroll
+              for (int c = 0; c < C::BN / 4; ++c) {
+                const float4 b4 = __ldg(reinterpret_cast<const float4*>(br) + c);
+                s[4 * c] += b4.x * isc;
+                s[4 * c + 1] += b4.y * isc;
+                s[4 * c + 2] += b4.z * isc;
+                s[4 * c + 3] += b4.w * isc;
+              }
+            } else {
+              const int nvalid = p.Skv - j * C::BN;
+#pragma unroll
+              for (int c = 0; c < C::BN; ++c)
+                if (c < nvalid) s[c] += __ldg(br + c) * isc;
+            }
           }
         }
         // row max: 3-input max, four independent chains

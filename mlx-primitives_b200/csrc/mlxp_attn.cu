@@ -451,14 +451,15 @@ int noalloc_scratch(void** out) {
   return MLXP_OK;
 }
 
-template <int D, bool BF16>
+template <int D, bool BF16, bool BIAS>
 struct TcKernel {
   static constexpr int NS = (D == 128) ? 2 : 3;  // K/V ring stages
   using Cfg = Sm100Cfg<D, NS>;
-  static constexpr unsigned kBit = 1u << ((D == 128 ? 0 : 1) + (BF16 ? 0 : 2));
+  // attribute-cache bits 0..7: (head_dim, element type, bias)
+  static constexpr unsigned kBit = 1u << ((D == 128 ? 0 : 1) + (BF16 ? 0 : 2) + (BIAS ? 4 : 0));
   static int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                     const CUtensorMap& mo, const FwdParams& p, cudaStream_t stream) {
-    auto kern = attn_fwd_sm100_kernel<D, BF16, NS>;
+    auto kern = attn_fwd_sm100_kernel<D, BF16, NS, BIAS>;
     if (int rc = ensure_smem_attr(kern, Cfg::SMEM_ALLOC, kBit)) return rc;
     const long long items = (long long)p.n_qblk * p.B * p.H * p.splits;
     if (items <= 0) return MLXP_OK;
@@ -480,12 +481,20 @@ struct TcKernel {
   }
 };
 
+template <bool BIAS>
+int launch_tc_t(int D, bool bf16, const CUtensorMap& mq, const CUtensorMap& mk,
+                const CUtensorMap& mv, const CUtensorMap& mo, const FwdParams& p, cudaStream_t s) {
+  if (D == 128) return bf16 ? TcKernel<128, true, BIAS>::launch(mq, mk, mv, mo, p, s)
+                            : TcKernel<128, false, BIAS>::launch(mq, mk, mv, mo, p, s);
+  return bf16 ? TcKernel<64, true, BIAS>::launch(mq, mk, mv, mo, p, s)
+              : TcKernel<64, false, BIAS>::launch(mq, mk, mv, mo, p, s);
+}
+// The bias (custom mask) variant is a separate instantiation: the default kernel's softmax
+// carries no trace of it.
 int launch_tc(int D, bool bf16, const CUtensorMap& mq, const CUtensorMap& mk,
               const CUtensorMap& mv, const CUtensorMap& mo, const FwdParams& p, cudaStream_t s) {
-  if (D == 128) return bf16 ? TcKernel<128, true>::launch(mq, mk, mv, mo, p, s)
-                            : TcKernel<128, false>::launch(mq, mk, mv, mo, p, s);
-  return bf16 ? TcKernel<64, true>::launch(mq, mk, mv, mo, p, s)
-              : TcKernel<64, false>::launch(mq, mk, mv, mo, p, s);
+  return p.bias != nullptr ? launch_tc_t<true>(D, bf16, mq, mk, mv, mo, p, s)
+                           : launch_tc_t<false>(D, bf16, mq, mk, mv, mo, p, s);
 }
 
 template <int D>
@@ -578,7 +587,8 @@ enum FwdMode { kOutNormal = 0, kOutPartial = 1, kOutAccumulate = 2 };
 int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* lse,
                   const Problem& pr, const int64_t* qs, const int64_t* ks, const int64_t* vs,
                   const int64_t* os, float scale, int64_t kv_splits, void* ws, size_t ws_bytes,
-                  int mode, cudaStream_t stream, const RopeArgs* rope = nullptr) {
+                  int mode, cudaStream_t stream, const RopeArgs* rope = nullptr,
+                  const float* bias = nullptr, const int64_t* bias_st = nullptr) {
   const bool out_f32 = mode != kOutNormal;
   const bool accumulate = mode == kOutAccumulate;
   if (int rc = validate(pr)) return rc;
@@ -592,6 +602,16 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
   const bool fp32 = pr.dtype == MLXP_DTYPE_FP32;
   if (out_f32 && fp32)
     return fail(MLXP_ERR_UNSUPPORTED, "partial and accumulating outputs take bf16/fp16 inputs");
+  if (bias != nullptr) {
+    // fp32, unit key stride, 16-byte aligned rows (the kernels read 4 keys at a time)
+    if (!bias_st || bias_st[3] != 1)
+      return fail(MLXP_ERR_INVALID, "mask: the key (last) stride must be 1");
+    if (reinterpret_cast<uintptr_t>(bias) % 16 || (bias_st[0] % 4) || (bias_st[1] % 4) ||
+        (bias_st[2] % 4) || bias_st[0] < 0 || bias_st[1] < 0 || bias_st[2] < 0)
+      return fail(MLXP_ERR_INVALID, "mask: base and (batch, head, row) strides must be 16-byte "
+                                    "aligned and non-negative");
+    if (out_f32 || rope) return fail(MLXP_ERR_UNSUPPORTED, "mask with this entry point");
+  }
   if (int rc = check_out_strides(o, os, (fp32 || out_f32) ? 4 : 8, "o")) return rc;
   if (reinterpret_cast<uintptr_t>(lse) % 4) return fail(MLXP_ERR_INVALID, "lse misaligned");
   if (pr.Sq == 0) return MLXP_OK;
@@ -628,6 +648,12 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
     p.lse = lse;
     p.scale_log2 = scale_log2;
     p.mask = mask_of(pr);
+    if (bias) {
+      p.bias = bias;
+      p.bias_sb = bias_st[0];
+      p.bias_sh = bias_st[1];
+      p.bias_sq = bias_st[2];
+    }
     int splits = 1;
     if (!out_f32) {
       if (kv_splits == 0) splits = choose_splits_f32(pr, sms);
@@ -756,6 +782,13 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
   p.n_groups = sched_groups(pr.B * pr.H, (long long)p.n_qblk * splits, sms);
   p.scale_log2 = scale_log2;
   p.mask = mask_of(pr);
+  if (bias) {
+    p.bias = bias;
+    p.bias_sb = bias_st[0];
+    p.bias_sh = bias_st[1];
+    p.bias_sq = bias_st[2];
+    p.inv_scale = 1.0f / scale;
+  }
   p.status = status;
   p.timeout_ns = g_timeout_ns.load();
   {
@@ -1275,6 +1308,23 @@ int mlxp_attn_fwd_partial(const void* q, const void* k, const void* v, float* o_
   return attn_fwd_impl(q, k, v, o_part, lse_part, pr, q_strides, k_strides, v_strides,
                        o_strides, scale, 1, nullptr, 0, kOutPartial,
                        static_cast<cudaStream_t>(cuda_stream));
+}
+
+int mlxp_attn_fwd_masked(const void* q, const void* k, const void* v, void* o, float* lse,
+                         int dtype, int64_t B, int64_t H, int64_t H_kv, int64_t Sq, int64_t Skv,
+                         int64_t D, const int64_t q_strides[4], const int64_t k_strides[4],
+                         const int64_t v_strides[4], const int64_t o_strides[4],
+                         const float* mask, const int64_t mask_strides[4], float scale,
+                         int causal, int64_t window_left, int64_t window_right,
+                         int64_t q_pos_offset, int64_t kv_pos_offset, int64_t kv_splits,
+                         void* workspace, size_t ws_bytes, void* cuda_stream) {
+  Problem pr{dtype, B, H, Sq, Skv, D, causal ? 1 : 0, window_left, window_right, q_pos_offset,
+             kv_pos_offset, H_kv};
+  if (H_kv < 1) return fail(MLXP_ERR_INVALID, "num_kv_heads must be >= 1");
+  if (mask == nullptr && Sq > 0 && Skv > 0) return fail(MLXP_ERR_INVALID, "mask is null");
+  return attn_fwd_impl(q, k, v, o, lse, pr, q_strides, k_strides, v_strides, o_strides, scale,
+                       kv_splits, workspace, ws_bytes, kOutNormal,
+                       static_cast<cudaStream_t>(cuda_stream), nullptr, mask, mask_strides);
 }
 
 int mlxp_attn_fwd_accumulate(const void* q, const void* k, const void* v, float* o_acc,

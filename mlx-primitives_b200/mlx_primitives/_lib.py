@@ -56,6 +56,10 @@ _SIGNATURES = {
         _p, _p, _p, _p, _p, ctypes.c_int, _i64, _i64, _i64, _i64, _i64,
         _i64x4, _i64x4, _i64x4, _i64x4, ctypes.c_float, ctypes.c_int, _i64, _i64, _i64, _i64,
         _p]),
+    "mlxp_attn_fwd_masked": (ctypes.c_int, [
+        _p, _p, _p, _p, _p, ctypes.c_int, _i64, _i64, _i64, _i64, _i64, _i64,
+        _i64x4, _i64x4, _i64x4, _i64x4, _p, _i64x4, ctypes.c_float, ctypes.c_int,
+        _i64, _i64, _i64, _i64, _i64, _p, ctypes.c_size_t, _p]),
     "mlxp_rope_attn_fwd": (ctypes.c_int, [
         _p, _p, _p, _p, _p, ctypes.c_int, _i64, _i64, _i64, _i64, _i64,
         _i64x4, _i64x4, _i64x4, _i64x4, _p, _p, _i64, _i64, _i64, ctypes.c_float, ctypes.c_int,

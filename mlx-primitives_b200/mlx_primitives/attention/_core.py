@@ -41,7 +41,8 @@ def _dims(t: torch.Tensor, layout: str):
 def attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, layout: str,
                       scale: float, causal: bool, window_left: int = -1, window_right: int = -1,
                       q_offset: int = 0, kv_offset: int = 0, kv_splits: int = 0,
-                      return_lse: bool = False, out: torch.Tensor | None = None):
+                      return_lse: bool = False, out: torch.Tensor | None = None,
+                      mask: torch.Tensor | None = None):
     """O = softmax(scale * Q K^T + mask) V for 4-D q/k/v in `layout` ("BSHD" or "BHSD").
 
     Masking is in absolute positions (qpos = i + q_offset, kpos = j + kv_offset): causal keeps
@@ -53,6 +54,10 @@ def attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, layo
     ``out`` (optional): a tensor of O's shape, dtype and layout, e.g. a slice of a larger
     output, that receives the result in place and is returned.
 
+    ``mask`` (optional): an additive score mask broadcastable to (B, H, Sq, Skv) — the custom
+    mask of the reference's gqa/mqa attention, added to scale * Q K^T (booleans count 0/1, as
+    in the reference's addition); -inf excludes a key.  Forward only.
+
     Differentiable: when autograd records and q, k or v requires grad, the backward runs the
     library's backward kernels (mlxp_attn_bwd) from the saved O and log-sum-exp.
     """
@@ -62,12 +67,41 @@ def attention_forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, layo
     if torch.is_grad_enabled() and any(t.requires_grad for t in (q, k, v)):
         if out is not None:
             raise ValueError("out= cannot be used while recording gradients")
+        if mask is not None:
+            raise NotImplementedError("gradients through a custom attention mask are not "
+                                      "supported (the backward kernels take causal/window masks)")
         if q.device.type != "cuda":
             raise NotImplementedError("attention gradients need CUDA tensors (host tensors are "
                                       "only staged for the forward)")
         out, lse = _AttentionFn.apply(q, k, v, kw)
         return (out, lse) if return_lse else out
-    return _forward_impl(q, k, v, return_lse=return_lse, out=out, **kw)
+    return _forward_impl(q, k, v, return_lse=return_lse, out=out, mask=mask, **kw)
+
+
+def _prepare_mask(mask, B: int, H: int, Sq: int, Skv: int, device) -> torch.Tensor:
+    """fp32 view of `mask` broadcast to (B, H, Sq, Skv) that the kernels can read: unit key
+    stride, rows and base on 16 bytes.  Broadcast dims stay stride 0 (a (Sq, Skv) mask is not
+    expanded over batch and heads); rows are padded to a multiple of 4 keys when needed."""
+    m = torch.as_tensor(mask, device=device)
+    m = m.to(torch.float32)
+    while m.dim() < 4:
+        m = m.unsqueeze(0)
+    if m.dim() != 4:
+        raise ValueError(f"mask must broadcast to (batch, heads, seq_q, seq_kv), got {tuple(m.shape)}")
+    try:
+        torch.broadcast_shapes(tuple(m.shape), (B, H, Sq, Skv))
+    except RuntimeError as e:
+        raise ValueError(f"mask of shape {tuple(mask.shape)} does not broadcast to "
+                         f"(batch, heads, seq_q, seq_kv) = {(B, H, Sq, Skv)}") from e
+    small = m.expand(*(s if s != 1 else 1 for s in m.shape))
+    ok = (small.stride(3) == 1 or small.shape[3] == 1) and small.data_ptr() % 16 == 0 and \
+        all(st % 4 == 0 for st, n in zip(small.stride()[:3], small.shape[:3]) if n > 1)
+    if not ok or small.shape[3] != Skv:
+        pad = -(-Skv // 4) * 4
+        buf = torch.zeros(tuple(small.shape[:3]) + (pad,), dtype=torch.float32, device=device)
+        buf[..., :Skv] = small
+        small = buf
+    return small.expand(B, H, Sq, small.shape[3])[..., :Skv]
 
 
 class _AttentionFn(torch.autograd.Function):
@@ -132,11 +166,27 @@ def attention_backward(q, k, v, out, lse, dout, *, layout: str, scale: float, ca
 def _forward_impl(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, layout: str,
                   scale: float, causal: bool, window_left: int = -1, window_right: int = -1,
                   q_offset: int = 0, kv_offset: int = 0, kv_splits: int = 0,
-                  return_lse: bool = False, out: torch.Tensor | None = None):
+                  return_lse: bool = False, out: torch.Tensor | None = None,
+                  mask: torch.Tensor | None = None):
     """The forward launch.  ``out``: a tensor of the output's shape, dtype and layout (any
     strides, e.g. a slice of a larger output) that receives the result; it is returned."""
     if q.dtype not in _lib.DTYPE_CODES:
         raise ValueError(f"unsupported dtype {q.dtype}; expected float32, bfloat16 or float16")
+    if q.device.type == "cpu" and mask is not None:
+        # host tensors with a mask: staged whole (the mask need not split by batch)
+        if not torch.cuda.is_available():
+            raise RuntimeError("attention requires a CUDA device (there is no CPU fallback)")
+        dev = torch.device("cuda", torch.cuda.current_device())
+        res = _forward_impl(*(t.to(dev, non_blocking=True) for t in (q, k, v)), layout=layout,
+                            scale=scale, causal=causal, window_left=window_left,
+                            window_right=window_right, q_offset=q_offset, kv_offset=kv_offset,
+                            kv_splits=kv_splits, return_lse=return_lse,
+                            mask=torch.as_tensor(mask).to(dev))
+        res = tuple(r.cpu() for r in res) if return_lse else res.cpu()
+        if out is None:
+            return res
+        out.copy_(res[0] if return_lse else res)
+        return (out, res[1]) if return_lse else out
     if q.device.type == "cpu":
         res = _host_attention(q, k, v, layout=layout, scale=scale, causal=causal,
                               window_left=window_left, window_right=window_right,
@@ -190,7 +240,14 @@ def _forward_impl(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, layout: 
                   ws.data_ptr() if ws is not None else None, ws_bytes,
                   _lib.stream_handle(q.device))
         lse_ptr = lse.data_ptr() if lse is not None else None
-        if Hkv == H:
+        if mask is not None:
+            mk = _prepare_mask(mask, B, H, Sq, Skv, q.device)
+            rc = L.mlxp_attn_fwd_masked(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                        lse_ptr, dt, B, H, Hkv, Sq, Skv, Dp, *common[:4],
+                                        mk.data_ptr(), (ctypes.c_int64 * 4)(*mk.stride()),
+                                        *common[4:])
+            what = "mlxp_attn_fwd_masked"
+        elif Hkv == H:
             rc = L.mlxp_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
                                  lse_ptr, dt, B, H, Sq, Skv, Dp, *common)
             what = "mlxp_attn_fwd"

@@ -8,10 +8,13 @@ here the attention kernel reads K/V head ``h // num_kv_groups`` for query head `
 (mlxp_attn_fwd_gqa), so the repeated K/V never exist.  Causal masking is bottom-right aligned
 (``triu(k=seq_kv - seq_q + 1)``), as in the reference.
 
-Differences, each where the reference has no equivalent on this path: a custom additive
-``mask`` raises ``NotImplementedError`` (the kernel has no dense-mask input and there is no CPU
-fallback); a query row with no admissible key (causal with seq_q > seq_kv) returns zeros where
-the reference's -inf mask would give NaN.
+A custom additive ``mask`` (broadcastable to (batch, heads, seq_q, seq_kv)) is added to the
+scores after the causal mask, as the reference does (grouped_query.py:253-254); the kernels
+read it tile by tile (mlxp_attn_fwd_masked), never as a repeated dense copy.  Where the
+reference has no defined result: a query row with no admissible key (causal with seq_q >
+seq_kv, or a mask of -inf across the row) returns zeros where the reference's -inf would give
+NaN.  Gradients through a custom mask are not supported (the backward kernels take causal and
+window masks).
 """
 
 from __future__ import annotations
@@ -29,10 +32,6 @@ __all__ = ["GroupedQueryAttention", "gqa_attention"]
 
 def _grouped_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                        scale: Optional[float], mask, causal: bool) -> torch.Tensor:
-    if mask is not None:
-        raise NotImplementedError(
-            "custom attention masks are not supported by the B200 kernels; use causal=True or "
-            "the sliding-window / chunked entry points")
     if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
         raise ValueError("q, k and v must be 4-D (batch, seq, heads, head_dim)")
     if k.shape != v.shape:
@@ -45,7 +44,7 @@ def _grouped_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         scale = 1.0 / math.sqrt(D)
     Sq, Skv = q.shape[1], k.shape[1]
     return attention_forward(q, k, v, layout="BSHD", scale=float(scale), causal=bool(causal),
-                             q_offset=(Skv - Sq) if causal else 0)
+                             q_offset=(Skv - Sq) if causal else 0, mask=mask)
 
 
 def gqa_attention(

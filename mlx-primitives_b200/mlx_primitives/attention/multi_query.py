@@ -3,8 +3,9 @@
 ``mqa_attention`` (multi_query.py:161-225) and ``MultiQueryAttention`` (multi_query.py:20-158):
 every query head shares one K/V head.  The reference broadcasts K/V to all heads; here the
 kernel reads the single K/V head for every query head (mlxp_attn_fwd_gqa with one K/V head).
-Causal masking is bottom-right aligned as in the reference; a custom ``mask`` raises
-``NotImplementedError`` and fully masked rows return zeros (see grouped_query.py).
+Causal masking is bottom-right aligned as in the reference; a custom additive ``mask`` is added
+to the scores (multi_query.py:218-219 of the reference) and fully masked rows return zeros
+(see grouped_query.py).
 """
 
 from __future__ import annotations

@@ -68,13 +68,16 @@ def create_sliding_window_mask(seq_len: int, window_size: int, causal: bool = Tr
 # ----------------------------------------------------------------------------------------
 def attention_bhsd(q, k, v, scale: float, causal: bool = False, window_left: int = -1,
                    window_right: int = -1, q_offset: int = 0, kv_offset: int = 0,
-                   dtype=np.float64, empty_rows: str = "zero", return_lse: bool = False):
+                   dtype=np.float64, empty_rows: str = "zero", return_lse: bool = False,
+                   bias=None):
     """softmax(scale * Q K^T + mask) V per (b, h) for BHSD arrays, computed in `dtype`.
 
     This is the reference's dense path (flash.py:186-192 / 479-525, sliding_window.py:514-560,
     chunked.py:172-203) with the mask given in absolute positions.  Rows with no admissible key:
     empty_rows="zero" gives O = 0 / LSE = -inf (the B200 library's definition); "mean" gives the
-    reference's finite-mask result mean(V) (every score replaced by -1e38).
+    reference's finite-mask result mean(V) (every score replaced by -1e38).  `bias`: an additive
+    score mask broadcastable to (B, H, Sq, Skv), added after scaling (grouped_query.py:253-254);
+    rows it leaves without a finite score count as empty.
     """
     q = np.asarray(q, dtype=dtype)
     k = np.asarray(k, dtype=dtype)
@@ -85,10 +88,16 @@ def attention_bhsd(q, k, v, scale: float, causal: bool = False, window_left: int
     empty = ~ok.any(axis=1)
     out = np.zeros((B, H, Sq, v.shape[3]), dtype=dtype)
     lse = np.full((B, H, Sq), -np.inf, dtype=np.float64)
+    if bias is not None:
+        bias = np.broadcast_to(np.asarray(bias, dtype=dtype), (B, H, Sq, Skv))
     for b in range(B):
         for h in range(H):
             s = (q[b, h] @ k[b, h].T) * scale
+            if bias is not None:
+                s = s + bias[b, h]
             s = np.where(ok, s, -np.inf)
+            if bias is not None:
+                empty = ~np.isfinite(s).any(axis=1)
             m = s.max(axis=1, keepdims=True)
             m = np.where(np.isfinite(m), m, 0.0)
             e = np.exp(s - m)
@@ -184,14 +193,21 @@ def gqa_attention(q, k, v, num_kv_groups, scale=None, mask=None, causal=False, d
     j*num_kv_groups .. (j+1)*num_kv_groups-1 (broadcast + reshape in the reference); causal
     aligned bottom-right (triu(k = seq_kv - seq_q + 1)).  Rows with no admissible key give 0
     (the library's convention; the reference's -inf mask would give NaN there)."""
-    if mask is not None:
-        raise NotImplementedError("custom masks are not part of the oracle")
     q, k, v = (np.asarray(t) for t in (q, k, v))
     if q.shape[2] != k.shape[2] * num_kv_groups:
         raise ValueError("num_heads must equal num_kv_heads * num_kv_groups")
     k = np.repeat(k, num_kv_groups, axis=2)
     v = np.repeat(v, num_kv_groups, axis=2)
-    return flash_attention(q, k, v, scale=scale, causal=causal, layout="BSHD", dtype=dtype)
+    if mask is None:
+        return flash_attention(q, k, v, scale=scale, causal=causal, layout="BSHD", dtype=dtype)
+    # custom additive mask (grouped_query.py:253-254): scores + causal mask + mask, softmax
+    Sq, Skv = q.shape[1], k.shape[1]
+    if scale is None:
+        scale = 1.0 / np.sqrt(q.shape[-1])
+    o = attention_bhsd(to_bhsd(q, "BSHD"), to_bhsd(k, "BSHD"), to_bhsd(v, "BSHD"), scale,
+                       causal=causal, q_offset=(Skv - Sq) if causal else 0, dtype=dtype,
+                       bias=mask)
+    return from_bhsd(o, "BSHD")
 
 
 def mqa_attention(q, k, v, scale=None, mask=None, causal=False, dtype=np.float64):

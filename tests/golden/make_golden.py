@@ -248,6 +248,23 @@ def main() -> None:
          lambda q, k, v: mq.mqa_attention(q, k, v, causal=True))
     case("mqa_3d_kv_noncausal_d128", 124, (1, 50, 3, 128), (1, 75, 1, 128),
          lambda q, k, v: mq.mqa_attention(q, k[:, :, 0], v[:, :, 0], causal=False))
+    # custom additive masks (grouped_query.py:253-254, multi_query.py:218-219), stored with the
+    # case as "<case>__mask": a (seq_q, seq_kv) bias, a (batch, 1, seq_q, seq_kv) exclusion mask
+    # (-inf entries, every row keeps a key) with causal masking, a per-head bias for mqa
+    rs = np.random.RandomState(7)
+    m1 = (rs.standard_normal((60, 90)) * 2.0).astype(np.float32)
+    out["gqa_mask_bias_g2_d64__mask"] = m1
+    case("gqa_mask_bias_g2_d64", 140, (2, 60, 4, 64), (2, 90, 2, 64),
+         lambda q, k, v: gq.gqa_attention(q, k, v, num_kv_groups=2, mask=m1))
+    m2 = np.where(rs.rand(2, 1, 48, 48) < 0.3, -np.inf, 0.0).astype(np.float32)
+    m2[..., np.arange(48), np.arange(48)] = 0.0  # the diagonal stays: no empty row under causal
+    out["gqa_mask_exclude_causal_d128__mask"] = m2
+    case("gqa_mask_exclude_causal_d128", 141, (2, 48, 6, 128), (2, 48, 3, 128),
+         lambda q, k, v: gq.gqa_attention(q, k, v, num_kv_groups=2, mask=m2, causal=True))
+    m3 = (rs.standard_normal((1, 3, 33, 70)) * 0.5).astype(np.float32)
+    out["mqa_mask_head_bias_d64__mask"] = m3
+    case("mqa_mask_head_bias_d64", 142, (1, 33, 3, 64), (1, 70, 1, 64),
+         lambda q, k, v: mq.mqa_attention(q, k, v, mask=m3))
 
     # RoPE (kernels/rope.py:223-255, 451-496) and RoPE + attention
     # (kernels/fused_rope_attention.py:766-800 via fused_rope_attention(use_metal=False))

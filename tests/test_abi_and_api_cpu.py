@@ -105,9 +105,6 @@ def test_grouped_query_validation():
 
     with pytest.raises(ValueError, match="num_kv_heads"):
         gqa_attention(_t(1, 4, 6, 8), _t(1, 4, 4, 8), _t(1, 4, 4, 8), num_kv_groups=2)
-    with pytest.raises(NotImplementedError, match="mask"):
-        gqa_attention(_t(1, 4, 4, 8), _t(1, 4, 2, 8), _t(1, 4, 2, 8), num_kv_groups=2,
-                      mask=_t(4, 4))
     with pytest.raises(ValueError, match="one K/V head"):
         mqa_attention(_t(1, 4, 4, 8), _t(1, 4, 2, 8), _t(1, 4, 2, 8))
     with pytest.raises(ValueError, match="divisible"):

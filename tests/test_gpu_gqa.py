@@ -12,7 +12,7 @@ from oracle import attention_oracle as O
 
 pytestmark = pytest.mark.gpu
 
-TOL = {torch.float32: 1e-4, torch.bfloat16: 2e-2}
+TOL = {torch.float32: 1e-4, torch.bfloat16: 2e-2, torch.float16: 2e-2}
 
 
 def _inputs(shape_q, shape_kv, dtype, seed):
@@ -99,3 +99,62 @@ def test_modules_match_projection_plus_oracle(cls):
     out1, cache1 = mod(x1, cache=cache)
     assert cache1[0].shape == (2, 151, Hkv, hd) and out1.shape == (2, 1, dims)
     assert torch.isfinite(out1).all()
+
+
+# --------------------------------------------------------------------- custom additive masks
+GOLDEN = np.load(__import__("pathlib").Path(__file__).parent / "golden" / "reference_outputs.npz")
+
+
+@pytest.mark.parametrize("case", ["gqa_mask_bias_g2_d64", "gqa_mask_exclude_causal_d128",
+                                  "mqa_mask_head_bias_d64"])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_custom_mask_matches_reference_golden(case, dtype):
+    """The reference's own gqa/mqa outputs with a custom mask (tests/golden): through the public
+    API on the GPU (fp32: the CUDA-core kernel, <= 1e-4 against the golden; bf16: the
+    tensor-core kernel's mask instantiation, <= 2e-2 against the oracle on the rounded inputs)."""
+    from mlx_primitives.attention import gqa_attention, mqa_attention
+
+    meta = GOLDEN[f"{case}__meta"]
+    seed, std = int(meta[0]), float(meta[1])
+    sq, skv = tuple(int(x) for x in meta[2:6]), tuple(int(x) for x in meta[6:10])
+    (q, k, v), (nq, nk, nv) = _inputs(sq, skv, dtype, seed)
+    mask = torch.from_numpy(GOLDEN[f"{case}__mask"]).cuda()
+    groups = sq[2] // skv[2]
+    causal = "causal" in case
+    if case.startswith("mqa"):
+        out = mqa_attention(q, k, v, mask=mask, causal=causal)
+    else:
+        out = gqa_attention(q, k, v, num_kv_groups=groups, mask=mask, causal=causal)
+    want = O.gqa_attention(nq, nk, nv, groups, mask=GOLDEN[f"{case}__mask"], causal=causal)
+    assert _maxabs(out, want) <= TOL[dtype]
+    if dtype == torch.float32:
+        assert _maxabs(out, GOLDEN[f"{case}__out"]) <= 1e-4
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("shape", ["SqSkv", "bhqk", "b1qk", "odd_keys"])
+def test_custom_mask_broadcast_forms(dtype, D, shape):
+    """Masks of every broadcast form, with key counts that are not multiples of 4 (rows padded
+    by the wrapper) and of the 128-key tile (the partial last tile), causal and windowed by the
+    kernel at the same time; -inf entries exclude keys; fully excluded rows give zeros."""
+    from mlx_primitives.attention._core import attention_forward
+
+    B, H, Hkv, Sq = 2, 4, 2, 200
+    Skv = 301 if shape == "odd_keys" else 260
+    (q, k, v), (nq, nk, nv) = _inputs((B, Sq, H, D), (B, Skv, Hkv, D), dtype, seed=D + Skv)
+    rs = np.random.RandomState(D)
+    mshape = {"SqSkv": (Sq, Skv), "bhqk": (B, H, Sq, Skv), "b1qk": (B, 1, Sq, Skv),
+              "odd_keys": (1, H, Sq, Skv)}[shape]
+    m = (rs.standard_normal(mshape) * 1.5).astype(np.float32)
+    m[rs.rand(*mshape) < 0.2] = -np.inf
+    m[..., 7, :] = -np.inf  # a row with no admissible key
+    out = attention_forward(q, k, v, layout="BSHD", scale=D ** -0.5, causal=True,
+                            q_offset=Skv - Sq, window_left=150, mask=torch.from_numpy(m).cuda())
+    kr, vr = (np.repeat(t, H // Hkv, axis=2) for t in (nk, nv))
+    want = O.from_bhsd(O.attention_bhsd(O.to_bhsd(nq, "BSHD"), O.to_bhsd(kr, "BSHD"),
+                                        O.to_bhsd(vr, "BSHD"), D ** -0.5, causal=True,
+                                        q_offset=Skv - Sq, window_left=150, bias=m), "BSHD")
+    tol = 1e-4 if dtype == torch.float32 else 2e-2
+    assert _maxabs(out, want) <= tol
+    assert torch.count_nonzero(out[:, 7]) == 0

@@ -57,6 +57,15 @@ SEMANTIC = {
     "mqa_causal_d64": (lambda q, k, v: O.mqa_attention(q, k, v, causal=True), None),
     "mqa_3d_kv_noncausal_d128": (
         lambda q, k, v: O.mqa_attention(q, k[:, :, 0], v[:, :, 0], causal=False), None),
+    "gqa_mask_bias_g2_d64": (
+        lambda q, k, v: O.gqa_attention(q, k, v, 2, mask=GOLDEN["gqa_mask_bias_g2_d64__mask"]),
+        None),
+    "gqa_mask_exclude_causal_d128": (
+        lambda q, k, v: O.gqa_attention(q, k, v, 2, causal=True,
+                                        mask=GOLDEN["gqa_mask_exclude_causal_d128__mask"]), None),
+    "mqa_mask_head_bias_d64": (
+        lambda q, k, v: O.mqa_attention(q, k, v, mask=GOLDEN["mqa_mask_head_bias_d64__mask"]),
+        None),
     "rope_only_offset7_d64": (
         lambda q, k, v: O.rope(q, *O.precompute_rope_cache(80, 64), offset=7), None),
     "fused_rope_causal_d64": (lambda q, k, v: O.fused_rope_attention(q, k, v, causal=True), None),
