@@ -172,10 +172,11 @@ struct WorkItem {
 
 // One work item, decoded identically by every role from its index (item_coords in
 // attn_common.cuh gives its unit, key split and query block).
+template <bool kRope>
 __device__ __forceinline__ WorkItem decode_item(const FwdParams& p, int idx, int BN) {
   WorkItem w;
   int bh, qb;
-  if (p.rope_items > 0) {
+  if constexpr (kRope) {
     item_coords_rope(p, idx, bh, w.split, qb, w.rot, w.grp);
   } else {
     item_coords(p, idx, bh, w.split, qb);
@@ -213,54 +214,73 @@ __device__ __forceinline__ WorkItem decode_item(const FwdParams& p, int idx, int
   return w;
 }
 
-// A rotation item, run by the 256 softmax threads: rows [chunk * 256, +256) of one unit's Q
-// or K, rotated with the half-split RoPE (rope_pair: the RoPE kernel's exact arithmetic) into
-// the contiguous copy that the tensor maps read.  Per thread 8 + 8 elements of one row at a
-// time (16-byte loads and stores), so a warp moves 4 whole rows (D = 128) together.
+// A rotation item, run by the 256 softmax threads: positions [chunk * kRopeRows, +kRopeRows)
+// of Q or K for every (batch, head) unit of one scheduling group, rotated with the half-split
+// RoPE (rope_pair: the RoPE kernel's exact arithmetic) into the contiguous copies that the
+// tensor maps read.  A thread owns (row, 8-element chunk pair) slots: it loads the slot's cos
+// and sin once and applies them to the group's units, whose loads it issues in batches of UB
+// before any store (the stores could alias the loads as far as the compiler knows, which would
+// otherwise serialise every unit on a full memory latency).
 template <int D, bool kBF16>
-__device__ __forceinline__ void rope_rotate_rows(const FwdParams& p, const WorkItem& w, int tid) {
+__device__ __forceinline__ void rope_rotate_group(const FwdParams& p, const WorkItem& w, int tid) {
   using T = std::conditional_t<kBF16, __nv_bfloat16, __half>;
   constexpr int CP = D / 16;  // chunk pairs (8 elements of each half) per row
+  constexpr int UB = 8;       // units whose loads are in flight together
   const bool isq = w.rot < p.rope_q_items;
   const int chunk = isq ? w.rot : w.rot - p.rope_q_items;
   const long long S = isq ? p.Sq : p.Skv;
-  const long long r0 = (long long)chunk * 256;
-  const int nrows = (int)(S - r0 < 256 ? S - r0 : 256);
+  const long long r0 = (long long)chunk * kRopeRows;
+  const int nrows = (int)(S - r0 < kRopeRows ? S - r0 : kRopeRows);
+  const int BH = p.B * p.H, base = BH / p.n_groups, n_big = BH % p.n_groups;
+  const int u0 = w.b * p.H + w.h;  // the group's first unit
+  const int u1 = u0 + base + (w.grp < n_big ? 1 : 0);
   const long long* st = isq ? p.rq_s : p.rk_s;
-  const T* src = static_cast<const T*>(isq ? p.rq_src : p.rk_src) + (long long)w.b * st[0] +
-                 (long long)w.h * st[1] + r0 * st[2];
-  T* dst = static_cast<T*>(isq ? p.rq_dst : p.rk_dst) +
-           (((long long)w.b * p.H + w.h) * S + r0) * D;
+  const T* __restrict__ srcb = static_cast<const T*>(isq ? p.rq_src : p.rk_src);
+  T* __restrict__ dstb = static_cast<T*>(isq ? p.rq_dst : p.rk_dst);
   const long long pos0 = (isq ? p.rope_q_pos : p.rope_k_pos) + r0;
-#pragma unroll 4
   for (int i = tid; i < nrows * CP; i += 256) {
     const int r = i / CP, j = i - r * CP;
-    const T* x = src + r * st[2] + 8 * j;
-    const uint4 v1 = *reinterpret_cast<const uint4*>(x);
-    const uint4 v2 = *reinterpret_cast<const uint4*>(x + D / 2);
     const float4* cr = reinterpret_cast<const float4*>(p.rope_cos + (pos0 + r) * (D / 2) + 8 * j);
     const float4* sr = reinterpret_cast<const float4*>(p.rope_sin + (pos0 + r) * (D / 2) + 8 * j);
     const float4 c0 = __ldg(cr), c1 = __ldg(cr + 1), s0 = __ldg(sr), s1 = __ldg(sr + 1);
-    const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-    const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-    const T* x1 = reinterpret_cast<const T*>(&v1);
-    const T* x2 = reinterpret_cast<const T*>(&v2);
-    uint4 o1, o2;
-    T* y1 = reinterpret_cast<T*>(&o1);
-    T* y2 = reinterpret_cast<T*>(&o2);
+    const float cc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const float ss[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    const long long row = r0 + r;
+    for (int u = u0; u < u1; u += UB) {
+      uint4 v1[UB], v2[UB];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      float a, b;
-      rope_pair(to_f<T>(x1[e]), to_f<T>(x2[e]), c[e], sn[e], a, b);
-      y1[e] = from_f<T>(a);
-      y2[e] = from_f<T>(b);
+      for (int k = 0; k < UB; ++k) {
+        if (u + k < u1) {
+          const int b = (u + k) / p.H, h = (u + k) - b * p.H;
+          const T* x = srcb + (long long)b * st[0] + (long long)h * st[1] + row * st[2] + 8 * j;
+          v1[k] = *reinterpret_cast<const uint4*>(x);
+          v2[k] = *reinterpret_cast<const uint4*>(x + D / 2);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < UB; ++k) {
+        if (u + k >= u1) continue;
+        const T* x1 = reinterpret_cast<const T*>(&v1[k]);
+        const T* x2 = reinterpret_cast<const T*>(&v2[k]);
+        uint4 o1, o2;
+        T* y1 = reinterpret_cast<T*>(&o1);
+        T* y2 = reinterpret_cast<T*>(&o2);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          float a, bb;
+          rope_pair(to_f<T>(x1[e]), to_f<T>(x2[e]), cc[e], ss[e], a, bb);
+          y1[e] = from_f<T>(a);
+          y2[e] = from_f<T>(bb);
+        }
+        T* y = dstb + ((long long)(u + k) * S + row) * D + 8 * j;
+        *reinterpret_cast<uint4*>(y) = o1;
+        *reinterpret_cast<uint4*>(y + D / 2) = o2;
+      }
     }
-    *reinterpret_cast<uint4*>(dst + r * D + 8 * j) = o1;
-    *reinterpret_cast<uint4*>(dst + r * D + D / 2 + 8 * j) = o2;
   }
 }
 
-template <int D, bool kBF16, int NS, bool kBias>
+template <int D, bool kBF16, int NS, bool kBias, bool kRope>
 __global__ void __launch_bounds__(384, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                           const __grid_constant__ CUtensorMap tm_k,
@@ -279,7 +299,7 @@ __global__ void __launch_bounds__(384, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n_items = p.n_qblk * p.B * p.H * p.splits + p.B * p.H * p.rope_items;
+  const int n_items = p.n_qblk * p.B * p.H * p.splits + (kRope ? p.n_groups * p.rope_items : 0);
 #if MLXP_TRACE
   if (threadIdx.x == 0 && blockIdx.x < 1024) g_mlxp_cta_life[blockIdx.x * 3] = (long long)global_timer_ns();
 #endif
@@ -341,20 +361,19 @@ __global__ void __launch_bounds__(384, 1)
           // critical path); later ones come from the counter, past the first gridDim.x.  With
           // rotation items every item comes from the counter: an item may wait for smaller
           // ones, which must then belong to CTAs that are running.
-          const int idx = p.rope_items > 0 ? (int)atomicAdd(p.work_counter, 1u)
-                          : item == 0      ? (int)blockIdx.x
-                                           : (int)(gridDim.x + atomicAdd(p.work_counter, 1u));
+          const int idx = kRope      ? (int)atomicAdd(p.work_counter, 1u)
+                          : item == 0 ? (int)blockIdx.x
+                                      : (int)(gridDim.x + atomicAdd(p.work_counter, 1u));
           work_slot[slot] = idx;
           MLXP_TR(true, 3, item, 1);
           mbar_arrive(BAR(C::B_WF + slot));  // release: the slot write is visible to waiters
           if (idx >= n_items) break;
-          const WorkItem w = decode_item(p, idx, C::BN);
+          const WorkItem w = decode_item<kRope>(p, idx, C::BN);
           if (w.hi <= w.lo) continue;  // rotation items and empty items load nothing
-          if (p.rope_items > 0 && w.grp > rot_ready) {
-            // Q and K of this group are rotated by other items: wait until all are done
-            const int base = p.B * p.H / p.n_groups, n_big = p.B * p.H % p.n_groups;
-            // two arrivals (one per softmax warpgroup) per rotation item
-            const unsigned need = (unsigned)((base + (w.grp < n_big ? 1 : 0)) * p.rope_items * 2);
+          if (kRope && w.grp > rot_ready) {
+            // Q and K of this group are rotated by other items: wait until all are done (two
+            // arrivals, one per softmax warpgroup, per rotation item)
+            const unsigned need = (unsigned)(p.rope_items * 2);
             ok = wait_count_geq(p.rot_done + w.grp, need, wctx, kSiteRope);
             if (!ok) break;
             fence_proxy_async_global();  // the rotated rows, written by generic stores, for TMA
@@ -465,7 +484,7 @@ __global__ void __launch_bounds__(384, 1)
           const int idx = work_slot[slot];
           mbar_arrive(BAR(C::B_WE + slot));
           if (idx >= n_items) break;
-          const WorkItem w = decode_item(p, idx, C::BN);
+          const WorkItem w = decode_item<kRope>(p, idx, C::BN);
           if (w.hi <= w.lo) continue;
           // One tile's share of key tile j: PV_t(j) once P_t(j) is ready, then QK_t(j+1).
           // The K of key tile j+1 is fill c+1 (ring stage ksn).
@@ -570,13 +589,26 @@ __global__ void __launch_bounds__(384, 1)
       const int idx = work_slot[slot];
       mbar_arrive(BAR(C::B_WE + slot));
       if (idx >= n_items) break;
-      const WorkItem w = decode_item(p, idx, C::BN);
-      if (w.rot >= 0) {
+      const WorkItem w = decode_item<kRope>(p, idx, C::BN);
+      if (kRope && w.rot >= 0) {
         // rotation item: both warpgroups rotate their share of the rows, then each counts
         // itself done for the group (release: its rows are visible at device scope, to
         // generic and async-proxy readers, first).  Each warpgroup syncs only its own 128
         // threads, which all reach the barrier: the other may have left on an abort.
-        rope_rotate_rows<D, kBF16>(p, w, (int)threadIdx.x);
+#if MLXP_TRACE
+        const long long tr0 = (long long)global_timer_ns();
+#endif
+        rope_rotate_group<D, kBF16>(p, w, (int)threadIdx.x);
+#if MLXP_TRACE
+        if (threadIdx.x == 0 && idx < 8192) {
+          uint32_t smid;
+          asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+          g_mlxp_cta_trace[idx * 4 + 0] = tr0;
+          g_mlxp_cta_trace[idx * 4 + 1] = (long long)global_timer_ns();
+          g_mlxp_cta_trace[idx * 4 + 2] = smid;
+          g_mlxp_cta_trace[idx * 4 + 3] = 0;
+        }
+#endif
         fence_proxy_async_global();
         __threadfence();
         named_bar_sync(1 + t, 128);

@@ -64,7 +64,7 @@ int* g_status_ptr[kMaxDevices] = {};
 unsigned* g_counter_ptr[kMaxDevices] = {};
 std::atomic<unsigned> g_counter_seq[kMaxDevices];
 int g_num_sms[kMaxDevices] = {};
-unsigned g_attr_done[kMaxDevices] = {};
+unsigned long long g_attr_done[kMaxDevices] = {};
 
 int current_device(int& dev) {
   cudaError_t e = cudaGetDevice(&dev);
@@ -99,7 +99,7 @@ int device_info(int** status, int* sms) {
 
 // Sets the dynamic shared memory limit of a kernel once per device.
 template <typename K>
-int ensure_smem_attr(K kernel, int bytes, unsigned bit) {
+int ensure_smem_attr(K kernel, int bytes, unsigned long long bit) {
   int dev;
   if (int rc = current_device(dev)) return rc;
   {
@@ -451,15 +451,16 @@ int noalloc_scratch(void** out) {
   return MLXP_OK;
 }
 
-template <int D, bool BF16, bool BIAS>
+template <int D, bool BF16, bool BIAS, bool ROPE>
 struct TcKernel {
   static constexpr int NS = (D == 128) ? 2 : 3;  // K/V ring stages
   using Cfg = Sm100Cfg<D, NS>;
-  // attribute-cache bits 0..7: (head_dim, element type, bias)
-  static constexpr unsigned kBit = 1u << ((D == 128 ? 0 : 1) + (BF16 ? 0 : 2) + (BIAS ? 4 : 0));
+  // attribute-cache bits 32..43: (head_dim, element type) x (plain, bias, RoPE)
+  static constexpr unsigned long long kBit =
+      1ull << (32 + (D == 128 ? 0 : 1) + (BF16 ? 0 : 2) + 4 * (BIAS ? 1 : ROPE ? 2 : 0));
   static int launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                     const CUtensorMap& mo, const FwdParams& p, cudaStream_t stream) {
-    auto kern = attn_fwd_sm100_kernel<D, BF16, NS, BIAS>;
+    auto kern = attn_fwd_sm100_kernel<D, BF16, NS, BIAS, ROPE>;
     if (int rc = ensure_smem_attr(kern, Cfg::SMEM_ALLOC, kBit)) return rc;
     const long long items = (long long)p.n_qblk * p.B * p.H * p.splits;
     if (items <= 0) return MLXP_OK;
@@ -481,20 +482,21 @@ struct TcKernel {
   }
 };
 
-template <bool BIAS>
+template <bool BIAS, bool ROPE>
 int launch_tc_t(int D, bool bf16, const CUtensorMap& mq, const CUtensorMap& mk,
                 const CUtensorMap& mv, const CUtensorMap& mo, const FwdParams& p, cudaStream_t s) {
-  if (D == 128) return bf16 ? TcKernel<128, true, BIAS>::launch(mq, mk, mv, mo, p, s)
-                            : TcKernel<128, false, BIAS>::launch(mq, mk, mv, mo, p, s);
-  return bf16 ? TcKernel<64, true, BIAS>::launch(mq, mk, mv, mo, p, s)
-              : TcKernel<64, false, BIAS>::launch(mq, mk, mv, mo, p, s);
+  if (D == 128) return bf16 ? TcKernel<128, true, BIAS, ROPE>::launch(mq, mk, mv, mo, p, s)
+                            : TcKernel<128, false, BIAS, ROPE>::launch(mq, mk, mv, mo, p, s);
+  return bf16 ? TcKernel<64, true, BIAS, ROPE>::launch(mq, mk, mv, mo, p, s)
+              : TcKernel<64, false, BIAS, ROPE>::launch(mq, mk, mv, mo, p, s);
 }
-// The bias (custom mask) variant is a separate instantiation: the default kernel's softmax
-// carries no trace of it.
+// The bias (custom mask) and RoPE variants are separate instantiations: the default kernel
+// carries no trace of either.
 int launch_tc(int D, bool bf16, const CUtensorMap& mq, const CUtensorMap& mk,
               const CUtensorMap& mv, const CUtensorMap& mo, const FwdParams& p, cudaStream_t s) {
-  return p.bias != nullptr ? launch_tc_t<true>(D, bf16, mq, mk, mv, mo, p, s)
-                           : launch_tc_t<false>(D, bf16, mq, mk, mv, mo, p, s);
+  if (p.bias != nullptr) return launch_tc_t<true, false>(D, bf16, mq, mk, mv, mo, p, s);
+  if (p.rope_items > 0) return launch_tc_t<false, true>(D, bf16, mq, mk, mv, mo, p, s);
+  return launch_tc_t<false, false>(D, bf16, mq, mk, mv, mo, p, s);
 }
 
 template <int D>
@@ -739,8 +741,8 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
     p.rope_sin = rope->sinc;
     p.rope_q_pos = rope->q_pos;
     p.rope_k_pos = rope->k_pos;
-    p.rope_q_items = (int)((pr.Sq + 255) / 256);
-    p.rope_items = p.rope_q_items + (int)((pr.Skv + 255) / 256);
+    p.rope_q_items = (int)((pr.Sq + kRopeRows - 1) / kRopeRows);
+    p.rope_items = p.rope_q_items + (int)((pr.Skv + kRopeRows - 1) / kRopeRows);
     const int64_t qc[4] = {pr.H * pr.Sq * pr.D, pr.Sq * pr.D, pr.D, 1};
     const int64_t kc[4] = {pr.H * pr.Skv * pr.D, pr.Skv * pr.D, pr.D, 1};
     std::memcpy(rq_st, qc, sizeof(qc));

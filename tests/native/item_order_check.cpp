@@ -59,7 +59,7 @@ int main(int argc, char** argv) {
         break;
       }
   }
-  // With RoPE rotation items: every rotation item (unit, chunk) and attention item (unit,
+  // With RoPE rotation items: every rotation item (group, chunk) and attention item (unit,
   // split, query block) exactly once, each in its unit's group, and every attention item after
   // the last rotation item of its group.
   for (int trial = 0; trial < trials; ++trial) {
@@ -76,7 +76,7 @@ int main(int argc, char** argv) {
     auto group_of = [&](int bh) {
       return bh < n_big * (base + 1) ? bh / (base + 1) : n_big + (bh - n_big * (base + 1)) / base;
     };
-    const int n_att = p.n_qblk * BH * p.splits, n_rot = BH * p.rope_items;
+    const int n_att = p.n_qblk * BH * p.splits, n_rot = p.n_groups * p.rope_items;
     std::vector<int> seen_a((size_t)n_att, 0), seen_r((size_t)n_rot, 0);
     std::vector<int> last_rot(p.n_groups, -1), first_att(p.n_groups, 1 << 30);
     for (int idx = 0; idx < n_att + n_rot; ++idx) {
@@ -88,7 +88,9 @@ int main(int argc, char** argv) {
       }
       if (rot >= 0) {
         if (rot >= p.rope_items) { report("rope: chunk out of range", trial); continue; }
-        seen_r[(size_t)bh * p.rope_items + rot]++;
+        if (bh != (grp < n_big ? grp * (base + 1) : n_big * (base + 1) + (grp - n_big) * base))
+          report("rope: rotation item not at its group's first unit", trial);
+        seen_r[(size_t)grp * p.rope_items + rot]++;
         last_rot[grp] = idx > last_rot[grp] ? idx : last_rot[grp];
       } else {
         if (split < 0 || split >= p.splits || qb < 0 || qb >= p.n_qblk) {

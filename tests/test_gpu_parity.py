@@ -297,6 +297,11 @@ GOLDEN_CALLS = {
     "gqa_g2_causal_kv_longer_d64": ("gqa", dict(num_kv_groups=2, scale=0.2, causal=True)),
     "mqa_causal_d64": ("mqa", dict(causal=True)),
     "mqa_3d_kv_noncausal_d128": ("mqa3d", dict(causal=False)),
+    # custom additive masks, stored with the case ("<case>__mask")
+    "gqa_mask_bias_g2_d64": ("gqa", dict(num_kv_groups=2, mask_case="gqa_mask_bias_g2_d64")),
+    "gqa_mask_exclude_causal_d128": ("gqa", dict(num_kv_groups=2, causal=True,
+                                                 mask_case="gqa_mask_exclude_causal_d128")),
+    "mqa_mask_head_bias_d64": ("mqa", dict(mask_case="mqa_mask_head_bias_d64")),
     "rope_only_offset7_d64": ("rope", dict(offset=7)),
     "fused_rope_causal_d64": ("frope", dict(causal=True)),
     "fused_rope_offsets_noncausal_d128": ("frope", dict(q_offset=30, kv_offset=0, causal=False)),
@@ -345,6 +350,10 @@ def _call(api, mod, q, k, v, kw):
         return fused_rope_attention(q, k, v, **kw)
     if api in ("gqa", "mqa", "mqa3d"):
         m = getattr(mod, "attention", mod)  # the package keeps them in mlx_primitives.attention
+        if "mask_case" in kw:
+            kw = dict(kw)
+            mask = _golden()[f"{kw.pop('mask_case')}__mask"]
+            kw["mask"] = mask if mod is O else torch.from_numpy(mask).cuda()
         if api == "gqa":
             return m.gqa_attention(q, k, v, **kw)
         if api == "mqa3d":

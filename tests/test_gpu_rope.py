@@ -122,8 +122,10 @@ def test_rope_attention_single_launch_is_the_two_launch_result(dtype, D, shape, 
     """mlxp_rope_attn_fwd (rotation items inside the attention launch) against mlxp_rope_qk +
     attention: bit-identical (same rotation arithmetic and rounding, same attention kernel),
     and within the bf16/fp16 tolerance of the oracle's rope + attention."""
-    import mlx_primitives.kernels.fused_rope_attention as M
+    import importlib
+
     from mlx_primitives.kernels import fused_rope_attention, precompute_rope_cache
+    M = importlib.import_module("mlx_primitives.kernels.fused_rope_attention")
 
     B, Sq, H = shape[:3]
     Skv = shape[3] if len(shape) > 3 else Sq
