@@ -161,14 +161,12 @@ struct FwdParams {
   long long acc_sb, acc_sh, acc_ss;
   // RoPE in the same launch (rope_items > 0): besides its attention items every scheduling
   // group has rope_items rotation items — chunks of kRopeRows positions of Q (the first
-  // rope_q_items)
-  // and of K, each over every (batch, head) unit of the group, so that a thread loads the
-  // cos/sin of its positions once for all the group's heads — which rotate the rows (the
-  // half-split rotation of the RoPE kernel, rounded once to the element type) into contiguous
-  // BHSD copies that the Q and K tensor maps read.  Rotation items of scheduling group g+1 are
-  // handed out before the attention items of group g (see item_coords_rope); the TMA producer
-  // waits for rot_done[g] == 2 x rope_items (each item is counted by both softmax warpgroups)
-  // before loading a group-g item's Q and K.
+  // rope_q_items) and of K, each over every (batch, head) unit of the group, so that a thread
+  // loads the cos/sin of its positions once for all the group's heads — which rotate the rows
+  // (the half-split rotation of the RoPE kernel, rounded once to the element type) into
+  // contiguous BHSD copies that the Q and K tensor maps read.  The rotation items come first
+  // (see item_coords_rope); the TMA producer waits for rot_done[g] == 2 x rope_items (each item
+  // is counted by both softmax warpgroups) before loading a group-g item's Q and K.
   int rope_items, rope_q_items;
   const void* rq_src;
   const void* rk_src;
@@ -278,62 +276,31 @@ __host__ __device__ inline void item_coords(const FwdParams& p, int idx, int& bh
 // Positions per RoPE rotation item (FwdParams::rope_items counts chunks of this many rows).
 constexpr int kRopeRows = 128;
 
-// Item order with RoPE rotation items (rope_items > 0).  Group g's rotation items R_g
-// (rope_items of them) and attention items A_g (in item_coords' order inside the group) are
-// laid out as  R_0 | R_1 A_0 | R_2 A_1 | ... | R_{G-1} A_{G-2} | A_{G-1}:  every attention item
-// comes after all rotation items of its group, and every item depends only on items with
-// smaller indices, so a persistent grid that hands items out in index order always has one it
-// can finish.  Returns rot = -1 for an attention item (bh, split, qb set), otherwise the
-// rotation chunk (bh = the group's first unit); grp = the item's scheduling group either way.
+// Item order with RoPE rotation items (rope_items > 0): all rotation items first, group by
+// group (R_0 | R_1 | ... | R_{G-1}), then the attention items in item_coords' order.  Rotation
+// is memory-bound streaming, which one SM alone does at a fraction of its share of HBM
+// bandwidth but all SMs together do at close to the full rate, so it runs as a first phase;
+// an attention item waits only for its own group's rotation, so the first groups' attention
+// overlaps the end of that phase.  Every item depends only on items with smaller indices, so a
+// persistent grid that hands items out in index order always has one it can finish.  Returns
+// rot = -1 for an attention item (bh, split, qb set), otherwise the rotation chunk (bh = the
+// group's first unit); grp = the item's scheduling group either way.
 __host__ __device__ inline void item_coords_rope(const FwdParams& p, int idx, int& bh, int& split,
                                                  int& qb, int& rot, int& grp) {
   const int BH = p.B * p.H, G = p.n_groups;
   const int base = BH / G, n_big = BH % G;
-  const long long rpg = p.rope_items, apu = (long long)p.n_qblk * p.splits;
-  auto cum = [&](long long n) -> long long { return n * base + (n < n_big ? n : n_big); };
-  auto gsz = [&](long long g) -> long long { return base + (g < n_big ? 1 : 0); };
-  const long long r0 = rpg;
-  // start of segment g (1 <= g <= G): R_g A_{g-1} for g < G, the final A_{G-1} for g = G
-  auto start = [&](long long g) -> long long { return r0 + rpg * (g - 1) + apu * cum(g - 1); };
-  split = 0;
-  qb = 0;
-  if (idx < r0) {
-    grp = 0;
-    bh = 0;
-    rot = idx;
+  const int n_rot = G * p.rope_items;
+  if (idx < n_rot) {
+    grp = idx / p.rope_items;
+    rot = idx - grp * p.rope_items;
+    bh = grp * base + (grp < n_big ? grp : n_big);
+    split = 0;
+    qb = 0;
     return;
   }
-  long long lo = 1, hi = G;  // largest g in [1, G] with start(g) <= idx
-  while (lo < hi) {
-    const long long mid = (lo + hi + 1) / 2;
-    if (start(mid) <= idx) lo = mid;
-    else hi = mid - 1;
-  }
-  const long long g = lo;
-  long long local = idx - start(g);
-  if (g < G && local < rpg) {  // rotation item of group g
-    grp = (int)g;
-    bh = (int)cum(g);
-    rot = (int)local;
-    return;
-  }
-  if (g < G) local -= rpg;
-  // attention item of group g - 1
-  grp = (int)(g - 1);
   rot = -1;
-  const long long g0 = cum(g - 1), gs = gsz(g - 1);
-  if (p.heavy_first) {
-    const long long qrank = local / (gs * p.splits);
-    const long long rem = local - qrank * gs * p.splits;
-    bh = (int)(g0 + rem / p.splits);
-    split = (int)(rem % p.splits);
-    qb = p.n_qblk - 1 - (int)qrank;
-  } else {
-    bh = (int)(g0 + local / apu);
-    const long long rem = local % apu;
-    split = (int)(rem / p.n_qblk);
-    qb = (int)(rem % p.n_qblk);
-  }
+  item_coords(p, idx - n_rot, bh, split, qb);
+  grp = bh < n_big * (base + 1) ? bh / (base + 1) : n_big + (bh - n_big * (base + 1)) / base;
 }
 
 }  // namespace mlxp
