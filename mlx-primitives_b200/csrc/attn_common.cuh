@@ -164,9 +164,9 @@ struct FwdParams {
   // rope_q_items) and of K, each over every (batch, head) unit of the group, so that a thread
   // loads the cos/sin of its positions once for all the group's heads — which rotate the rows
   // (the half-split rotation of the RoPE kernel, rounded once to the element type) into
-  // contiguous BHSD copies that the Q and K tensor maps read.  The rotation items come first
-  // (see item_coords_rope); the TMA producer waits for rot_done[g] == 2 x rope_items (each item
-  // is counted by both softmax warpgroups) before loading a group-g item's Q and K.
+  // contiguous BHSD copies that the Q and K tensor maps read.  They run as a first phase of
+  // the kernel, by all threads of every CTA, before the warp roles split; the TMA producer
+  // waits for rot_done[g] == rope_items before loading a group-g item's Q and K.
   int rope_items, rope_q_items;
   const void* rq_src;
   const void* rk_src;
@@ -177,6 +177,7 @@ struct FwdParams {
   const float* rope_sin;        // fp32 [n_pos][D/2]
   long long rope_q_pos, rope_k_pos;  // position of row 0 of q and of k
   unsigned* rot_done;           // per scheduling group, zero at launch
+  unsigned* rot_counter;        // next rotation item of the RoPE phase, zero at launch
   // Additive score bias (the custom mask of gqa_attention / mqa_attention), fp32, element
   // strides (batch, head, query row) — 0 for broadcast dims — and unit stride along keys:
   // scores become scale * q.k + bias[b][h][i][j] before the softmax.  Only the kernel
@@ -275,32 +276,5 @@ __host__ __device__ inline void item_coords(const FwdParams& p, int idx, int& bh
 
 // Positions per RoPE rotation item (FwdParams::rope_items counts chunks of this many rows).
 constexpr int kRopeRows = 128;
-
-// Item order with RoPE rotation items (rope_items > 0): all rotation items first, group by
-// group (R_0 | R_1 | ... | R_{G-1}), then the attention items in item_coords' order.  Rotation
-// is memory-bound streaming, which one SM alone does at a fraction of its share of HBM
-// bandwidth but all SMs together do at close to the full rate, so it runs as a first phase;
-// an attention item waits only for its own group's rotation, so the first groups' attention
-// overlaps the end of that phase.  Every item depends only on items with smaller indices, so a
-// persistent grid that hands items out in index order always has one it can finish.  Returns
-// rot = -1 for an attention item (bh, split, qb set), otherwise the rotation chunk (bh = the
-// group's first unit); grp = the item's scheduling group either way.
-__host__ __device__ inline void item_coords_rope(const FwdParams& p, int idx, int& bh, int& split,
-                                                 int& qb, int& rot, int& grp) {
-  const int BH = p.B * p.H, G = p.n_groups;
-  const int base = BH / G, n_big = BH % G;
-  const int n_rot = G * p.rope_items;
-  if (idx < n_rot) {
-    grp = idx / p.rope_items;
-    rot = idx - grp * p.rope_items;
-    bh = grp * base + (grp < n_big ? grp : n_big);
-    split = 0;
-    qb = 0;
-    return;
-  }
-  rot = -1;
-  item_coords(p, idx - n_rot, bh, split, qb);
-  grp = bh < n_big * (base + 1) ? bh / (base + 1) : n_big + (bh - n_big * (base + 1)) / base;
-}
 
 }  // namespace mlxp

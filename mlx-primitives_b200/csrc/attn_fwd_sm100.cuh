@@ -52,6 +52,7 @@ namespace mlxp {
 __device__ long long g_mlxp_trace[4 * 64 * 8];
 __device__ long long g_mlxp_cta_trace[8192 * 4];  // per item: start ns, end ns, SM id, key tiles
 __device__ long long g_mlxp_cta_life[1024 * 3];   // per CTA: entry ns, prologue done ns, exit ns
+__device__ long long g_mlxp_rot_trace[2048 * 3];  // per rotation item: start ns, end ns, SM id
 #define MLXP_TR(cond, role, it, k)                                                    \
   do {                                                                                \
     if ((cond) && blockIdx.x == 0 && (it) < 64)                                       \
@@ -96,9 +97,10 @@ struct Sm100Cfg {
   static constexpr int B_WE = B_WF + 2;    // 2: work-item slot read by every consumer
   static constexpr int B_DR = B_WE + 2;    // 1: MMA drain
   static constexpr int NBAR = B_DR + 1;
-  // tmem slot, abort flag, 2 item slots, 2 per-tile "merge the key splits" flags
+  // tmem slot, abort flag, 2 item slots, 2 per-tile "merge the key splits" flags, 2 slots of
+  // the RoPE phase's item counter
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
-  static constexpr int SMEM_BYTES = OFF_MISC + 24;
+  static constexpr int SMEM_BYTES = OFF_MISC + 32;
   static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024 B
   // Three warpgroups: WG0/WG1 softmax (tiles 0/1), WG2 = MMA warp, TMA warp, two spare warps.
   // Registers are split per SM sub-partition, so the launch gets 65536/384 -> 168 per thread
@@ -176,20 +178,15 @@ template <bool kRope>
 __device__ __forceinline__ WorkItem decode_item(const FwdParams& p, int idx, int BN) {
   WorkItem w;
   int bh, qb;
-  if constexpr (kRope) {
-    item_coords_rope(p, idx, bh, w.split, qb, w.rot, w.grp);
-  } else {
-    item_coords(p, idx, bh, w.split, qb);
-    w.rot = -1;
-    w.grp = 0;
+  item_coords(p, idx, bh, w.split, qb);
+  w.rot = -1;
+  w.grp = 0;
+  if constexpr (kRope) {  // the scheduling group, whose rotation the item waits for
+    const int base = p.B * p.H / p.n_groups, n_big = p.B * p.H % p.n_groups;
+    w.grp = bh < n_big * (base + 1) ? bh / (base + 1) : n_big + (bh - n_big * (base + 1)) / base;
   }
   w.h = bh % p.H;
   w.b = bh / p.H;
-  if (w.rot >= 0) {  // a rotation item: no query block, no key range
-    w.q0 = 0;
-    w.lo0 = w.hi0 = w.lo1 = w.hi1 = w.lo = w.hi = 0;
-    return w;
-  }
   w.q0 = qb * 256;
   int lo_t[2], hi_t[2];
 #pragma unroll
@@ -214,14 +211,14 @@ __device__ __forceinline__ WorkItem decode_item(const FwdParams& p, int idx, int
   return w;
 }
 
-// A rotation item, run by the 256 softmax threads: positions [chunk * kRopeRows, +kRopeRows)
+// A rotation item, run by all NT threads of the CTA: positions [chunk * kRopeRows, +kRopeRows)
 // of Q or K for every (batch, head) unit of one scheduling group, rotated with the half-split
 // RoPE (rope_pair: the RoPE kernel's exact arithmetic) into the contiguous copies that the
 // tensor maps read.  A thread owns (row, 8-element chunk pair) slots: it loads the slot's cos
 // and sin once and applies them to the group's units, whose loads it issues in batches of UB
 // before any store (the stores could alias the loads as far as the compiler knows, which would
 // otherwise serialise every unit on a full memory latency).
-template <int D, bool kBF16>
+template <int D, bool kBF16, int NT>
 __device__ __forceinline__ void rope_rotate_group(const FwdParams& p, const WorkItem& w, int tid) {
   using T = std::conditional_t<kBF16, __nv_bfloat16, __half>;
   constexpr int CP = D / 16;  // chunk pairs (8 elements of each half) per row
@@ -238,7 +235,7 @@ __device__ __forceinline__ void rope_rotate_group(const FwdParams& p, const Work
   const T* __restrict__ srcb = static_cast<const T*>(isq ? p.rq_src : p.rk_src);
   T* __restrict__ dstb = static_cast<T*>(isq ? p.rq_dst : p.rk_dst);
   const long long pos0 = (isq ? p.rope_q_pos : p.rope_k_pos) + r0;
-  for (int i = tid; i < nrows * CP; i += 256) {
+  for (int i = tid; i < nrows * CP; i += NT) {
     const int r = i / CP, j = i - r * CP;
     const float4* cr = reinterpret_cast<const float4*>(p.rope_cos + (pos0 + r) * (D / 2) + 8 * j);
     const float4* sr = reinterpret_cast<const float4*>(p.rope_sin + (pos0 + r) * (D / 2) + 8 * j);
@@ -295,11 +292,12 @@ __global__ void __launch_bounds__(384, 1)
   int* abort_flag = reinterpret_cast<int*>(smem + C::OFF_MISC + 4);
   volatile int* work_slot = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8);
   volatile int* merge_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 16);
+  // (RoPE phase: two more slots after merge_flag, work_slot + 4 and + 5)
   auto BAR = [&](int i) -> uint32_t { return sbase + C::OFF_BAR + 8 * i; };
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n_items = p.n_qblk * p.B * p.H * p.splits + (kRope ? p.n_groups * p.rope_items : 0);
+  const int n_items = p.n_qblk * p.B * p.H * p.splits;
 #if MLXP_TRACE
   if (threadIdx.x == 0 && blockIdx.x < 1024) g_mlxp_cta_life[blockIdx.x * 3] = (long long)global_timer_ns();
 #endif
@@ -335,6 +333,48 @@ __global__ void __launch_bounds__(384, 1)
 #if MLXP_TRACE
   if (threadIdx.x == 0 && blockIdx.x < 1024) g_mlxp_cta_life[blockIdx.x * 3 + 1] = (long long)global_timer_ns();
 #endif
+  if constexpr (kRope) {
+    // RoPE phase, before the warp roles split (and rebalance their registers): all threads
+    // claim rotation items from their own counter until none is left, then count each one
+    // done for its group.  Rotation never waits for anything, so the attention items that
+    // wait for it (producer, below) always see it finish.
+    volatile int* rot_slot = work_slot + 4;  // merge_flag[2] sits at work_slot + 2
+    const int n_rot = p.n_groups * p.rope_items;
+    for (int round = 0;; ++round) {
+      if (threadIdx.x == 0) rot_slot[round & 1] = (int)atomicAdd(p.rot_counter, 1u);
+      __syncthreads();
+      const int r = rot_slot[round & 1];
+      if (r >= n_rot) break;
+      WorkItem w;
+      w.grp = r / p.rope_items;
+      w.rot = r - w.grp * p.rope_items;
+      {
+        const int base = p.B * p.H / p.n_groups, n_big = p.B * p.H % p.n_groups;
+        const int u0 = w.grp * base + (w.grp < n_big ? w.grp : n_big);
+        w.b = u0 / p.H;
+        w.h = u0 - w.b * p.H;
+      }
+#if MLXP_TRACE
+      const long long tr0 = (long long)global_timer_ns();
+#endif
+      rope_rotate_group<D, kBF16, C::THREADS>(p, w, (int)threadIdx.x);
+      fence_proxy_async_global();
+      __threadfence();
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        atomicAdd(p.rot_done + w.grp, 1u);
+#if MLXP_TRACE
+        if (r < 2048) {
+          uint32_t smid;
+          asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+          g_mlxp_rot_trace[r * 3 + 0] = tr0;
+          g_mlxp_rot_trace[r * 3 + 1] = (long long)global_timer_ns();
+          g_mlxp_rot_trace[r * 3 + 2] = smid;
+        }
+#endif
+      }
+    }
+  }
 
   if (warp >= 8) {
     // ================================ control warpgroup ================================
@@ -361,9 +401,8 @@ __global__ void __launch_bounds__(384, 1)
           // critical path); later ones come from the counter, past the first gridDim.x.  With
           // rotation items every item comes from the counter: an item may wait for smaller
           // ones, which must then belong to CTAs that are running.
-          const int idx = kRope      ? (int)atomicAdd(p.work_counter, 1u)
-                          : item == 0 ? (int)blockIdx.x
-                                      : (int)(gridDim.x + atomicAdd(p.work_counter, 1u));
+          const int idx = item == 0 ? (int)blockIdx.x
+                                    : (int)(gridDim.x + atomicAdd(p.work_counter, 1u));
           work_slot[slot] = idx;
           MLXP_TR(true, 3, item, 1);
           mbar_arrive(BAR(C::B_WF + slot));  // release: the slot write is visible to waiters
@@ -371,9 +410,9 @@ __global__ void __launch_bounds__(384, 1)
           const WorkItem w = decode_item<kRope>(p, idx, C::BN);
           if (w.hi <= w.lo) continue;  // rotation items and empty items load nothing
           if (kRope && w.grp > rot_ready) {
-            // Q and K of this group are rotated by other items: wait until all are done (two
-            // arrivals, one per softmax warpgroup, per rotation item)
-            const unsigned need = (unsigned)(p.rope_items * 2);
+            // Q and K of this group are rotated by the RoPE phase of this and other CTAs: wait
+            // until all of the group's rotation items are done
+            const unsigned need = (unsigned)p.rope_items;
             ok = wait_count_geq(p.rot_done + w.grp, need, wctx, kSiteRope);
             if (!ok) break;
             fence_proxy_async_global();  // the rotated rows, written by generic stores, for TMA
@@ -590,31 +629,6 @@ __global__ void __launch_bounds__(384, 1)
       mbar_arrive(BAR(C::B_WE + slot));
       if (idx >= n_items) break;
       const WorkItem w = decode_item<kRope>(p, idx, C::BN);
-      if (kRope && w.rot >= 0) {
-        // rotation item: both warpgroups rotate their share of the rows, then each counts
-        // itself done for the group (release: its rows are visible at device scope, to
-        // generic and async-proxy readers, first).  Each warpgroup syncs only its own 128
-        // threads, which all reach the barrier: the other may have left on an abort.
-#if MLXP_TRACE
-        const long long tr0 = (long long)global_timer_ns();
-#endif
-        rope_rotate_group<D, kBF16>(p, w, (int)threadIdx.x);
-#if MLXP_TRACE
-        if (threadIdx.x == 0 && idx < 8192) {
-          uint32_t smid;
-          asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-          g_mlxp_cta_trace[idx * 4 + 0] = tr0;
-          g_mlxp_cta_trace[idx * 4 + 1] = (long long)global_timer_ns();
-          g_mlxp_cta_trace[idx * 4 + 2] = smid;
-          g_mlxp_cta_trace[idx * 4 + 3] = 0;
-        }
-#endif
-        fence_proxy_async_global();
-        __threadfence();
-        named_bar_sync(1 + t, 128);
-        if (wq == 0 && lane == 0) atomicAdd(p.rot_done + w.grp, 1u);
-        continue;
-      }
       const int tlo = t ? w.lo1 : w.lo0, thi = t ? w.hi1 : w.hi0;
       const int qrow = w.q0 + t * 128 + row;
       const long long r0 = w.q0 + t * 128;

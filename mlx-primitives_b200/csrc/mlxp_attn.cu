@@ -576,7 +576,7 @@ struct RopeLayout {
 RopeLayout rope_layout(const Problem& pr) {
   auto up = [](size_t x) { return (x + 255) / 256 * 256; };
   RopeLayout l;
-  l.cnt_bytes = up((size_t)pr.B * pr.H * 4);
+  l.cnt_bytes = up((size_t)pr.B * pr.H * 4 + 4);  // per-group counters + the item counter
   l.q_bytes = up((size_t)pr.B * pr.H * pr.Sq * pr.D * 2);
   l.k_bytes = up((size_t)pr.B * pr.H * pr.Skv * pr.D * 2);
   return l;
@@ -729,6 +729,7 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
       return fail(MLXP_ERR_INVALID, "workspace must be 256-byte aligned");
     char* base = static_cast<char*>(ws);
     p.rot_done = reinterpret_cast<unsigned*>(base);
+    p.rot_counter = p.rot_done + pr.B * pr.H;  // one past the per-group counters
     p.rq_dst = base + rlay.cnt_bytes;
     p.rk_dst = base + rlay.cnt_bytes + rlay.q_bytes;
     p.rq_src = q;
@@ -1706,6 +1707,11 @@ int mlxp_cta_life_read(long long* dst, int n) {
   const int cap = 1024 * 3;
   cudaError_t e = cudaMemcpyFromSymbol(dst, g_mlxp_cta_life, sizeof(long long) * (n < cap ? n : cap));
   return e == cudaSuccess ? MLXP_OK : cuda_fail(e, "cta life read");
+}
+int mlxp_rot_trace_read(long long* dst, int n) {
+  const int cap = 2048 * 3;
+  cudaError_t e = cudaMemcpyFromSymbol(dst, g_mlxp_rot_trace, sizeof(long long) * (n < cap ? n : cap));
+  return e == cudaSuccess ? MLXP_OK : cuda_fail(e, "rot trace read");
 }
 int mlxp_cta_trace_read(long long* dst, int n) {
   const int cap = 8192 * 4;

@@ -59,53 +59,6 @@ int main(int argc, char** argv) {
         break;
       }
   }
-  // With RoPE rotation items: every rotation item (group, chunk) and attention item (unit,
-  // split, query block) exactly once, each in its unit's group, and every attention item after
-  // the last rotation item of its group.
-  for (int trial = 0; trial < trials; ++trial) {
-    FwdParams p{};
-    p.B = 1 + (int)(g() % 5);
-    p.H = 1 + (int)(g() % 40);
-    p.n_qblk = 1 + (int)(g() % 12);
-    p.splits = (g() % 3 == 0) ? 1 + (int)(g() % 3) : 1;
-    p.heavy_first = (int)(g() % 2);
-    p.rope_items = 1 + (int)(g() % 20);
-    const int BH = p.B * p.H;
-    p.n_groups = 1 + (int)(g() % BH);
-    const int base = BH / p.n_groups, n_big = BH % p.n_groups;
-    auto group_of = [&](int bh) {
-      return bh < n_big * (base + 1) ? bh / (base + 1) : n_big + (bh - n_big * (base + 1)) / base;
-    };
-    const int n_att = p.n_qblk * BH * p.splits, n_rot = p.n_groups * p.rope_items;
-    std::vector<int> seen_a((size_t)n_att, 0), seen_r((size_t)n_rot, 0);
-    std::vector<int> last_rot(p.n_groups, -1), first_att(p.n_groups, 1 << 30);
-    for (int idx = 0; idx < n_att + n_rot; ++idx) {
-      int bh, split, qb, rot, grp;
-      item_coords_rope(p, idx, bh, split, qb, rot, grp);
-      if (bh < 0 || bh >= BH || grp != group_of(bh)) {
-        report("rope: unit out of range or in the wrong group", trial);
-        continue;
-      }
-      if (rot >= 0) {
-        if (rot >= p.rope_items) { report("rope: chunk out of range", trial); continue; }
-        if (bh != (grp < n_big ? grp * (base + 1) : n_big * (base + 1) + (grp - n_big) * base))
-          report("rope: rotation item not at its group's first unit", trial);
-        seen_r[(size_t)grp * p.rope_items + rot]++;
-        last_rot[grp] = idx > last_rot[grp] ? idx : last_rot[grp];
-      } else {
-        if (split < 0 || split >= p.splits || qb < 0 || qb >= p.n_qblk) {
-          report("rope: attention coordinates out of range", trial);
-          continue;
-        }
-        seen_a[((size_t)bh * p.splits + split) * p.n_qblk + qb]++;
-        first_att[grp] = idx < first_att[grp] ? idx : first_att[grp];
-      }
-    }
-    for (int c : seen_a) if (c != 1) { report("rope: attention item not produced once", trial); break; }
-    for (int c : seen_r) if (c != 1) { report("rope: rotation item not produced once", trial); break; }
-    for (int gi = 0; gi < p.n_groups; ++gi)
-      if (first_att[gi] < last_rot[gi]) report("rope: attention before its group's rotation", trial);
-  }
   printf("%lld violations\n", bad);
   return bad ? 1 : 0;
 }
