@@ -83,6 +83,11 @@ CONFIGS = {
     "p4": dict(workload="paged_attention decode bf16, 8 sequences x 4096 cached tokens, block 16",
                api="paged", dtype="bf16", layout="BSHD", B=8, H=32, S=1, Skv=4096, D=128,
                block=16, causal=True, window=-1, std=1.0),
+    # config 5's kernel on a profilable slice (2 of its 32 heads, the full 128K sequence): the
+    # case ncu summaries of the long-context kernel are taken on; not a BASELINE config
+    "c5s": dict(workload="flash_attention bf16 BHSD causal, 2 heads x 131072 tokens (config-5 slice)",
+                api="flash", dtype="bf16", layout="BHSD", B=1, H=2, S=131072, Skv=131072, D=128,
+                causal=True, window=-1, std=1.0),
     # total work fixed: one 128K-token sequence, sequence-parallel ring over the N GPUs
     "c5": dict(workload="long-context flash_attention bf16 BHSD causal, zig-zag ring (config 5)",
                api="ring", dtype="bf16", layout="BHSD", B=1, H=32, S=131072, Skv=131072,
