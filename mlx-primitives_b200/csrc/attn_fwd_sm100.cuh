@@ -84,13 +84,16 @@ struct Sm100Cfg {
   // barrier indices
   static constexpr int B_QF = 0;           // Q loaded
   static constexpr int B_QE = 1;           // Q buffer free (last QK of the item done)
-  // K and V of one key tile share a ring stage: K and V each have a "loaded" barrier, and one
-  // "free" barrier per stage is committed once both have been consumed (one tcgen05.commit per
-  // key tile instead of two: commits interleaved with the MMA stream are not free).
+  // K and V have rings of NS stages each, with a "loaded" and a "free" barrier per stage.  K of
+  // key tile j is last read by the QKs issued one step before V of tile j is read, so K's stage
+  // is released as soon as those QKs complete: the load of K(j + NS) then has about a whole step
+  // more lead than when K and V of a tile were released together (measured: QK waited 0.5-1.4 K
+  // cycles per key tile for its K with the shared release).
   static constexpr int B_KF = 2;
   static constexpr int B_VF = B_KF + NS;
-  static constexpr int B_E = B_VF + NS;
-  static constexpr int B_SF = B_E + NS;    // 2: S_t ready
+  static constexpr int B_KE = B_VF + NS;
+  static constexpr int B_VE = B_KE + NS;
+  static constexpr int B_SF = B_VE + NS;   // 2: S_t ready
   static constexpr int B_PF = B_SF + 2;    // 2: P_t ready (128 arrivals)
   static constexpr int B_OF = B_PF + 2;    // 2: last PV_t of an item complete
   static constexpr int B_WF = B_OF + 2;    // 2: work-item slot filled
@@ -308,7 +311,8 @@ __global__ void __launch_bounds__(384, 1)
     for (int i = 0; i < NS; ++i) {
       mbar_init(BAR(C::B_KF + i), 1);
       mbar_init(BAR(C::B_VF + i), 1);
-      mbar_init(BAR(C::B_E + i), 1);
+      mbar_init(BAR(C::B_KE + i), 1);
+      mbar_init(BAR(C::B_VE + i), 1);
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(BAR(C::B_SF + t), 1);
@@ -387,7 +391,8 @@ __global__ void __launch_bounds__(384, 1)
         tma_prefetch_desc(&tm_v);
         tma_prefetch_desc(&tm_o);
         const uint32_t sQ = sbase + C::OFF_Q, sK = sbase + C::OFF_K, sV = sbase + C::OFF_V;
-        int fk = 0, n_q = 0;  // key-tile fills (K and V) and Q loads issued so far
+        int fk = 0, n_q = 0;  // key-tile fills (K) and Q loads issued so far
+        int fv = 0;           // V fills issued (fk, or fk - 1 after an abort between K and V)
         int rot_ready = -1;   // scheduling groups up to this one have their Q and K rotated
         bool ok = true;
         for (int item = 0; ok; ++item) {
@@ -446,7 +451,7 @@ __global__ void __launch_bounds__(384, 1)
           ++n_q;
           for (int j = w.lo; j < w.hi && ok; ++j) {
             const int ks = fk % NS;
-            if (fk >= NS) ok = mbar_wait(BAR(C::B_E + ks), ((fk / NS) - 1) & 1, wctx, kSiteProducer);
+            if (fk >= NS) ok = mbar_wait(BAR(C::B_KE + ks), ((fk / NS) - 1) & 1, wctx, kSiteProducer);
             if (!ok) break;
             mbar_arrive_expect_tx(BAR(C::B_KF + ks), C::KV_TILE);
             tma_coords(p.ck, j * C::BN, w.h / p.kv_group, w.b, c1, c2, c3);
@@ -454,6 +459,11 @@ __global__ void __launch_bounds__(384, 1)
             for (int kb = 0; kb < C::KB; ++kb)
               tma_load_4d(sK + ks * C::KV_TILE + kb * C::BOX_KV, &tm_k, BAR(C::B_KF + ks),
                           kb * 64, c1, c2, c3);
+            if (fk >= NS) ok = mbar_wait(BAR(C::B_VE + ks), ((fk / NS) - 1) & 1, wctx, kSiteProducer);
+            if (!ok) {
+              ++fk;  // K of this fill is in flight (its V is not): the abort path waits for it
+              break;
+            }
             mbar_arrive_expect_tx(BAR(C::B_VF + ks), C::KV_TILE);
             tma_coords(p.cv, j * C::BN, w.h / p.kv_group, w.b, c1, c2, c3);
 #pragma unroll
@@ -463,15 +473,18 @@ __global__ void __launch_bounds__(384, 1)
             MLXP_TR(j == w.lo, 3, item, 3);
             MLXP_TR(j == w.hi - 1, 3, item, 4);
             ++fk;
+            ++fv;
           }
         }
         if (!ok) {
           // Abort: let every load already issued land before the CTA releases its smem.
           if (n_q > 0) mbar_wait_drain(BAR(C::B_QF), (n_q - 1) & 1, p.status, p.timeout_ns);
-          for (int f = (fk > NS ? fk - NS : 0); f < fk; ++f) {
+          // the last NS fills of each ring are the latest of their stages (older ones landed
+          // before their stage was waited free)
+          for (int f = (fk > NS ? fk - NS : 0); f < fk; ++f)
             mbar_wait_drain(BAR(C::B_KF + f % NS), (f / NS) & 1, p.status, p.timeout_ns);
+          for (int f = (fv > NS ? fv - NS : 0); f < fv; ++f)
             mbar_wait_drain(BAR(C::B_VF + f % NS), (f / NS) & 1, p.status, p.timeout_ns);
-          }
         }
       }
     } else if (warp == 8) {
@@ -525,10 +538,9 @@ __global__ void __launch_bounds__(384, 1)
           if (idx >= n_items) break;
           const WorkItem w = decode_item<kRope>(p, idx, C::BN);
           if (w.hi <= w.lo) continue;
-          // One tile's share of key tile j: PV_t(j) once P_t(j) is ready, then QK_t(j+1).
-          // The K of key tile j+1 is fill c+1 (ring stage ksn).
-          auto tile_step = [&](auto tile, int j, int vs, bool has_next, int ksn,
-                               bool& k_ready) -> bool {
+          // One tile's share of key tile j: PV_t(j) once P_t(j) is ready (tile_pv), then QK_t(j+1)
+          // (tile_qk).  The K of key tile j+1 is fill c+1 (ring stage ksn).
+          auto tile_pv = [&](auto tile, int j, int vs) -> bool {
             constexpr int T = decltype(tile)::value;
             const int tlo = T ? w.lo1 : w.lo0, thi = T ? w.hi1 : w.hi0;
             int& pc = T ? pc1 : pc0;
@@ -540,6 +552,11 @@ __global__ void __launch_bounds__(384, 1)
               issue_pv(tile, vs, j > tlo);
               if (j == thi - 1) tc_commit(BAR(C::B_OF + T));
             }
+            return true;
+          };
+          auto tile_qk = [&](auto tile, int j, bool has_next, int ksn, bool& k_ready) -> bool {
+            constexpr int T = decltype(tile)::value;
+            const int tlo = T ? w.lo1 : w.lo0, thi = T ? w.hi1 : w.hi0;
             if (has_next && j + 1 >= tlo && j + 1 < thi) {
               if (!k_ready) {
                 if (!mbar_wait(BAR(C::B_KF + ksn), ((c + 1) / NS) & 1, wctx, kSiteMmaLoad))
@@ -569,6 +586,7 @@ __global__ void __launch_bounds__(384, 1)
             issue_qk(T1{}, c % NS);
             tc_commit(BAR(C::B_SF + 1));
           }
+          tc_commit(BAR(C::B_KE + c % NS));  // K(lo) is consumed
           if (w.hi - w.lo == 1) tc_commit(BAR(C::B_QE));  // every QK of this item is issued
           for (int j = w.lo; j < w.hi && ok; ++j, ++trace_f, ++c) {
             const int vs = c % NS;
@@ -580,18 +598,22 @@ __global__ void __launch_bounds__(384, 1)
             MLXP_TR(true, 2, trace_f, 1);
             if (!ok) break;
             tc_fence_after();
-            ok = tile_step(T0{}, j, vs, has_next, ksn, k_ready);
-            if (ok) ok = tile_step(T1{}, j, vs, has_next, ksn, k_ready);
+            ok = tile_pv(T0{}, j, vs);
+            if (ok) ok = tile_qk(T0{}, j, has_next, ksn, k_ready);
+            if (ok) ok = tile_pv(T1{}, j, vs);
             if (!ok) break;
-            if (has_next && !k_ready) {
-              // neither tile uses key tile j+1: its K load must still land before the stage
-              // is released at the end of the next iteration
-              ok = mbar_wait(BAR(C::B_KF + ksn), ((c + 1) / NS) & 1, wctx, kSiteMmaLoad);
-              if (!ok) break;
+            tc_commit(BAR(C::B_VE + vs));  // V(j) is consumed
+            ok = tile_qk(T1{}, j, has_next, ksn, k_ready);
+            if (!ok) break;
+            if (has_next) {
+              if (!k_ready) {
+                // neither tile uses key tile j+1: its K load must still land before the stage
+                // is released
+                ok = mbar_wait(BAR(C::B_KF + ksn), ((c + 1) / NS) & 1, wctx, kSiteMmaLoad);
+                if (!ok) break;
+              }
+              tc_commit(BAR(C::B_KE + ksn));  // K(j+1) is consumed: every QK(j+1) is issued
             }
-            // K(j) (last read by QK(j), one iteration ago) and V(j) (read by PV(j) above) are
-            // consumed: release their stage with a single commit.
-            tc_commit(BAR(C::B_E + vs));
             if (j + 2 == w.hi) tc_commit(BAR(C::B_QE));  // the item's last QKs are issued
           }
         }
