@@ -527,6 +527,7 @@ __global__ void __launch_bounds__(384, 1)
         using T0 = std::integral_constant<int, 0>;
         using T1 = std::integral_constant<int, 1>;
         int c = 0, n_q = 0, pc0 = 0, pc1 = 0;  // consumed key-tile fills, Q loads, P waits
+        int ke_pending = -1;  // K ring stage whose release commit is still to be issued
         int trace_f = 0;
         bool ok = true;
         for (int item = 0; ok; ++item) {
@@ -586,7 +587,7 @@ __global__ void __launch_bounds__(384, 1)
             issue_qk(T1{}, c % NS);
             tc_commit(BAR(C::B_SF + 1));
           }
-          tc_commit(BAR(C::B_KE + c % NS));  // K(lo) is consumed
+          ke_pending = c % NS;  // K(lo) is consumed once these QKs complete
           if (w.hi - w.lo == 1) tc_commit(BAR(C::B_QE));  // every QK of this item is issued
           for (int j = w.lo; j < w.hi && ok; ++j, ++trace_f, ++c) {
             const int vs = c % NS;
@@ -595,28 +596,32 @@ __global__ void __launch_bounds__(384, 1)
             bool k_ready = false;
             MLXP_TR(true, 2, trace_f, 0);
             ok = mbar_wait(BAR(C::B_VF + vs), (c / NS) & 1, wctx, kSiteMmaLoad);
+            // K(j+1) too, here rather than between PV_0(j) and QK_0(j+1): a wait in the MMA
+            // thread leaves the tensor pipe idle for its duration when few MMAs are queued
+            if (ok && has_next) {
+              ok = mbar_wait(BAR(C::B_KF + ksn), ((c + 1) / NS) & 1, wctx, kSiteMmaLoad);
+              k_ready = true;
+            }
             MLXP_TR(true, 2, trace_f, 1);
             if (!ok) break;
             tc_fence_after();
             ok = tile_pv(T0{}, j, vs);
+            if (ke_pending >= 0) {
+              // the previous step's K release, issued behind PV_0(j) where the MMA queue is full
+              tc_commit(BAR(C::B_KE + ke_pending));
+              ke_pending = -1;
+            }
             if (ok) ok = tile_qk(T0{}, j, has_next, ksn, k_ready);
             if (ok) ok = tile_pv(T1{}, j, vs);
             if (!ok) break;
             tc_commit(BAR(C::B_VE + vs));  // V(j) is consumed
             ok = tile_qk(T1{}, j, has_next, ksn, k_ready);
             if (!ok) break;
-            if (has_next) {
-              if (!k_ready) {
-                // neither tile uses key tile j+1: its K load must still land before the stage
-                // is released
-                ok = mbar_wait(BAR(C::B_KF + ksn), ((c + 1) / NS) & 1, wctx, kSiteMmaLoad);
-                if (!ok) break;
-              }
-              tc_commit(BAR(C::B_KE + ksn));  // K(j+1) is consumed: every QK(j+1) is issued
-            }
+            if (has_next) ke_pending = ksn;  // K(j+1) is consumed: every QK(j+1) is issued
             if (j + 2 == w.hi) tc_commit(BAR(C::B_QE));  // the item's last QKs are issued
           }
         }
+        if (ke_pending >= 0) tc_commit(BAR(C::B_KE + ke_pending));
         // Every MMA issued by this thread must finish before TMEM/smem are released.
         tc_commit(BAR(C::B_DR));
         mbar_wait_drain(BAR(C::B_DR), 0, p.status, p.timeout_ns);
