@@ -469,16 +469,6 @@ __global__ void __launch_bounds__(384, 1)
 #endif
           int c1, c2, c3;
           const bool a0 = w.hi0 > w.lo0, a1 = w.hi1 > w.lo1;
-#if MLXP_Q_PREFETCH
-          // The Q buffer frees only when the current item's last QKs complete; warm L2 with this
-          // item's Q rows now so that the load issued then is served from L2, not DRAM.
-          for (int t = 0; t < 2; ++t) {
-            if (!(t ? a1 : a0)) continue;
-            tma_coords(p.cq, w.q0 + t * 128, w.h, w.b, c1, c2, c3);
-#pragma unroll
-            for (int kb = 0; kb < C::KB; ++kb) tma_prefetch_l2_4d(&tm_q, kb * 64, c1, c2, c3);
-          }
-#endif
           if (n_q > 0) {
             ok = mbar_wait(BAR(C::B_QE), (n_q - 1) & 1, wctx, kSiteProducer);
             if (!ok) break;
