@@ -221,9 +221,16 @@ struct FwdParamsF32 {
   float scale_log2;
   MaskSpec mask;
   // Key splits: CTA (query block, split) covers its share of the block's key tiles and writes
-  // a normalised partial at o + split * o_split, lse + split * lse_split (merged afterwards).
+  // a normalised partial at o + split * o_split, lse + split * lse_split, then adds one to its
+  // query block's counter (blk_cnt[query block], zero at launch); the split that completes the
+  // count merges the block's partials (LSE weights) into o_final / lse_final (nullable) and
+  // resets the counter.
   int splits;
   long long o_split, lse_split;
+  unsigned* blk_cnt;
+  float* o_final;
+  long long of_sb, of_sh, of_ss;
+  float* lse_final;
   // additive score bias (nullable), as FwdParams::bias
   const float* bias;
   long long bias_sb, bias_sh, bias_sq;

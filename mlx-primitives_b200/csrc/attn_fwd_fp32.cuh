@@ -10,7 +10,9 @@
 // head dimension.  Shared-memory operands are read as 16-byte vectors (4 head-dim elements of
 // Q and K per load, 4 keys of P per load, EPT consecutive columns of V), so a thread does
 // 64 FMAs per 8 vector loads instead of 16 per 8 scalar ones.  Row reductions are 16-lane
-// shuffles (the 16 threads of a row group share a warp).
+// shuffles (the 16 threads of a row group share a warp).  K and V tiles are double-buffered:
+// tile j+1 is copied with cp.async while tile j is computed.  Key splits (several CTAs per query
+// block) are merged by the split that finishes last, in the same launch.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -31,7 +33,8 @@ struct F32Cfg {
   static constexpr int SK = D + 4;     // K pitch: rows of different tx lanes 16 bytes apart mod 128
   static constexpr int SV = D;
   static constexpr int SP = BN + 4;    // P pitch (16-byte aligned rows)
-  static constexpr int SMEM_FLOATS = BM * SQ + BN * SK + BN * SV + BM * SP;
+  static constexpr int KV_FLOATS = BN * SK + BN * SV;  // one stage of K and V
+  static constexpr int SMEM_FLOATS = BM * SQ + 2 * KV_FLOATS + BM * SP;
   static constexpr int SMEM_BYTES = SMEM_FLOATS * 4;
   static_assert(D % 32 == 0 && D <= 128, "head_dim 32, 64 or 128");
 };
@@ -55,18 +58,27 @@ __global__ void __launch_bounds__(256) attn_fwd_fp32_kernel(const FwdParamsF32 p
   using C = F32Cfg<D>;
   extern __shared__ __align__(16) float fsm[];
   float* Qs = fsm;
-  float* Ks = Qs + C::BM * C::SQ;
-  float* Vs = Ks + C::BN * C::SK;
-  float* Ps = Vs + C::BN * C::SV;
+  float* KVs = Qs + C::BM * C::SQ;  // [2][K tile, V tile]
+  float* Ps = KVs + 2 * C::KV_FLOATS;
 
   const int tid = threadIdx.x;
   const int ty = tid >> 4, tx = tid & 15;
   const int n_qblk = (p.Sq + C::BM - 1) / C::BM;
   const int split = blockIdx.x % p.splits;
   const int blk = blockIdx.x / p.splits;
-  const int bh = blk / n_qblk;
-  int qb = blk - bh * n_qblk;
-  if (p.mask.causal) qb = n_qblk - 1 - qb;  // heaviest first
+  // causal: query blocks heaviest first across all (batch, head) units (longest-processing-time
+  // order, so that the last wave holds the lightest blocks); otherwise unit-major, so that the
+  // blocks reading the same K/V run side by side
+  int bh, qb;
+  if (p.mask.causal) {
+    const int BH = p.B * p.H;
+    const int qrank = blk / BH;
+    bh = blk - qrank * BH;
+    qb = n_qblk - 1 - qrank;
+  } else {
+    bh = blk / n_qblk;
+    qb = blk - bh * n_qblk;
+  }
   const int h = bh % p.H, b = bh / p.H;
   const int q0 = qb * C::BM;
 
@@ -104,20 +116,36 @@ __global__ void __launch_bounds__(256) attn_fwd_fp32_kernel(const FwdParamsF32 p
   }
   const float sl2 = p.scale_log2;
 
-  for (int jt = tlo; jt < thi; ++jt) {
+  // K and V of key tile jt into stage buf (rows past Skv are zero-filled; their source address
+  // stays row 0, which exists whenever the kernel runs)
+  auto load_kv = [&](int jt, int buf) {
     const int c0 = jt * C::BN;
-    __syncthreads();  // previous tile fully consumed (and Q stored, first time)
+    float* Kb = KVs + buf * C::KV_FLOATS;
+    float* Vb = Kb + C::BN * C::SK;
     for (int i = tid; i < C::BN * (D / 4); i += 256) {
       const int r = i / (D / 4), c4 = i % (D / 4);
-      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-      if (c0 + r < p.Skv) {
-        kv = *reinterpret_cast<const float4*>(kg + (long long)(c0 + r) * p.k_ss + c4 * 4);
-        vv = *reinterpret_cast<const float4*>(vg + (long long)(c0 + r) * p.v_ss + c4 * 4);
-      }
-      *reinterpret_cast<float4*>(Ks + r * C::SK + c4 * 4) = kv;
-      *reinterpret_cast<float4*>(Vs + r * C::SV + c4 * 4) = vv;
+      const bool in = c0 + r < p.Skv;
+      const long long row = in ? c0 + r : 0;
+      cp_async_piece<16>(smem_u32(Kb + r * C::SK + c4 * 4), kg + row * p.k_ss + c4 * 4, in ? 16 : 0);
+      cp_async_piece<16>(smem_u32(Vb + r * C::SV + c4 * 4), vg + row * p.v_ss + c4 * 4, in ? 16 : 0);
     }
-    __syncthreads();
+    cp_async_commit();
+  };
+  if (tlo < thi) load_kv(tlo, 0);
+
+  for (int jt = tlo; jt < thi; ++jt) {
+    const int c0 = jt * C::BN;
+    const int buf = (jt - tlo) & 1;
+    __syncthreads();  // previous tile fully consumed (and Q stored, first time)
+    if (jt + 1 < thi) {
+      load_kv(jt + 1, buf ^ 1);  // overlaps this tile's compute
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();  // tile jt is visible to every thread
+    const float* Ks = KVs + buf * C::KV_FLOATS;
+    const float* Vs = Ks + C::BN * C::SK;
 
     float s[4][C::NC];
 #pragma unroll
@@ -219,6 +247,61 @@ __global__ void __launch_bounds__(256) attn_fwd_fp32_kernel(const FwdParamsF32 p
     if (p.lse != nullptr && tx == 0)
       p.lse[split * p.lse_split + ((long long)b * p.H + h) * p.Sq + row] =
           (l[i] > 0.f) ? (m[i] + log2f(l[i])) * 0.69314718055994531f : -INFINITY;
+  }
+
+  // Key splits: the split that completes the query block's count merges every split's partial
+  // (w_s = exp(lse_s - max) / sum, O = sum_s w_s O_s, LSE = max + log(sum): the arithmetic of
+  // lse_merge_kernel), reading the partials through L2.
+  if (p.splits > 1 && p.blk_cnt != nullptr) {
+    __shared__ int s_last;
+    __threadfence();  // this split's partial is visible device-wide before it counts
+    __syncthreads();
+    if (tid == 0) {
+      const unsigned prev = atomicAdd(p.blk_cnt + blk, 1u);
+      const int last = prev == (unsigned)(p.splits - 1);
+      if (last) p.blk_cnt[blk] = 0u;  // every split has counted: ready for the next launch
+      s_last = last;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+#pragma unroll 1
+    for (int i = 0; i < 4; ++i) {
+      const int row = q0 + ty * 4 + i;
+      if (row >= p.Sq) continue;
+      const long long r = ((long long)b * p.H + h) * p.Sq + row;
+      float mx = -INFINITY;
+      for (int sp = 0; sp < p.splits; ++sp) mx = fmaxf(mx, __ldcg(p.lse + sp * p.lse_split + r));
+      float* of = p.o_final + (long long)b * p.of_sb + (long long)h * p.of_sh +
+                  (long long)row * p.of_ss + C::EPT * tx;
+      if (mx == -INFINITY) {
+#pragma unroll
+        for (int d = 0; d < C::EPT; ++d) of[d] = 0.f;
+        if (p.lse_final != nullptr && tx == 0) p.lse_final[r] = -INFINITY;
+        continue;
+      }
+      float wsum = 0.f;
+      for (int sp = 0; sp < p.splits; ++sp) wsum += expf(__ldcg(p.lse + sp * p.lse_split + r) - mx);
+      float a[C::EPT];
+#pragma unroll
+      for (int d = 0; d < C::EPT; ++d) a[d] = 0.f;
+      const float* pb = p.o + (long long)b * p.o_sb + (long long)h * p.o_sh +
+                        (long long)row * p.o_ss + C::EPT * tx;
+      for (int sp = 0; sp < p.splits; ++sp) {
+        const float w = expf(__ldcg(p.lse + sp * p.lse_split + r) - mx);
+        const float* ps = pb + sp * p.o_split;
+#pragma unroll
+        for (int d = 0; d < C::EPT; d += 2) {
+          const float2 v2 = __ldcg(reinterpret_cast<const float2*>(ps + d));
+          a[d] = fmaf(w, v2.x, a[d]);
+          a[d + 1] = fmaf(w, v2.y, a[d + 1]);
+        }
+      }
+      const float inv = 1.0f / wsum;
+#pragma unroll
+      for (int d = 0; d < C::EPT; ++d) of[d] = a[d] * inv;
+      if (p.lse_final != nullptr && tx == 0) p.lse_final[r] = mx + logf(wsum);
+    }
   }
 }
 

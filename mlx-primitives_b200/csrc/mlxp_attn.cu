@@ -385,26 +385,35 @@ int choose_splits(const Problem& pr, int sms) {
   return best;
 }
 
-// Key splits of the fp32 kernel: its CTAs (64 query rows) are all resident at once for small
-// problems, so the time is the longest chain of key tiles (the last query block under a causal
-// mask).  Split until there are about four CTAs per resident slot (3 per SM), keeping at least
-// 4 key tiles per split and at most 8 splits.
+// Key splits of the fp32 kernel (two resident CTAs of 64 query rows per SM): split only while
+// the query blocks alone would not fill one wave of resident CTAs, keeping at least 4 key tiles
+// per split and at most 8 splits.  With the causal blocks ordered heaviest first, extra splits
+// cost more (partials written, merged by the last split) than the tail they remove (config 1,
+// 384 query blocks: 1 / 2 / 3 / 4 splits 23.5 / 23.1 / 22.0 / 21.4 TFLOPS).
 int choose_splits_f32(const Problem& pr, int sms) {
   const int bm = 64, bn = pr.D >= 128 ? 32 : 64;
   const long long base = (pr.Sq + bm - 1) / bm * pr.B * pr.H;
   const long long kv_tiles = (pr.Skv + bn - 1) / bn;
   int s = 1;
-  while (s < 8 && base * s < 4LL * 3 * sms && kv_tiles / (2 * s) >= 4) s *= 2;
+  while (s < 8 && base * s < 2LL * sms && kv_tiles / (2 * s) >= 4) s *= 2;
   return s;
 }
 
 // Workspace of the fp32 kernel's key splits: fp32 partials [split][B][H][Sq][D], then their
-// LSEs [split][B][H][Sq] (merged by lse_merge_kernel).
+// LSEs [split][B][H][Sq], then one counter per 64-row query block (the split that completes a
+// block's count merges its partials inside the kernel).
+size_t f32_lse_offset(const Problem& pr, int splits) {
+  const size_t rows = (size_t)splits * pr.B * pr.H * pr.Sq;
+  return ((rows * pr.D * 4) + 255) / 256 * 256;
+}
+size_t f32_cnt_offset(const Problem& pr, int splits) {
+  const size_t rows = (size_t)splits * pr.B * pr.H * pr.Sq;
+  return (f32_lse_offset(pr, splits) + rows * 4 + 255) / 256 * 256;
+}
+size_t f32_blocks(const Problem& pr) { return (size_t)((pr.Sq + 63) / 64) * pr.B * pr.H; }
 size_t split_workspace_f32(const Problem& pr, int splits) {
   if (splits <= 1) return 0;
-  const size_t rows = (size_t)splits * pr.B * pr.H * pr.Sq;
-  const size_t o_bytes = ((rows * pr.D * 4) + 255) / 256 * 256;
-  return o_bytes + rows * 4;
+  return f32_cnt_offset(pr, splits) + f32_blocks(pr) * 4;
 }
 
 // Workspace of the tensor-core kernel's key splits (merged inside the kernel): one counter per
@@ -662,9 +671,7 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
       else if (kv_splits > 1) splits = (int)std::min<int64_t>(kv_splits, (pr.Skv + 31) / 32);
     }
     p.splits = splits;
-    float* o_parts = nullptr;
-    float* lse_parts = nullptr;
-    if (splits > 1) {  // partials in the workspace, then the LSE merge into o
+    if (splits > 1) {  // partials in the workspace, merged inside the kernel into o
       const size_t need = split_workspace(pr, splits);
       if (ws == nullptr || ws_bytes < need)
         return fail(MLXP_ERR_WORKSPACE, "split-KV needs %zu bytes of workspace, got %zu", need,
@@ -672,9 +679,17 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
       if (reinterpret_cast<uintptr_t>(ws) % 256)
         return fail(MLXP_ERR_INVALID, "workspace must be 256-byte aligned");
       const long long rows = pr.B * pr.H * pr.Sq;
-      o_parts = static_cast<float*>(ws);
-      lse_parts = reinterpret_cast<float*>(static_cast<char*>(ws) +
-                                           ((size_t)splits * rows * pr.D * 4 + 255) / 256 * 256);
+      float* o_parts = static_cast<float*>(ws);
+      float* lse_parts =
+          reinterpret_cast<float*>(static_cast<char*>(ws) + f32_lse_offset(pr, splits));
+      p.blk_cnt = reinterpret_cast<unsigned*>(static_cast<char*>(ws) + f32_cnt_offset(pr, splits));
+      cudaError_t e = cudaMemsetAsync(p.blk_cnt, 0, f32_blocks(pr) * 4, stream);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(split counters)");
+      p.o_final = (float*)o;
+      p.of_sb = os[0];
+      p.of_sh = os[1];
+      p.of_ss = os[2];
+      p.lse_final = lse;
       p.o = o_parts;
       p.o_sh = pr.Sq * pr.D;
       p.o_sb = pr.H * p.o_sh;
@@ -689,8 +704,7 @@ int attn_fwd_impl(const void* q, const void* k, const void* v, void* o, float* l
       case 64: rc = launch_f32_t<64>(p, stream); break;
       default: rc = launch_f32_t<128>(p, stream); break;
     }
-    if (rc || splits <= 1) return rc;
-    return merge_dispatch(o_parts, lse_parts, splits, o, lse, pr, os, stream);
+    return rc;
   }
 
   const bool bf16 = pr.dtype == MLXP_DTYPE_BF16;

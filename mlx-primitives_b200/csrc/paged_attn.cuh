@@ -84,24 +84,6 @@ __host__ __device__ constexpr int paged_smem_bytes(int D) {
   return kPagedWarps * kPagedStages * paged_stage_bytes<T>(D) + kPagedWarps * (D + 2) * 4;
 }
 
-// 4 * sizeof(T) bytes global -> shared; src_bytes = 0 writes zeros without reading global.
-template <int BYTES>
-__device__ __forceinline__ void cp_async_piece(uint32_t dst, const void* src, int src_bytes) {
-  if constexpr (BYTES == 16)
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src),
-                 "r"(src_bytes) : "memory");
-  else
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(dst), "l"(src),
-                 "r"(src_bytes) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() {
-  asm volatile("cp.async.commit_group;\n" ::: "memory");
-}
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
-}
-
 template <typename T>
 __device__ __forceinline__ void quad_to_f(const T* p, float (&x)[4]) {
   if constexpr (sizeof(T) == 4) {

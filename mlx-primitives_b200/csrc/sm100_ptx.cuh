@@ -224,6 +224,25 @@ __device__ __forceinline__ void tma_prefetch_l2_4d(const void* map, int c0, int 
                : "memory");
 }
 
+// cp.async (per-thread async global -> shared copies), used by the CUDA-core kernels.
+// BYTES (16 or 8) global -> shared; src_bytes = 0 writes zeros without reading global.
+template <int BYTES>
+__device__ __forceinline__ void cp_async_piece(uint32_t dst, const void* src, int src_bytes) {
+  if constexpr (BYTES == 16)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src),
+                 "r"(src_bytes) : "memory");
+  else
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(dst), "l"(src),
+                 "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
 // ------------------------------------------------------------------------------------------
 // TMEM allocation and tcgen05 fences
 // ------------------------------------------------------------------------------------------
