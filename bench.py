@@ -850,7 +850,9 @@ def main():
             "higher_is_better": True,
             "scaling": "strong" if c["api"] == "ring" or part else "weak", "vs_baseline": None,
             "dtype": "f32" if c["dtype"] == "fp32" else "bf16",
-            "data": "synthetic: seeded N(0, std^2) tensors generated on device (seed 42 + rank)",
+            "data": ("synthetic: seeded N(0, std^2) tensors generated on device (seed 42; every "
+                     "rank builds the same tensors of the split workload)" if (part or ring) else
+                     "synthetic: seeded N(0, std^2) tensors generated on device (seed 42 + rank)"),
             "config": config_json(c, world, len(units) if part else None),
             "tflops_per_gpu": value / world,
             "pct_of_bf16_peak": 100.0 * (value / world) / peak,
