@@ -76,7 +76,9 @@ const char* mlxp_last_error(void);
  * dtype: element type of q, k, v and o.  BF16/FP16 run the tcgen05 tensor-core kernel
  * (head_dim 64 or 128); FP32 runs the CUDA-core kernel (head_dim 32, 64 or 128).
  * kv_splits: 1 = no split, 0 = automatic, >1 = split the key range into that many parts that
- * run as separate CTAs and are combined by an LSE merge (needs workspace).
+ * run as separate CTAs; the part that finishes a query block last merges the parts' results
+ * (LSE weights) inside the same launch.  Needs workspace (mlxp_attn_workspace_size): the parts'
+ * fp32 partials and per-block counters; the counters are cleared on the call's stream.
  */
 int mlxp_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
                   int dtype, int64_t B, int64_t H, int64_t Sq, int64_t Skv, int64_t D,
