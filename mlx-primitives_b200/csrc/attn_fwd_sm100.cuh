@@ -6,9 +6,10 @@
 // groups of (batch, head) units so that the CTAs running at the same time share K/V through
 // L2, heaviest query blocks of a group first when the mask is causal (see decode_item).
 //
-//   warp 9        TMA producer: fetches items, then loads Q once per item and K, V tiles into
-//                 two shared-memory rings (128-byte swizzle).  The rings, barriers and TMEM
-//                 persist across items, so the next item's loads overlap the current one.
+//   warp 9        TMA producer: fetches items and decodes each into a shared-memory slot for the
+//                 other roles, then loads Q once per item and K, V tiles into two shared-memory
+//                 rings (128-byte swizzle), K and V released separately.  The rings, barriers and
+//                 TMEM persist across items, so the next item's loads overlap the current one.
 //   warp 8        MMA issuer (one thread): S_t = Q_t K^T (SS form, fp32 accumulate in TMEM),
 //                 then O_t += P_t V (TS form: P_t read from TMEM, V from smem).
 //   warps 0-3     softmax for tile 0, warps 4-7 softmax for tile 1: one thread owns one query
