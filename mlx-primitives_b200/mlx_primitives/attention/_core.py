@@ -265,6 +265,10 @@ def _forward_impl(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, layout: 
 
 
 _HOST_CHUNKS = 4
+# BHSD host tensors are pipelined in (batch, head-range) pieces, each a contiguous block of
+# q, k, v and o, so that the last piece's kernel and copy back, the part of the call that no
+# copy to the device hides, are a small fraction of it.
+_HOST_PIECES_BHSD = 16
 _copy_streams = {}
 
 
@@ -277,17 +281,25 @@ def _streams(dev: torch.device):
 
 def _host_attention(q, k, v, *, layout, scale, causal, window_left, window_right, q_offset,
                     kv_offset, kv_splits, return_lse):
-    """Host tensors: staged through the current CUDA device in batch chunks, pipelined so
-    that the copy of chunk i+1 to the device, the kernel of chunk i and the copy of chunk i-1's
-    result back run at the same time (two copy streams, the two copy engines of the GPU, and
-    the compute stream).  The result lands in pinned host memory."""
+    """Host tensors: staged through the current CUDA device in pieces (batch chunks; for BHSD
+    tensors with fewer batches than _HOST_PIECES_BHSD, (batch, head-range) blocks), pipelined
+    so that the copy of piece i+1 to the device, the kernel of piece i and the copy of piece
+    i-1's result back run at the same time (two copy streams, the two copy engines of the GPU,
+    and the compute stream).  The result lands in pinned host memory."""
     if not torch.cuda.is_available():
         raise RuntimeError("attention requires a CUDA device (there is no CPU fallback)")
     dev = torch.device("cuda", torch.cuda.current_device())
     B = q.shape[0]
     kv_whole = k.shape[0] != B  # a broadcast K/V batch is copied once, whole
-    n = max(1, min(B, _HOST_CHUNKS))
-    bounds = [(B * i // n, B * (i + 1) // n) for i in range(n)]
+    # pieces: (batch range, head range or None for all heads)
+    H, Hkv = q.shape[1], k.shape[1]
+    if layout == "BHSD" and not kv_whole and H == Hkv and B < _HOST_PIECES_BHSD:
+        per_b = max(1, min(H, _HOST_PIECES_BHSD // B))
+        pieces = [((b, b + 1), (H * i // per_b, H * (i + 1) // per_b))
+                  for b in range(B) for i in range(per_b)]
+    else:
+        n = max(1, min(B, _HOST_CHUNKS))
+        pieces = [((B * i // n, B * (i + 1) // n), None) for i in range(n)]
     cur = torch.cuda.current_stream(dev)
     s_in, s_out = _streams(dev)
     s_in.wait_stream(cur)
@@ -306,24 +318,25 @@ def _host_attention(q, k, v, *, layout, scale, causal, window_left, window_right
         with torch.cuda.stream(s_in):
             dk.copy_(k, non_blocking=True)
             dv.copy_(v, non_blocking=True)
-    for b0, b1 in bounds:
+    for (b0, b1), hr in pieces:
+        sl = (slice(b0, b1),) if hr is None else (slice(b0, b1), slice(*hr))
         with torch.cuda.stream(s_in):
-            dq[b0:b1].copy_(q[b0:b1], non_blocking=True)
+            dq[sl].copy_(q[sl], non_blocking=True)
             if not kv_whole:
-                dk[b0:b1].copy_(k[b0:b1], non_blocking=True)
-                dv[b0:b1].copy_(v[b0:b1], non_blocking=True)
+                dk[sl].copy_(k[sl], non_blocking=True)
+                dv[sl].copy_(v[sl], non_blocking=True)
         cur.wait_stream(s_in)
-        kk, vv = (dk, dv) if kv_whole else (dk[b0:b1], dv[b0:b1])
-        res = attention_forward(dq[b0:b1], kk, vv, layout=layout, scale=scale, causal=causal,
+        kk, vv = (dk, dv) if kv_whole else (dk[sl], dv[sl])
+        res = attention_forward(dq[sl], kk, vv, layout=layout, scale=scale, causal=causal,
                                 window_left=window_left, window_right=window_right,
                                 q_offset=q_offset, kv_offset=kv_offset, kv_splits=kv_splits,
                                 return_lse=return_lse)
         o, lse = res if return_lse else (res, None)
         s_out.wait_stream(cur)
         with torch.cuda.stream(s_out):
-            out_host[b0:b1].copy_(o, non_blocking=True)
+            out_host[sl].copy_(o, non_blocking=True)
             if lse is not None:
-                lse_host[b0:b1].copy_(lse, non_blocking=True)
+                lse_host[sl].copy_(lse, non_blocking=True)
         o.record_stream(s_out)
         if lse is not None:
             lse.record_stream(s_out)

@@ -395,6 +395,21 @@ def test_host_tensors_are_staged_through_the_gpu():
     assert torch.equal(o_host, o_dev.cpu())
 
 
+@pytest.mark.parametrize("B,H", [(2, 6), (3, 5), (1, 20)])
+def test_host_bhsd_tensors_staged_in_head_pieces(B, H):
+    # BHSD host tensors with few batches are pipelined in (batch, head-range) pieces; every
+    # piece's output and LSE must land in its place, bit-identical to one device call
+    from mlx_primitives.attention._core import attention_forward
+    q, k, v = (torch.from_numpy(np.ascontiguousarray(np.swapaxes(a, 1, 2))).to(torch.bfloat16)
+               for a in O.make_qkv((B, 200, H, 64), (B, 230, H, 64), seed=40 + B))
+    kw = dict(layout="BHSD", scale=0.125, causal=True, q_offset=30, return_lse=True)
+    o_host, lse_host = attention_forward(q, k, v, **kw)
+    assert o_host.device.type == "cpu" and lse_host.device.type == "cpu"
+    o_dev, lse_dev = attention_forward(q.cuda(), k.cuda(), v.cuda(), **kw)
+    assert torch.equal(o_host, o_dev.cpu())
+    assert torch.equal(lse_host, lse_dev.cpu())
+
+
 def test_padded_head_dims():
     import mlx_primitives as mp
     for D, dt in ((48, torch.bfloat16), (100, torch.bfloat16), (16, torch.float32), (80, torch.float32)):
