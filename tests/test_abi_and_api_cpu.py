@@ -55,6 +55,23 @@ def test_workspace_size_is_zero_without_split():
     assert n >= rows * 64 * 4 + rows * 4
 
 
+def test_fp32_split_workspace_holds_partials_lses_and_block_counters():
+    from mlx_primitives import _lib
+
+    L = _lib.lib()
+    L.mlxp_attn_workspace_size.restype = ctypes.c_size_t
+    # fp32 (dtype 0), explicit 3 splits of config 1's shape: 256-byte aligned partials
+    # [split][B][H][Sq][D], then LSEs [split][B][H][Sq], then one counter per 64-row query block
+    B, H, Sq, Skv, D, s = 2, 12, 1024, 1024, 64, 3
+    up = lambda x: (x + 255) // 256 * 256
+    rows = s * B * H * Sq
+    want = up(up(rows * D * 4) + rows * 4) + ((Sq + 63) // 64) * B * H * 4
+    assert L.mlxp_attn_workspace_size(0, B, H, Sq, Skv, D, 1, -1, -1, 0, 0, s) == want
+    # splits are capped at one per 32 keys
+    assert (L.mlxp_attn_workspace_size(0, 1, 1, 100, 64, 32, 0, -1, -1, 0, 0, 8) ==
+            L.mlxp_attn_workspace_size(0, 1, 1, 100, 64, 32, 0, -1, -1, 0, 0, 2))
+
+
 def test_invalid_arguments_are_rejected_before_any_launch():
     from mlx_primitives import _lib
 
