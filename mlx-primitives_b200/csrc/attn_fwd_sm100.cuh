@@ -197,8 +197,8 @@ __device__ __forceinline__ WorkItem get_item(const volatile int* d) {
   return w;
 }
 
-// One work item, decoded identically by every role from its index (item_coords in
-// attn_common.cuh gives its unit, key split and query block).
+// Decodes work item idx (item_coords in attn_common.cuh gives its unit, key split and query
+// block); run by the producer, which publishes the result for the other roles.
 template <bool kRope>
 __device__ __forceinline__ WorkItem decode_item(const FwdParams& p, int idx, int BN) {
   WorkItem w;
@@ -437,9 +437,7 @@ __global__ void __launch_bounds__(384, 1)
             if (!ok) break;
           }
           // the first item of every CTA is its block index (no atomic on the launch's
-          // critical path); later ones come from the counter, past the first gridDim.x.  With
-          // rotation items every item comes from the counter: an item may wait for smaller
-          // ones, which must then belong to CTAs that are running.
+          // critical path); later ones come from the counter, past the first gridDim.x.
           const int idx = item == 0 ? (int)blockIdx.x
                                     : (int)(gridDim.x + atomicAdd(p.work_counter, 1u));
           WorkItem w{};
@@ -449,7 +447,7 @@ __global__ void __launch_bounds__(384, 1)
           MLXP_TR(true, 3, item, 1);
           mbar_arrive(BAR(C::B_WF + slot));  // release: the slot writes are visible to waiters
           if (idx >= n_items) break;
-          if (w.hi <= w.lo) continue;  // rotation items and empty items load nothing
+          if (w.hi <= w.lo) continue;  // empty items load nothing
           if (kRope && w.grp > rot_ready) {
             // Q and K of this group are rotated by the RoPE phase of this and other CTAs: wait
             // until all of the group's rotation items are done
