@@ -43,9 +43,11 @@ for _p in (REPO, REPO / "mlx-primitives_b200"):
 METRIC = "attention fwd TFLOPS/GPU and % of BF16 tensor peak at 1/2/4/8 B200"
 
 # DRAM bytes (read + write) of one launch of the dominant kernel at N=1 (attn_fwd_sm100_kernel
-# for c2 and c4, paged_attn_tma_kernel for p4, attn_bwd_sm100_kernel for b2), from one ncu
-# capture of the same command; null where no capture of that configuration was taken.
-NCU_TRAFFIC_BYTES = {"c2": 546.2e6, "c4": 2.2867e9, "p4": 541.18e6, "b2": 1.3016e9}
+# for c2, c3, c4 and c5s, attn_fwd_fp32_kernel for c1, paged_attn_tma_kernel for p4,
+# attn_bwd_sm100_kernel for b2), from one ncu capture of the same command; null where no
+# capture of that configuration was taken.
+NCU_TRAFFIC_BYTES = {"c1": 18.94e6, "c2": 546.2e6, "c3": 1.0947e9, "c4": 2.2867e9,
+                     "c5s": 351.6e6, "p4": 541.18e6, "b2": 1.3016e9}
 
 CONFIGS = {
     "c1": dict(workload="flash_attention fp32 BSHD causal (config 1)", api="flash", dtype="fp32",
