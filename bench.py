@@ -861,9 +861,10 @@ def main():
             "roofline": {
                 "bound": "fp32" if fp32 else "tensor", "achieved": achieved,
                 "peak": roof_peak, "unit": "TFLOP/s", "frac": achieved / roof_peak,
-                # per-rank launches are the N=1 workload except for the ring
-                "traffic": (NCU_TRAFFIC_BYTES.get(args.config)
-                            if c["api"] != "ring" else None),
+                # the N=1 launch's capture; a split rank's launch covers unit_frac of its units
+                # (traffic in proportion: every unit's Q, K, V and O once); none for the ring
+                "traffic": (NCU_TRAFFIC_BYTES[args.config] * unit_frac
+                            if c["api"] != "ring" and args.config in NCU_TRAFFIC_BYTES else None),
                 "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + write.sum)",
                 "kernel": ("attn_fwd_fp32_kernel" if c["dtype"] == "fp32" else
                            "attn_fwd_sm100_kernel"),
