@@ -858,6 +858,8 @@ def main():
             "config": config_json(c, world, len(units) if part else None),
             "tflops_per_gpu": value / world,
             "pct_of_bf16_peak": 100.0 * (value / world) / peak,
+            "pct_of_bf16_sustained": (100.0 * (value / world) / peak_sus
+                                      if peak_sus else None),
             "roofline": {
                 "bound": "fp32" if fp32 else "tensor", "achieved": achieved,
                 "peak": roof_peak, "unit": "TFLOP/s", "frac": achieved / roof_peak,
