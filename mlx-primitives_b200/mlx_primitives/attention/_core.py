@@ -279,6 +279,20 @@ def _streams(dev: torch.device):
     return _copy_streams[dev.index]
 
 
+def _host_pieces(B, dim1_q, dim1_k, layout, kv_whole):
+    """The pieces _host_attention stages host tensors in: ((b0, b1), (h0, h1) or None for every
+    head).  BHSD tensors with fewer batches than _HOST_PIECES_BHSD and as many K/V heads as query
+    heads (dim 1 of q and k) are cut into (batch, head-range) blocks; otherwise into batch
+    chunks.  Every (batch, head) is in exactly one piece."""
+    if layout == "BHSD" and not kv_whole and dim1_q == dim1_k and B < _HOST_PIECES_BHSD:
+        H = dim1_q
+        per_b = max(1, min(H, _HOST_PIECES_BHSD // B))
+        return [((b, b + 1), (H * i // per_b, H * (i + 1) // per_b))
+                for b in range(B) for i in range(per_b)]
+    n = max(1, min(B, _HOST_CHUNKS))
+    return [((B * i // n, B * (i + 1) // n), None) for i in range(n)]
+
+
 def _host_attention(q, k, v, *, layout, scale, causal, window_left, window_right, q_offset,
                     kv_offset, kv_splits, return_lse):
     """Host tensors: staged through the current CUDA device in pieces (batch chunks; for BHSD
@@ -291,15 +305,7 @@ def _host_attention(q, k, v, *, layout, scale, causal, window_left, window_right
     dev = torch.device("cuda", torch.cuda.current_device())
     B = q.shape[0]
     kv_whole = k.shape[0] != B  # a broadcast K/V batch is copied once, whole
-    # pieces: (batch range, head range or None for all heads)
-    H, Hkv = q.shape[1], k.shape[1]
-    if layout == "BHSD" and not kv_whole and H == Hkv and B < _HOST_PIECES_BHSD:
-        per_b = max(1, min(H, _HOST_PIECES_BHSD // B))
-        pieces = [((b, b + 1), (H * i // per_b, H * (i + 1) // per_b))
-                  for b in range(B) for i in range(per_b)]
-    else:
-        n = max(1, min(B, _HOST_CHUNKS))
-        pieces = [((B * i // n, B * (i + 1) // n), None) for i in range(n)]
+    pieces = _host_pieces(B, q.shape[1], k.shape[1], layout, kv_whole)
     cur = torch.cuda.current_stream(dev)
     s_in, s_out = _streams(dev)
     s_in.wait_stream(cur)

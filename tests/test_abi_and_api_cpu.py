@@ -162,3 +162,26 @@ def test_modules_store_reference_attributes():
     ca = mp.ChunkedCrossAttention(8, 64)
     assert (ca.chunk_size, ca.causal) == (1024, False)
     assert mp.Layout("BSHD") == "BSHD" and mp.Layout.BHSD == "BHSD"
+
+
+@pytest.mark.parametrize("B,H,Hkv,layout,kv_whole", [
+    (4, 32, 32, "BHSD", False), (1, 20, 20, "BHSD", False), (3, 5, 5, "BHSD", False),
+    (16, 8, 8, "BHSD", False), (4, 32, 8, "BHSD", False), (2, 128, 128, "BSHD", False),
+    (8, 16, 16, "BHSD", True), (1, 1, 1, "BHSD", False)])
+def test_host_pieces_cover_every_unit_once(B, H, Hkv, layout, kv_whole):
+    # host tensors are staged in these pieces; each (batch, head) must be copied, computed
+    # and copied back exactly once (for BSHD, dim 1 is the sequence: batch chunks only)
+    from mlx_primitives.attention._core import _host_pieces
+    pieces = _host_pieces(B, H, Hkv, layout, kv_whole)
+    seen = {}
+    for (b0, b1), hr in pieces:
+        assert 0 <= b0 < b1 <= B
+        h0, h1 = hr if hr is not None else (0, H)
+        assert 0 <= h0 < h1 <= H
+        if hr is not None:
+            assert layout == "BHSD" and not kv_whole and H == Hkv
+        for b in range(b0, b1):
+            for h in range(h0, h1):
+                seen[(b, h)] = seen.get((b, h), 0) + 1
+    assert sorted(seen) == [(b, h) for b in range(B) for h in range(H)]
+    assert set(seen.values()) == {1}
